@@ -1,0 +1,471 @@
+"""Benchmark of the fused GGUF dequant + matvec path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload layer_q4k|q8_0|head_q6k|down_q5k|...]
+
+Default workload (the configuration the headline metric is quoted on): one
+Qwen2-7B layer's projections at batch 1 in Q4_K -- q/o 3584x3584, k/v
+512x3584, gate/up 18944x3584, down 3584x18944 (131,088,384 weight bytes).  A
+step is one pass over the seven matvecs.  Eight distinct copies of the layer
+(1.05 GB, well above the 126 MB L2) are rotated step by step, so every step
+streams its weights from HBM.
+
+value  = algorithmic bytes (weights + x + y) per step / device time per step,
+         weights and activations resident in HBM; the K steps are one CUDA
+         graph replay timed with CUDA events on the launching stream.
+e2e    = the same metric through the public call a user makes,
+         CudaBackend.matmul_q4k(x, weight, n, k) with x in pinned host memory:
+         x host->device, kernel, y device->host and a synchronise per call.
+roofline: achieved GB/s of the dominant kernel (the gemv_x1 launches of the
+         3584-column projections: 6 of 7 launches, 71% of the bytes) from
+         per-launch CUDA events inside the timed graph, against the measured
+         copy bandwidth in MEASURED_PEAKS.json.
+cpu_baseline: the reference's own native kernels (flatrun_native._C, built
+         from its sources into oracle/_ref) on the same layer.
+
+Multi-GPU (--gpus N under torchrun): each rank owns an n-row shard (the
+config's shapes) of every projection of an N-times taller layer, whole quant
+blocks per row, and the outputs are assembled by NCCL all-gathers in the
+forwarder's dependency groups (qkv, o, gate+up, down).  Per-GPU work is fixed
+("weak" scaling); value = bytes of all ranks / max-over-ranks time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+from flatrun_b200 import synth  # noqa: E402
+
+METRIC = "weight-stream HBM GB/s per quant matvec"
+UNIT = "GB/s"
+
+QWEN2_7B = [  # (name, quant, n, k, gather group)
+    ("q", "Q4_K", 3584, 3584, "qkv"),
+    ("k", "Q4_K", 512, 3584, "qkv"),
+    ("v", "Q4_K", 512, 3584, "qkv"),
+    ("o", "Q4_K", 3584, 3584, "o"),
+    ("gate", "Q4_K", 18944, 3584, "gateup"),
+    ("up", "Q4_K", 18944, 3584, "gateup"),
+    ("down", "Q4_K", 3584, 18944, "down"),
+]
+
+WORKLOADS = {
+    "layer_q4k": dict(mats=QWEN2_7B, batch=1,
+                      desc="config 2: Qwen2-7B layer projections (q,k,v,o,gate,up,down) in Q4_K, batch 1"),
+    "q8_0": dict(mats=[("w", "Q8_0", 4096, 4096, "w")], batch=1, desc="config 1: Q8_0 4096x4096, batch 1"),
+    "head_q6k": dict(mats=[("lm_head", "Q6_K", 152064, 3584, "w")], batch=1,
+                     desc="config 3: lm_head 152064x3584 Q6_K, batch 1"),
+    "head_q6k_b4": dict(mats=[("lm_head", "Q6_K", 152064, 3584, "w")], batch=4,
+                        desc="config 3: lm_head 152064x3584 Q6_K, batch 4"),
+    "head_q6k_b16": dict(mats=[("lm_head", "Q6_K", 152064, 3584, "w")], batch=16,
+                         desc="config 3: lm_head 152064x3584 Q6_K, batch 16"),
+    "down_q5k": dict(mats=[("down", "Q5_K", 3584, 18944, "w")], batch=1,
+                     desc="config 3: FFN down 3584x18944 Q5_K, batch 1"),
+    "down_q5k_b4": dict(mats=[("down", "Q5_K", 3584, 18944, "w")], batch=4,
+                        desc="config 3: FFN down 3584x18944 Q5_K, batch 4"),
+    "down_q5k_b16": dict(mats=[("down", "Q5_K", 3584, 18944, "w")], batch=16,
+                         desc="config 3: FFN down 3584x18944 Q5_K, batch 16"),
+    "down_q6k": dict(mats=[("down", "Q6_K", 3584, 18944, "w")], batch=1,
+                     desc="Q6_K down 3584x18944, batch 1"),
+    "q1_0": dict(mats=[("w", "Q1_0", 4096, 4096, "w")], batch=1, desc="Q1_0 4096x4096, batch 1"),
+    "gate_q4k": dict(mats=[("gate", "Q4_K", 18944, 3584, "w")], batch=1, desc="Q4_K gate 18944x3584, batch 1"),
+}
+
+
+def algorithmic_bytes(mats, batch: int) -> int:
+    return sum(synth.weight_bytes(q, n, k) + batch * (k + n) * 4 for _, q, n, k, _ in mats)
+
+
+def peaks() -> tuple[float, str]:
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback 6.65 TB/s"
+
+
+def ncu_traffic(workload: str):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
+    summary, if one exists for this workload."""
+    path = os.path.join(REPO, "profiles", "ncu_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(workload)
+    except (OSError, ValueError):
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling in the background."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(device_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "samples": len(sm), "power_w_max": max(power) if power else None, "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# reference CPU arm / cpu_baseline
+# ---------------------------------------------------------------------------
+
+def _load_ref_native():
+    import importlib.util
+    d = os.path.join(REPO, "oracle", "_ref")
+    if not os.path.isdir(d):
+        return None
+    for name in os.listdir(d):
+        if name.startswith("_C") and name.endswith(".so"):
+            spec = importlib.util.spec_from_file_location("_C", os.path.join(d, name))
+            mod = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(mod)
+            return mod
+    return None
+
+
+_REF_FN = {"Q4_K": "matmul_q4_k", "Q6_K": "matmul_q6_k", "Q8_0": "matmul_q8_0"}
+
+
+def cpu_reference_step_fn(mats, batch, host_w, xs):
+    """One step of the reference's CPU path: the native C++ kernels where the
+    reference has one (scalar, single-threaded on x86: q4_k.h:38-41), else its
+    NumPy decoders + BLAS (restated in oracle/)."""
+    nat = _load_ref_native()
+    from oracle import gguf_oracle as O
+
+    calls = []
+    kinds = set()
+    for (name, q, n, k, _), w, x in zip(mats, host_w, xs):
+        if nat is not None and q in _REF_FN:
+            fn = getattr(nat, _REF_FN[q] + ("_batched" if batch > 1 else ""))
+            calls.append(lambda fn=fn, x=x, w=w, n=n, k=k: fn(x, w, n, k))
+            kinds.add("reference")
+        else:
+            calls.append(lambda q=q, x=x, w=w, n=n, k=k: O.matvec_fp32(q, w, x, n, k))
+            kinds.add("port")
+    return (lambda: [c() for c in calls]), ("reference" if kinds == {"reference"} else "port")
+
+
+def run_cpu(mats, batch, steps, warmup, host_w, xs):
+    step, kind = cpu_reference_step_fn(mats, batch, host_w, xs)
+    for _ in range(warmup):
+        step()
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times), sum(times), kind
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def make_host_layer(mats, copy: int):
+    return [synth.make_weight(q, n, k, seed=1000 * copy + i) for i, (_, q, n, k, _) in enumerate(mats)]
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="layer_q4k")
+    ap.add_argument("--copies", type=int, default=0, help="distinct weight copies rotated (0 = auto, > 3x L2)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    wl = WORKLOADS[args.workload]
+    mats, batch = wl["mats"], wl["batch"]
+    step_bytes = algorithmic_bytes(mats, batch)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        host_w = make_host_layer(mats, 0)
+        xs = [synth.make_x(k, batch=None if batch == 1 else batch, seed=50 + i)
+              for i, (_, _, _, k, _) in enumerate(mats)]
+        steps = max(1, min(args.steps, 20))
+        med, total, kind = run_cpu(mats, batch, steps, min(args.warmup, 2), host_w, xs)
+        value = step_bytes / med / 1e9
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
+            "steps": steps, "warmup": min(args.warmup, 2), "ms_per_step": round(med * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": wl["desc"], "global_batch": batch},
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": 1, "kind": kind,
+                             "sample": f"{steps} timed steps of the full workload (median), reference "
+                                       "flatrun_native._C scalar kernels (single-threaded on x86)"},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
+
+    import ctypes
+
+    import torch
+
+    from flatrun_b200 import CudaBackend, _lib
+
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.cuda.current_device()
+    lib = _lib.load()
+    be = CudaBackend(dev)
+    if not be.available:
+        raise RuntimeError(f"CUDA backend unavailable: {be._load_error}")
+
+    props = torch.cuda.get_device_properties(dev)
+    l2 = getattr(props, "L2_cache_size", 126 * 2**20)
+    wbytes = sum(synth.weight_bytes(q, n, k) for _, q, n, k, _ in mats)
+    copies = args.copies or max(2, min(16, int(np.ceil(3 * l2 / wbytes)) + 1))
+
+    # weights: `copies` distinct layers (row-rolled copies of one random layer)
+    base = make_host_layer(mats, rank)
+    dws = []  # [copy][mat] DeviceWeight
+    host_arrays = []  # the host bytes each DeviceWeight was uploaded from (the backend's cache keys)
+    for c in range(copies):
+        layer, hosts = [], []
+        for (name, q, n, k, _), raw in zip(mats, base):
+            rb = synth.row_bytes(q, k)
+            host = raw if c == 0 else np.ascontiguousarray(np.roll(raw.reshape(n, rb), c * 7919 % n, axis=0)).reshape(-1)
+            layer.append(be.weight(host, n, k, q))
+            hosts.append(host)
+        dws.append(layer)
+        host_arrays.append(hosts)
+    xs_host = [synth.make_x(k, batch=None if batch == 1 else batch, seed=50 + i)
+               for i, (_, _, _, k, _) in enumerate(mats)]
+    xs_dev = [torch.from_numpy(x).cuda() for x in xs_host]
+    ys_dev = [torch.empty((batch, n), device="cuda") for (_, _, n, _, _) in mats]
+    wptr = [[dw.device_ptr() for dw in layer] for layer in dws]
+    qid = [_lib.QUANT_IDS[q] for _, q, _, _, _ in mats]
+
+    # all-gather groups (N > 1)
+    groups = []
+    if world > 1:
+        import torch.distributed as dist
+        order = []
+        for i, m in enumerate(mats):
+            if not order or order[-1][0] != m[4]:
+                order.append((m[4], []))
+            order[-1][1].append(i)
+        for gname, idx in order:
+            local = sum(mats[i][2] for i in idx) * batch
+            groups.append((idx[-1], torch.empty(local, device="cuda"), torch.empty(local * world, device="cuda"),
+                           idx))
+
+    stream = torch.cuda.Stream()
+
+    def launch(step: int, evs=None):
+        c = step % copies
+        for i, (_, q, n, k, _) in enumerate(mats):
+            if evs is not None:
+                evs[i][0].record(stream)
+            rc = lib.frc_gemv(qid[i], wptr[c][i], dws[c][i].nbytes, n, k, xs_dev[i].data_ptr(), batch,
+                              ys_dev[i].data_ptr(), ctypes.c_void_p(stream.cuda_stream))
+            if rc:
+                _lib.check(rc, lib)
+            if evs is not None:
+                evs[i][1].record(stream)
+            for last, sendbuf, recvbuf, idx in groups:
+                if last == i:
+                    off = 0
+                    for j in idx:
+                        sz = mats[j][2] * batch
+                        sendbuf[off:off + sz].copy_(ys_dev[j].view(-1))
+                        off += sz
+                    dist.all_gather_into_tensor(recvbuf, sendbuf)
+
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev if world == 1 else local_rank)
+    with torch.cuda.stream(stream):
+        for s in range(args.warmup):
+            launch(s)
+    torch.cuda.synchronize()
+
+    # capture the K timed steps (with per-launch events) as one graph
+    K = args.steps
+    chunk = min(K, 200)
+    graphs = []
+    evs_all = []
+    with torch.cuda.stream(stream):
+        for g0 in range(0, K, chunk):
+            g = torch.cuda.CUDAGraph()
+            evs_chunk = []
+            with torch.cuda.graph(g, stream=stream):
+                for s in range(g0, min(K, g0 + chunk)):
+                    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                          for _ in mats]
+                    evs_chunk.append(ev)
+                    launch(s, ev)
+            graphs.append(g)
+            evs_all.extend(evs_chunk)
+    # soak: replay untimed for ~1 s so clocks settle and the sampler sees load
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < 1.0:
+        for g in graphs:
+            g.replay()
+        torch.cuda.synchronize()
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for g in graphs:
+        g.replay()
+    end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = start.elapsed_time(end)
+    clk = clocks.stop()
+
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    ms_step = elapsed_ms / K
+    value = step_bytes * world / (ms_step / 1e3) / 1e9
+
+    # per-launch timing -> roofline of the dominant kernel
+    per = {}
+    for i, (name, q, n, k, _) in enumerate(mats):
+        durs = [ev[i][0].elapsed_time(ev[i][1]) for ev in evs_all]
+        b = synth.weight_bytes(q, n, k) + batch * (k + n) * 4
+        per[name] = {"us": round(statistics.mean(durs) * 1e3, 3),
+                     "gbs": round(b / (statistics.mean(durs) / 1e3) / 1e9, 1), "bytes": b}
+    dom = [i for i, (_, q, n, k, _) in enumerate(mats) if k == mats[0][3]]
+    dom_bytes = sum(per[mats[i][0]]["bytes"] for i in dom) / len(dom)
+    dom_us = sum(per[mats[i][0]]["us"] for i in dom) / len(dom)
+    achieved = dom_bytes / (dom_us / 1e6) / 1e9
+    peak, peak_src = peaks()
+    traffic = ncu_traffic(args.workload)
+
+    # e2e through the public call, host buffers (pinned x), synchronous calls
+    e2e = None
+    if not args.no_e2e and world == 1:
+        method = {"Q4_K": be.matmul_q4k, "Q6_K": be.matmul_q6k, "Q8_0": be.matmul_q8_0,
+                  "Q5_K": be.matmul_q5k, "Q1_0": be.matmul_q1_0}
+        pinned = []
+        for x in xs_host:
+            t = torch.empty(x.shape, dtype=torch.float32, pin_memory=True)
+            t.numpy()[...] = x
+            pinned.append(t.numpy())
+        e2e_steps = min(K, 200)
+        for s in range(3):
+            for i, (_, q, n, k, _) in enumerate(mats):
+                method[q](pinned[i], host_arrays[s % copies][i], n, k)
+        t0 = time.perf_counter()
+        for s in range(e2e_steps):
+            for i, (_, q, n, k, _) in enumerate(mats):
+                method[q](pinned[i], host_arrays[s % copies][i], n, k)
+        t_e2e = (time.perf_counter() - t0) / e2e_steps
+        e2e = {"value": round(step_bytes / t_e2e / 1e9, 2), "unit": UNIT,
+               "h2d_bytes_per_step": sum(batch * k * 4 for _, _, _, k, _ in mats),
+               "d2h_bytes_per_step": sum(batch * n * 4 for _, _, n, _, _ in mats),
+               "ms_per_step": round(t_e2e * 1e3, 4), "steps": e2e_steps,
+               "timer": "host wall clock over synchronous calls (each call copies x in, y out and synchronises)"}
+
+    # CPU baseline: the reference's own native kernels on the same workload
+    cpu = None
+    if not args.no_cpu and rank == 0:
+        med, total, kind = run_cpu(mats, batch, 3, 1, base, xs_host)
+        cpu = {"value": round(step_bytes / med / 1e9, 4), "unit": UNIT, "cores": 1, "kind": kind,
+               "sample": "3 timed passes over the full workload (median) after 1 warm-up, reference "
+                         "flatrun_native._C built from its sources (scalar, single-threaded on x86)"}
+
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": wl["desc"], "global_batch": batch * world, "seq_len": 1,
+                       "parallelism": f"row-shard x{world}" if world > 1 else "single GPU",
+                       "weight_bytes_per_step": wbytes, "algorithmic_bytes_per_step": step_bytes,
+                       "layer_copies_rotated": copies,
+                       "l2": f"inputs larger than L2: {copies} distinct weight copies "
+                             f"({copies * wbytes / 1e9:.2f} GB) rotated per step, L2 {l2 / 2**20:.0f} MiB"},
+            "frac_of_8tbs": round(value / world / 8000.0, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": f"gemv_x1 <{mats[dom[0]][1]}> over the k={mats[dom[0]][3]} projections",
+                         "peak_source": peak_src},
+            "per_projection": per,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clk,
+            "gpu_launches": K * len(mats),
+        }
+        print(json.dumps(out), flush=True)
+
+    del graphs
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    be.close()
+
+
+if __name__ == "__main__":
+    main()

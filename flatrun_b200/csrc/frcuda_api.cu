@@ -1,0 +1,528 @@
+// C ABI of libfrcuda.so (declared in include/frcuda.h).
+//
+// Argument checks mirror the reference pybind11 boundary
+// (src/flatrun_native/_C.cpp:99-138, :154-283, :285-433): k must be a
+// multiple of the block size, the weight must have exactly n*(k/QK)*TS bytes,
+// x must have k columns.  They run before any CUDA call, so they behave the
+// same on a machine without a GPU.  No exception crosses the ABI: every entry
+// point returns a status and leaves a message for frc_last_error.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/frcuda.h"
+#include "launch.cuh"
+
+namespace frc {
+extern template cudaError_t launch_gemv<kQ8_0>(const GemvRequest&);
+extern template cudaError_t launch_gemv<kQ4_K>(const GemvRequest&);
+extern template cudaError_t launch_gemv<kQ5_K>(const GemvRequest&);
+extern template cudaError_t launch_gemv<kQ6_K>(const GemvRequest&);
+extern template cudaError_t launch_gemv<kQ1_0>(const GemvRequest&);
+extern template cudaError_t launch_dequant<kQ8_0>(const DequantRequest&);
+extern template cudaError_t launch_dequant<kQ4_K>(const DequantRequest&);
+extern template cudaError_t launch_dequant<kQ5_K>(const DequantRequest&);
+extern template cudaError_t launch_dequant<kQ6_K>(const DequantRequest&);
+extern template cudaError_t launch_dequant<kQ1_0>(const DequantRequest&);
+}  // namespace frc
+
+struct frc_weight {
+  int device;
+  int quant;
+  int64_t n, k;
+  size_t nbytes;
+  uint8_t* dev;
+};
+
+namespace {
+
+constexpr int kMaxGemvBatch = 16;
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(e == cudaErrorMemoryAllocation ? FRC_ERR_NOMEM : FRC_ERR_CUDA, "%s: %s", what,
+              cudaGetErrorString(e));
+}
+
+#define FRC_CUDA(call, what)                    \
+  do {                                          \
+    cudaError_t _e = (call);                    \
+    if (_e != cudaSuccess) return cuda_fail(_e, what); \
+  } while (0)
+
+bool geometry(int q, int* qk, int* ts) {
+  switch (q) {
+    case FRC_Q8_0: *qk = 32; *ts = 34; return true;
+    case FRC_Q4_K: *qk = 256; *ts = 144; return true;
+    case FRC_Q5_K: *qk = 256; *ts = 176; return true;
+    case FRC_Q6_K: *qk = 256; *ts = 210; return true;
+    case FRC_Q1_0: *qk = 128; *ts = 18; return true;
+    default: return false;
+  }
+}
+
+const char* quant_name(int q) {
+  switch (q) {
+    case FRC_Q8_0: return "Q8_0";
+    case FRC_Q4_K: return "Q4_K";
+    case FRC_Q5_K: return "Q5_K";
+    case FRC_Q6_K: return "Q6_K";
+    case FRC_Q1_0: return "Q1_0";
+    default: return "?";
+  }
+}
+
+// Checks shared by every matmul entry point; returns FRC_OK or an error.
+int check_matmul(int quant, size_t w_bytes, int64_t n, int64_t k, int64_t seq) {
+  int qk, ts;
+  if (!geometry(quant, &qk, &ts)) return fail(FRC_ERR_INVALID, "unsupported quant id %d", quant);
+  const char* q = quant_name(quant);
+  if (n < 0 || k < 0) return fail(FRC_ERR_INVALID, "%s matmul: negative shape (n=%lld, k=%lld)", q, (long long)n, (long long)k);
+  if (k % qk != 0) return fail(FRC_ERR_INVALID, "%s matmul: in_features must be a multiple of %d", q, qk);
+  if (k > (int64_t(1) << 30)) return fail(FRC_ERR_INVALID, "%s matmul: k=%lld too large", q, (long long)k);
+  if (seq < 1) return fail(FRC_ERR_INVALID, "%s matmul: batch/seq must be >= 1 (got %lld)", q, (long long)seq);
+  const unsigned long long want = (unsigned long long)n * (unsigned long long)(k / qk) * (unsigned long long)ts;
+  if (w_bytes != want)
+    return fail(FRC_ERR_INVALID, "%s matmul: weight byte size mismatch: expected %llu bytes, got %llu", q, want,
+                (unsigned long long)w_bytes);
+  return FRC_OK;
+}
+
+struct DeviceState {
+  int device = 0;
+  int sms = 0;
+  uint32_t* status = nullptr;       // device status word
+  uint32_t* status_host = nullptr;  // pinned readback
+  cudaStream_t stream = nullptr;    // stream of the host-buffer entry points
+  std::mutex mu;                    // serialises host-buffer calls on this device
+  uint8_t* scratch_w = nullptr;
+  size_t cap_w = 0;
+  float* scratch_x = nullptr;
+  size_t cap_x = 0;
+  float* scratch_y = nullptr;
+  size_t cap_y = 0;
+};
+
+std::mutex g_dev_mu;
+std::vector<std::unique_ptr<DeviceState>> g_devs;
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+  int prev = -1;
+  cudaError_t set(int dev) {
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return e;
+    if (prev == dev) return cudaSuccess;
+    return cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+// State of `dev`, created on first use (with `dev` current).
+int device_state(int dev, DeviceState** out) {
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  int count = 0;
+  FRC_CUDA(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+  if (dev < 0 || dev >= count) return fail(FRC_ERR_INVALID, "device %d out of range (%d devices)", dev, count);
+  if (g_devs.size() < static_cast<size_t>(count)) g_devs.resize(count);
+  if (!g_devs[dev]) {
+    auto s = std::make_unique<DeviceState>();
+    s->device = dev;
+    DeviceGuard g;
+    FRC_CUDA(g.set(dev), "cudaSetDevice");
+    FRC_CUDA(cudaDeviceGetAttribute(&s->sms, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
+    FRC_CUDA(cudaMalloc(&s->status, sizeof(uint32_t)), "cudaMalloc(status)");
+    FRC_CUDA(cudaMemset(s->status, 0, sizeof(uint32_t)), "cudaMemset(status)");
+    FRC_CUDA(cudaMallocHost(&s->status_host, sizeof(uint32_t)), "cudaMallocHost(status)");
+    FRC_CUDA(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    g_devs[dev] = std::move(s);
+  }
+  *out = g_devs[dev].get();
+  return FRC_OK;
+}
+
+int current_device_state(DeviceState** out) {
+  int dev = 0;
+  FRC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  return device_state(dev, out);
+}
+
+template <typename T>
+int ensure(T** buf, size_t* cap, size_t bytes, const char* what) {
+  if (bytes <= *cap) return FRC_OK;
+  if (*buf) cudaFree(*buf);
+  *buf = nullptr;
+  *cap = 0;
+  size_t want = bytes < 4096 ? 4096 : bytes;
+  want = (want + 255) / 256 * 256;
+  FRC_CUDA(cudaMalloc(reinterpret_cast<void**>(buf), want), what);
+  *cap = want;
+  return FRC_OK;
+}
+
+int launch_gemv_quant(int quant, const frc::GemvRequest& r) {
+  cudaError_t e;
+  switch (quant) {
+    case FRC_Q8_0: e = frc::launch_gemv<frc::kQ8_0>(r); break;
+    case FRC_Q4_K: e = frc::launch_gemv<frc::kQ4_K>(r); break;
+    case FRC_Q5_K: e = frc::launch_gemv<frc::kQ5_K>(r); break;
+    case FRC_Q6_K: e = frc::launch_gemv<frc::kQ6_K>(r); break;
+    case FRC_Q1_0: e = frc::launch_gemv<frc::kQ1_0>(r); break;
+    default: return fail(FRC_ERR_INVALID, "unsupported quant id %d", quant);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
+  return FRC_OK;
+}
+
+// y (seq, n) = x (seq, k) . W^T on `stream`, all pointers on device `ds`.
+int gemv_device(DeviceState* ds, int quant, const uint8_t* w, int64_t n, int64_t k, const float* x, int64_t seq,
+                float* y, cudaStream_t stream) {
+  if (n == 0) return FRC_OK;
+  if (k == 0) {
+    FRC_CUDA(cudaMemsetAsync(y, 0, sizeof(float) * n * seq, stream), "cudaMemsetAsync");
+    return FRC_OK;
+  }
+  for (int64_t c0 = 0; c0 < seq; c0 += kMaxGemvBatch) {
+    const int64_t cb = seq - c0 < kMaxGemvBatch ? seq - c0 : kMaxGemvBatch;
+    frc::GemvRequest r{};
+    r.w = w;
+    r.x = x + c0 * k;
+    r.y = y + c0 * n;
+    r.n = n;
+    r.k = static_cast<int>(k);
+    r.batch = static_cast<int>(cb);
+    r.status = ds->status;
+    r.stream = stream;
+    r.device = ds->device;
+    r.sms = ds->sms;
+    const int rc = launch_gemv_quant(quant, r);
+    if (rc != FRC_OK) return rc;
+  }
+  return FRC_OK;
+}
+
+int dequant_device(DeviceState* ds, int quant, const uint8_t* w, int64_t n_elems, float* out, cudaStream_t stream) {
+  frc::DequantRequest r{w, n_elems, out, stream, ds->sms};
+  cudaError_t e;
+  switch (quant) {
+    case FRC_Q8_0: e = frc::launch_dequant<frc::kQ8_0>(r); break;
+    case FRC_Q4_K: e = frc::launch_dequant<frc::kQ4_K>(r); break;
+    case FRC_Q5_K: e = frc::launch_dequant<frc::kQ5_K>(r); break;
+    case FRC_Q6_K: e = frc::launch_dequant<frc::kQ6_K>(r); break;
+    case FRC_Q1_0: e = frc::launch_dequant<frc::kQ1_0>(r); break;
+    default: return fail(FRC_ERR_INVALID, "unsupported quant id %d", quant);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "dequant launch");
+  return FRC_OK;
+}
+
+// Queue the status readback behind the work on ds->stream, synchronise and
+// turn a raised status word into FRC_ERR_DEVICE.
+int finish_host_call(DeviceState* ds) {
+  FRC_CUDA(cudaMemcpyAsync(ds->status_host, ds->status, sizeof(uint32_t), cudaMemcpyDeviceToHost, ds->stream),
+           "status readback");
+  FRC_CUDA(cudaStreamSynchronize(ds->stream), "cudaStreamSynchronize");
+  if (*ds->status_host != 0) {
+    const uint32_t f = *ds->status_host;
+    cudaMemsetAsync(ds->status, 0, sizeof(uint32_t), ds->stream);
+    cudaStreamSynchronize(ds->stream);
+    return fail(FRC_ERR_DEVICE, "kernel reported status 0x%x (a bounded wait ran out)", f);
+  }
+  return FRC_OK;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// Host-buffer matmul on device `dev` with weight bytes already at `w_dev`
+// (or, if w_host is non-null, uploaded into scratch first).
+int host_matmul(DeviceState* ds, int quant, const uint8_t* w_dev, const uint8_t* w_host, size_t w_bytes, int64_t n,
+                int64_t k, const float* x, int64_t seq, float* y) {
+  std::lock_guard<std::mutex> lock(ds->mu);
+  DeviceGuard g;
+  FRC_CUDA(g.set(ds->device), "cudaSetDevice");
+  if (w_host) {
+    int rc = ensure(&ds->scratch_w, &ds->cap_w, w_bytes, "cudaMalloc(weight scratch)");
+    if (rc) return rc;
+    if (w_bytes)
+      FRC_CUDA(cudaMemcpyAsync(ds->scratch_w, w_host, w_bytes, cudaMemcpyHostToDevice, ds->stream), "weight upload");
+    w_dev = ds->scratch_w;
+  }
+  int rc = ensure(&ds->scratch_x, &ds->cap_x, sizeof(float) * seq * (k ? k : 1), "cudaMalloc(x scratch)");
+  if (rc) return rc;
+  rc = ensure(&ds->scratch_y, &ds->cap_y, sizeof(float) * seq * (n ? n : 1), "cudaMalloc(y scratch)");
+  if (rc) return rc;
+  if (k && seq)
+    FRC_CUDA(cudaMemcpyAsync(ds->scratch_x, x, sizeof(float) * seq * k, cudaMemcpyHostToDevice, ds->stream), "x upload");
+  rc = gemv_device(ds, quant, w_dev, n, k, ds->scratch_x, seq, ds->scratch_y, ds->stream);
+  if (rc) return rc;
+  if (n && seq)
+    FRC_CUDA(cudaMemcpyAsync(y, ds->scratch_y, sizeof(float) * seq * n, cudaMemcpyDeviceToHost, ds->stream), "y download");
+  return finish_host_call(ds);
+}
+
+int host_dequant(DeviceState* ds, int quant, const uint8_t* w_dev, const uint8_t* w_host, size_t w_bytes,
+                 int64_t n_elems, float* out) {
+  std::lock_guard<std::mutex> lock(ds->mu);
+  DeviceGuard g;
+  FRC_CUDA(g.set(ds->device), "cudaSetDevice");
+  if (w_host) {
+    int rc = ensure(&ds->scratch_w, &ds->cap_w, w_bytes, "cudaMalloc(weight scratch)");
+    if (rc) return rc;
+    if (w_bytes)
+      FRC_CUDA(cudaMemcpyAsync(ds->scratch_w, w_host, w_bytes, cudaMemcpyHostToDevice, ds->stream), "weight upload");
+    w_dev = ds->scratch_w;
+  }
+  int rc = ensure(&ds->scratch_y, &ds->cap_y, sizeof(float) * (n_elems ? n_elems : 1), "cudaMalloc(out scratch)");
+  if (rc) return rc;
+  rc = dequant_device(ds, quant, w_dev, n_elems, ds->scratch_y, ds->stream);
+  if (rc) return rc;
+  if (n_elems)
+    FRC_CUDA(cudaMemcpyAsync(out, ds->scratch_y, sizeof(float) * n_elems, cudaMemcpyDeviceToHost, ds->stream),
+             "dequant download");
+  return finish_host_call(ds);
+}
+
+// Element count and block count checks of the dequant entry points.  `strict`
+// is the _C.cpp rule (element count a multiple of QK); otherwise the NumPy
+// rule (ceil(count / QK) blocks, trailing padding dropped, gguf.py:61-75).
+int check_dequant(int quant, size_t w_bytes, int64_t n_elems, bool strict) {
+  int qk, ts;
+  if (!geometry(quant, &qk, &ts)) return fail(FRC_ERR_INVALID, "unsupported quant id %d", quant);
+  if (n_elems < 0) return fail(FRC_ERR_INVALID, "%s dequant: negative element count", quant_name(quant));
+  if (strict && n_elems % qk != 0)
+    return fail(FRC_ERR_INVALID, "%s tensor element count must be a multiple of %d", quant_name(quant), qk);
+  const unsigned long long blocks = (unsigned long long)((n_elems + qk - 1) / qk);
+  if (w_bytes != blocks * ts)
+    return fail(FRC_ERR_INVALID, "%s weight byte size mismatch: expected %llu bytes, got %llu", quant_name(quant),
+                blocks * ts, (unsigned long long)w_bytes);
+  return FRC_OK;
+}
+
+int stateless_matmul(int quant, const float* x, int64_t seq, const uint8_t* w, size_t w_bytes, int64_t n, int64_t k,
+                     float* y) {
+  int rc = check_matmul(quant, w_bytes, n, k, seq);
+  if (rc) return rc;
+  if ((w_bytes && !w) || (seq * k && !x) || (seq * n && !y)) return fail(FRC_ERR_INVALID, "null buffer");
+  DeviceState* ds;
+  rc = current_device_state(&ds);
+  if (rc) return rc;
+  return host_matmul(ds, quant, nullptr, w, w_bytes, n, k, x, seq, y);
+}
+
+int stateless_dequant(int quant, const uint8_t* w, size_t w_bytes, int64_t out_dim, int64_t in_dim, float* out,
+                      bool strict) {
+  if (out_dim < 0 || in_dim < 0) return fail(FRC_ERR_INVALID, "negative shape");
+  const int64_t n_elems = out_dim * in_dim;
+  int rc = check_dequant(quant, w_bytes, n_elems, strict);
+  if (rc) return rc;
+  if ((w_bytes && !w) || (n_elems && !out)) return fail(FRC_ERR_INVALID, "null buffer");
+  DeviceState* ds;
+  rc = current_device_state(&ds);
+  if (rc) return rc;
+  return host_dequant(ds, quant, nullptr, w, w_bytes, n_elems, out);
+}
+
+}  // namespace
+
+extern "C" {
+
+int frc_version(char* buf, size_t len) {
+  static const char kVersion[] = "frcuda 0.1.0 (sm_100a; Q8_0 Q4_K Q5_K Q6_K Q1_0; TMA-staged GEMV)";
+  if (!buf || len == 0) return fail(FRC_ERR_INVALID, "null buffer");
+  snprintf(buf, len, "%s", kVersion);
+  return FRC_OK;
+}
+
+int frc_is_neon(void) { return 0; }
+
+int frc_last_error(char* buf, size_t len) {
+  if (!buf || len == 0) return FRC_ERR_INVALID;
+  snprintf(buf, len, "%s", g_err.c_str());
+  return FRC_OK;
+}
+
+int frc_device_count(int* count) {
+  if (!count) return fail(FRC_ERR_INVALID, "null pointer");
+  *count = 0;
+  FRC_CUDA(cudaGetDeviceCount(count), "cudaGetDeviceCount");
+  return FRC_OK;
+}
+
+int frc_block_geometry(int quant, int* elems_per_block, int* bytes_per_block) {
+  int qk, ts;
+  if (!geometry(quant, &qk, &ts)) return fail(FRC_ERR_INVALID, "unsupported quant id %d", quant);
+  if (elems_per_block) *elems_per_block = qk;
+  if (bytes_per_block) *bytes_per_block = ts;
+  return FRC_OK;
+}
+
+int frc_weight_nbytes(int quant, int64_t n, int64_t k, size_t* nbytes) {
+  int qk, ts;
+  if (!geometry(quant, &qk, &ts)) return fail(FRC_ERR_INVALID, "unsupported quant id %d", quant);
+  if (n < 0 || k < 0 || k % qk) return fail(FRC_ERR_INVALID, "%s: k=%lld is not a multiple of %d", quant_name(quant), (long long)k, qk);
+  if (nbytes) *nbytes = static_cast<size_t>(n) * static_cast<size_t>(k / qk) * ts;
+  return FRC_OK;
+}
+
+int frc_device_status(int device, uint32_t* flags) {
+  if (!flags) return fail(FRC_ERR_INVALID, "null pointer");
+  DeviceState* ds;
+  int rc = device_state(device, &ds);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lock(ds->mu);
+  DeviceGuard g;
+  FRC_CUDA(g.set(device), "cudaSetDevice");
+  FRC_CUDA(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  FRC_CUDA(cudaMemcpy(flags, ds->status, sizeof(uint32_t), cudaMemcpyDeviceToHost), "status read");
+  FRC_CUDA(cudaMemset(ds->status, 0, sizeof(uint32_t)), "status clear");
+  return FRC_OK;
+}
+
+int frc_gemv(int quant, const void* w_dev, size_t w_bytes, int64_t n, int64_t k, const float* x_dev, int64_t batch,
+             float* y_dev, void* stream) {
+  int rc = check_matmul(quant, w_bytes, n, k, batch);
+  if (rc) return rc;
+  if (batch > kMaxGemvBatch) return fail(FRC_ERR_INVALID, "frc_gemv: batch %lld > %d", (long long)batch, kMaxGemvBatch);
+  if ((w_bytes && !w_dev) || (batch * k && !x_dev) || (batch * n && !y_dev)) return fail(FRC_ERR_INVALID, "null buffer");
+  if (!aligned(w_dev, 16)) return fail(FRC_ERR_INVALID, "frc_gemv: weight must be 16-byte aligned");
+  if (!aligned(x_dev, 16)) return fail(FRC_ERR_INVALID, "frc_gemv: x must be 16-byte aligned");
+  if (!aligned(y_dev, 4)) return fail(FRC_ERR_INVALID, "frc_gemv: y must be 4-byte aligned");
+  DeviceState* ds;
+  rc = current_device_state(&ds);
+  if (rc) return rc;
+  return gemv_device(ds, quant, static_cast<const uint8_t*>(w_dev), n, k, x_dev, batch, y_dev,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int frc_dequant_dev(int quant, const void* w_dev, size_t w_bytes, int64_t n_elems, float* out_dev, void* stream) {
+  int rc = check_dequant(quant, w_bytes, n_elems, false);
+  if (rc) return rc;
+  if ((w_bytes && !w_dev) || (n_elems && !out_dev)) return fail(FRC_ERR_INVALID, "null buffer");
+  if (!aligned(w_dev, 2) || !aligned(out_dev, 4)) return fail(FRC_ERR_INVALID, "frc_dequant_dev: misaligned buffer");
+  DeviceState* ds;
+  rc = current_device_state(&ds);
+  if (rc) return rc;
+  return dequant_device(ds, quant, static_cast<const uint8_t*>(w_dev), n_elems, out_dev,
+                        static_cast<cudaStream_t>(stream));
+}
+
+int frc_weight_create(int device, int quant, const void* host, size_t nbytes, int64_t n, int64_t k, frc_weight** out) {
+  if (!out) return fail(FRC_ERR_INVALID, "null output handle");
+  *out = nullptr;
+  int rc = check_matmul(quant, nbytes, n, k, 1);
+  if (rc) return rc;
+  if (nbytes && !host) return fail(FRC_ERR_INVALID, "null host buffer");
+  if (frc::env_int("FRC_FAULT_INJECT_OOM", 0)) return fail(FRC_ERR_NOMEM, "weight upload: injected allocation failure");
+  DeviceState* ds;
+  rc = device_state(device, &ds);
+  if (rc) return rc;
+  DeviceGuard g;
+  FRC_CUDA(g.set(device), "cudaSetDevice");
+  uint8_t* dev = nullptr;
+  const size_t alloc = ((nbytes ? nbytes : 1) + 255) / 256 * 256;
+  FRC_CUDA(cudaMalloc(&dev, alloc), "cudaMalloc(weight)");
+  if (nbytes) {
+    cudaError_t e = cudaMemcpy(dev, host, nbytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      cudaFree(dev);
+      return cuda_fail(e, "weight upload");
+    }
+  }
+  frc_weight* w = new frc_weight{device, quant, n, k, nbytes, dev};
+  *out = w;
+  return FRC_OK;
+}
+
+int frc_weight_free(frc_weight* w) {
+  if (!w) return FRC_OK;
+  DeviceGuard g;
+  cudaError_t e = g.set(w->device);
+  if (e == cudaSuccess) e = cudaFree(w->dev);
+  delete w;
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFree(weight)");
+  return FRC_OK;
+}
+
+int frc_weight_info(const frc_weight* w, const void** dev_ptr, size_t* nbytes, int* quant, int64_t* n, int64_t* k,
+                    int* device) {
+  if (!w) return fail(FRC_ERR_INVALID, "null weight handle");
+  if (dev_ptr) *dev_ptr = w->dev;
+  if (nbytes) *nbytes = w->nbytes;
+  if (quant) *quant = w->quant;
+  if (n) *n = w->n;
+  if (k) *k = w->k;
+  if (device) *device = w->device;
+  return FRC_OK;
+}
+
+int frc_weight_matmul(frc_weight* w, const float* x_host, int64_t seq, float* y_host) {
+  if (!w) return fail(FRC_ERR_INVALID, "null weight handle");
+  if (seq < 1) return fail(FRC_ERR_INVALID, "seq must be >= 1");
+  if ((seq * w->k && !x_host) || (seq * w->n && !y_host)) return fail(FRC_ERR_INVALID, "null buffer");
+  DeviceState* ds;
+  int rc = device_state(w->device, &ds);
+  if (rc) return rc;
+  return host_matmul(ds, w->quant, w->dev, nullptr, w->nbytes, w->n, w->k, x_host, seq, y_host);
+}
+
+int frc_weight_matmul_dev(frc_weight* w, const float* x_dev, int64_t seq, float* y_dev, void* stream) {
+  if (!w) return fail(FRC_ERR_INVALID, "null weight handle");
+  if (seq < 1) return fail(FRC_ERR_INVALID, "seq must be >= 1");
+  if ((seq * w->k && !x_dev) || (seq * w->n && !y_dev)) return fail(FRC_ERR_INVALID, "null buffer");
+  if (!aligned(x_dev, 16) || !aligned(y_dev, 4)) return fail(FRC_ERR_INVALID, "misaligned x or y");
+  DeviceState* ds;
+  int rc = device_state(w->device, &ds);
+  if (rc) return rc;
+  DeviceGuard g;
+  FRC_CUDA(g.set(w->device), "cudaSetDevice");
+  return gemv_device(ds, w->quant, w->dev, w->n, w->k, x_dev, seq, y_dev, static_cast<cudaStream_t>(stream));
+}
+
+int frc_weight_dequant(frc_weight* w, float* out_host) {
+  if (!w) return fail(FRC_ERR_INVALID, "null weight handle");
+  if (w->n * w->k && !out_host) return fail(FRC_ERR_INVALID, "null buffer");
+  DeviceState* ds;
+  int rc = device_state(w->device, &ds);
+  if (rc) return rc;
+  return host_dequant(ds, w->quant, w->dev, nullptr, w->nbytes, w->n * w->k, out_host);
+}
+
+#define FRC_MIRROR(suffix, QUANT, STRICT)                                                                      \
+  int frc_matmul_##suffix(const float* x, const uint8_t* w, size_t w_bytes, int64_t n, int64_t k, float* y) {   \
+    return stateless_matmul(QUANT, x, 1, w, w_bytes, n, k, y);                                                 \
+  }                                                                                                            \
+  int frc_matmul_##suffix##_batched(const float* x, int64_t seq, const uint8_t* w, size_t w_bytes, int64_t n,    \
+                                    int64_t k, float* y) {                                                     \
+    return stateless_matmul(QUANT, x, seq, w, w_bytes, n, k, y);                                               \
+  }                                                                                                            \
+  int frc_dequant_##suffix(const uint8_t* w, size_t w_bytes, int64_t out_dim, int64_t in_dim, float* out) {      \
+    return stateless_dequant(QUANT, w, w_bytes, out_dim, in_dim, out, STRICT);                                 \
+  }
+
+FRC_MIRROR(q4_k, FRC_Q4_K, true)
+FRC_MIRROR(q8_0, FRC_Q8_0, true)
+FRC_MIRROR(q6_k, FRC_Q6_K, true)
+FRC_MIRROR(q5_k, FRC_Q5_K, false)
+FRC_MIRROR(q1_0, FRC_Q1_0, false)
+
+}  // extern "C"

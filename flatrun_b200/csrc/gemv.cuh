@@ -1,0 +1,376 @@
+// Fused dequantise + GEMV kernels for GGUF row-major weights.
+//
+// Both kernels are persistent and warp-specialised:
+//  * the last warp is the producer: one lane streams tiles of `RT` consecutive
+//    rows (a contiguous byte range of the weight) into a ring of shared-memory
+//    stages with cp.async.bulk, signalling each stage's mbarrier;
+//  * the other warps are consumers.  Consumer thread t owns the units
+//    t, t + NCT, t + 2*NCT, ... of every row (a unit is a fixed slice of one
+//    block, see formats.cuh), so it decodes the same columns of each row of
+//    every tile.
+// Each CTA owns the contiguous rows [c*n/G, (c+1)*n/G), which balances work
+// to within one row; a tile's global start is rounded down to 16 bytes for
+// the bulk copy (its offset is kept in shared memory), and the <16-byte tail
+// of the last tile is copied by the producer lane.
+//
+// gemv_x1: batch 1.  A consumer keeps its units' activations (and their
+//   16-element sums) in registers for the whole launch, so x is read from
+//   global memory once per CTA and the inner loop touches only the weight
+//   stream in shared memory.
+// gemv_xb: batch 2..16.  Each unit is decoded once per row into registers and
+//   reused for every activation column, which are read through L1.
+//
+// Per-row partial sums are reduced with a register-transpose butterfly
+// (V-1 shuffles for V rows), across warps through shared memory, and written
+// by warp 0.  Every mbarrier wait is bounded by wall-clock time; on a timeout
+// the CTA raises a shared abort flag, records a status bit, stops computing
+// and still passes every barrier, so it always exits.
+#pragma once
+
+#include "formats.cuh"
+
+namespace frc {
+
+constexpr int kMaxConsumerWarps = 15;  // + 1 producer = 512 threads, 128 registers each
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s per wait
+
+struct GemvParams {
+  const uint8_t* w;   // raw blocks, 16-byte aligned
+  const float* x;     // (batch, k)
+  float* y;           // (batch, n)
+  int64_t n;          // rows
+  int k;              // columns
+  int batch;
+  int row_bytes;      // (k / QK) * TS
+  int units;          // units per row
+  int stage_stride;   // bytes per shared-memory stage
+  int nstage;
+  uint32_t* status;   // device status word
+};
+
+FRC_DEVICE_INLINE uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait on an mbarrier phase that also gives up as soon as another
+// thread of the CTA has raised `abort`.
+FRC_DEVICE_INLINE bool wait_phase(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
+// Sum V per-lane values across the warp.  Afterwards lane l holds the total of
+// value index (l >> (5 - log2 V)) for V <= 32; V > 32 is done in 32-chunks and
+// lane l holds chunk c's value (c*32 + l) in out[c].
+template <int V>
+FRC_DEVICE_INLINE void butterfly(float (&v)[V], int lane) {
+  static_assert((V & (V - 1)) == 0 && V >= 1 && V <= 32, "V must be a power of two <= 32");
+  int width = V;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    if (width > 1) {
+      const bool upper = (lane & o) != 0;
+      const int h = width / 2;
+#pragma unroll
+      for (int i = 0; i < V / 2; ++i) {
+        if (i < h) {
+          const float send = upper ? v[i] : v[i + h];
+          const float keep = upper ? v[i + h] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      width = h;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+    }
+  }
+}
+
+struct SmemLayout {
+  uint64_t* full;
+  uint64_t* empty;
+  int* abort;
+  float* red;       // [2][kMaxConsumerWarps][VMAX]
+  uint8_t* stages;  // nstage * stage_stride
+};
+
+template <int VMAX>
+FRC_DEVICE_INLINE SmemLayout carve(uint8_t* smem, int nstage) {
+  SmemLayout L;
+  L.full = reinterpret_cast<uint64_t*>(smem);
+  L.empty = L.full + nstage;
+  L.abort = reinterpret_cast<int*>(L.empty + nstage);
+  L.red = reinterpret_cast<float*>(smem + 256);
+  const int red_bytes = 2 * kMaxConsumerWarps * VMAX * 4;
+  L.stages = smem + ((256 + red_bytes + 127) / 128) * 128;
+  return L;
+}
+
+template <int VMAX>
+__host__ __device__ constexpr int smem_header_bytes() {
+  return ((256 + 2 * kMaxConsumerWarps * VMAX * 4 + 127) / 128) * 128;
+}
+
+// Producer lane: stream the tiles of rows [r0, r1) in chunks of RT rows.
+FRC_DEVICE_INLINE void produce(const GemvParams& p, const SmemLayout& L, int64_t r0, int64_t r1, int RT) {
+  volatile int* abort = L.abort;
+  int issued = 0;
+  for (int64_t t0 = r0; t0 < r1; t0 += RT, ++issued) {
+    const int s = issued % p.nstage;
+    const uint32_t ph = static_cast<uint32_t>(issued / p.nstage) & 1u;
+    if (!wait_phase(&L.empty[s], ph ^ 1u, abort)) {
+      atomicOr(p.status, kStatusEmptyWaitTimeout);
+      break;
+    }
+    const int64_t t1 = t0 + RT < r1 ? t0 + RT : r1;
+    const uint64_t gs = static_cast<uint64_t>(t0) * p.row_bytes;
+    const uint64_t ge = static_cast<uint64_t>(t1) * p.row_bytes;
+    const uint64_t a0 = gs & ~uint64_t(15), a1 = ge & ~uint64_t(15);
+    uint8_t* dst = L.stages + static_cast<size_t>(s) * p.stage_stride;
+    for (uint64_t b = a1; b < ge; ++b) dst[b - a0] = p.w[b];
+    const uint32_t bulk = static_cast<uint32_t>(a1 - a0);
+    mbar_arrive_expect_tx(&L.full[s], bulk);
+    if (bulk) bulk_g2s(dst, p.w + a0, bulk, &L.full[s]);
+  }
+  // Every issued copy lands before this lane (and so the CTA) exits.
+  const int first = issued > p.nstage ? issued - p.nstage : 0;
+  for (int i = first; i < issued; ++i) {
+    if (!wait_phase(&L.full[i % p.nstage], static_cast<uint32_t>(i / p.nstage) & 1u, abort)) {
+      // the abort flag may stop this wait early; give in-flight copies a
+      // second bounded chance that ignores the flag
+      int zero = 0;
+      if (!wait_phase(&L.full[i % p.nstage], static_cast<uint32_t>(i / p.nstage) & 1u, &zero)) {
+        atomicOr(p.status, kStatusDrainTimeout);
+      }
+    }
+  }
+}
+
+FRC_DEVICE_INLINE void cta_rows(int64_t n, int64_t& r0, int64_t& r1) {
+  r0 = static_cast<int64_t>(blockIdx.x) * n / gridDim.x;
+  r1 = static_cast<int64_t>(blockIdx.x + 1) * n / gridDim.x;
+}
+
+FRC_DEVICE_INLINE void load_run16(const float* src, float* dst) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 v = __ldg(s4 + i);
+    dst[4 * i] = v.x;
+    dst[4 * i + 1] = v.y;
+    dst[4 * i + 2] = v.z;
+    dst[4 * i + 3] = v.w;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// batch 1, activations in registers
+// ---------------------------------------------------------------------------
+template <int Q, int UPT, int RT>
+__global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1) gemv_x1(GemvParams p) {
+  using F = Fmt<Q>;
+  constexpr int E = 16 * F::NRUN;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const SmemLayout L = carve<RT>(smem, p.nstage);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ncw = static_cast<int>(blockDim.x >> 5) - 1;
+  const int nct = ncw * 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.nstage; ++s) {
+      mbar_init(&L.full[s], 1);
+      mbar_init(&L.empty[s], ncw);
+    }
+    *L.abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  int64_t r0, r1;
+  cta_rows(p.n, r0, r1);
+
+  if (warp == ncw) {
+    if (lane == 0) produce(p, L, r0, r1, RT);
+    return;
+  }
+
+  // --- consumer: activations of the owned units, kept in registers --------
+  const int ct = threadIdx.x;
+  float xv[UPT][E];
+  float xs[UPT][F::NRUN];
+  int uoff[UPT], uj[UPT];
+  bool uval[UPT];
+#pragma unroll
+  for (int i = 0; i < UPT; ++i) {
+    const int u = ct + i * nct;
+    uval[i] = u < p.units;
+    const int b = uval[i] ? u / F::UPB : 0;
+    uj[i] = uval[i] ? u % F::UPB : 0;
+    uoff[i] = b * F::TS;
+#pragma unroll
+    for (int r = 0; r < F::NRUN; ++r) {
+      if (uval[i]) {
+        load_run16(p.x + static_cast<int64_t>(b) * F::QK + run_start<Q>(uj[i], r), &xv[i][16 * r]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) xv[i][16 * r + e] = 0.f;
+      }
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) s += xv[i][16 * r + e];
+      xs[i][r] = s;
+    }
+  }
+
+  volatile int* abort = L.abort;
+  int it = 0;
+  for (int64_t t0 = r0; t0 < r1; t0 += RT, ++it) {
+    const int s = it % p.nstage;
+    const uint32_t ph = static_cast<uint32_t>(it / p.nstage) & 1u;
+    const int rows = static_cast<int>((t0 + RT < r1 ? t0 + RT : r1) - t0);
+    float acc[RT];
+#pragma unroll
+    for (int r = 0; r < RT; ++r) acc[r] = 0.f;
+    if (wait_phase(&L.full[s], ph, abort)) {
+      const uint8_t* base = L.stages + static_cast<size_t>(s) * p.stage_stride +
+                            ((static_cast<uint64_t>(t0) * p.row_bytes) & 15u);
+#pragma unroll
+      for (int r = 0; r < RT; ++r) {
+        if (r < rows) {
+          const uint8_t* row = base + r * p.row_bytes;
+#pragma unroll
+          for (int i = 0; i < UPT; ++i) {
+            if (uval[i]) acc[r] += UnitDot<Q>::dot(row + uoff[i], uj[i], xv[i], xs[i]);
+          }
+        }
+      }
+    } else {
+      atomicOr(p.status, kStatusFullWaitTimeout);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&L.empty[s]);
+
+    butterfly<RT>(acc, lane);
+    float* red = L.red + (it & 1) * kMaxConsumerWarps * RT;
+    constexpr int kLanesPerValue = 32 / RT;
+    if ((lane & (kLanesPerValue - 1)) == 0) red[warp * RT + lane / kLanesPerValue] = acc[0];
+    named_barrier_sync(1, nct);
+    if (warp == 0 && lane < rows) {
+      float v = 0.f;
+      for (int w = 0; w < ncw; ++w) v += red[w * RT + lane];
+      if (!*abort) p.y[t0 + lane] = v;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// batch 2..BMAX, activations through L1
+// ---------------------------------------------------------------------------
+template <int Q, int RT, int BMAX>
+__global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1) gemv_xb(GemvParams p) {
+  using F = Fmt<Q>;
+  constexpr int E = 16 * F::NRUN;
+  constexpr int V = RT * BMAX;  // values reduced per tile, index b*RT + r
+  constexpr int VW = V < 32 ? V : 32;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const SmemLayout L = carve<V>(smem, p.nstage);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ncw = static_cast<int>(blockDim.x >> 5) - 1;
+  const int nct = ncw * 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.nstage; ++s) {
+      mbar_init(&L.full[s], 1);
+      mbar_init(&L.empty[s], ncw);
+    }
+    *L.abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  int64_t r0, r1;
+  cta_rows(p.n, r0, r1);
+
+  if (warp == ncw) {
+    if (lane == 0) produce(p, L, r0, r1, RT);
+    return;
+  }
+
+  volatile int* abort = L.abort;
+  int it = 0;
+  for (int64_t t0 = r0; t0 < r1; t0 += RT, ++it) {
+    const int s = it % p.nstage;
+    const uint32_t ph = static_cast<uint32_t>(it / p.nstage) & 1u;
+    const int rows = static_cast<int>((t0 + RT < r1 ? t0 + RT : r1) - t0);
+    float acc[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) acc[v] = 0.f;
+    if (wait_phase(&L.full[s], ph, abort)) {
+      const uint8_t* base = L.stages + static_cast<size_t>(s) * p.stage_stride +
+                            ((static_cast<uint64_t>(t0) * p.row_bytes) & 15u);
+      for (int u = threadIdx.x; u < p.units; u += nct) {
+        const int b = u / F::UPB, j = u % F::UPB;
+        const float* xb = p.x + static_cast<int64_t>(b) * F::QK;
+#pragma unroll
+        for (int r = 0; r < RT; ++r) {
+          if (r < rows) {
+            float wv[E];
+            UnitDecode<Q>::run(base + r * p.row_bytes + b * F::TS, j, wv);
+#pragma unroll
+            for (int c = 0; c < BMAX; ++c) {
+              if (c < p.batch) {
+                float a = 0.f;
+#pragma unroll
+                for (int rr = 0; rr < F::NRUN; ++rr) {
+                  float xr[16];
+                  load_run16(xb + static_cast<int64_t>(c) * p.k + run_start<Q>(j, rr), xr);
+#pragma unroll
+                  for (int e = 0; e < 16; ++e) a = fmaf(wv[16 * rr + e], xr[e], a);
+                }
+                acc[c * RT + r] += a;
+              }
+            }
+          }
+        }
+      }
+    } else {
+      atomicOr(p.status, kStatusFullWaitTimeout);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&L.empty[s]);
+
+    float* red = L.red + (it & 1) * kMaxConsumerWarps * V;
+    constexpr int kLanesPerValue = 32 / VW;
+#pragma unroll
+    for (int c0 = 0; c0 < V; c0 += 32) {
+      float part[VW];
+#pragma unroll
+      for (int i = 0; i < VW; ++i) part[i] = acc[c0 + i];
+      butterfly<VW>(part, lane);
+      if ((lane & (kLanesPerValue - 1)) == 0) red[warp * V + c0 + lane / kLanesPerValue] = part[0];
+    }
+    named_barrier_sync(1, nct);
+    if (warp == 0) {
+      for (int v = lane; v < V; v += 32) {
+        const int r = v % RT, c = v / RT;
+        if (r < rows && c < p.batch) {
+          float sum = 0.f;
+          for (int w = 0; w < ncw; ++w) sum += red[w * V + v];
+          if (!*abort) p.y[static_cast<int64_t>(c) * p.n + t0 + r] = sum;
+        }
+      }
+    }
+  }
+}
+
+}  // namespace frc

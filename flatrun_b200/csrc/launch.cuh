@@ -1,0 +1,218 @@
+// Host-side launch of the per-format kernels: configuration choice, dynamic
+// shared-memory opt-in and occupancy, cached per (device, kernel).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdlib>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "gemv.cuh"
+
+namespace frc {
+
+struct GemvRequest {
+  const uint8_t* w;
+  const float* x;
+  float* y;
+  int64_t n;
+  int k;
+  int batch;  // 1..16
+  uint32_t* status;
+  cudaStream_t stream;
+  int device;
+  int sms;
+};
+
+struct DequantRequest {
+  const uint8_t* w;
+  int64_t n_elems;
+  float* out;
+  cudaStream_t stream;
+  int sms;
+};
+
+// Integer knob from the environment (used for tuning sweeps), or `def`.
+inline int env_int(const char* name, int def) {
+  const char* s = std::getenv(name);
+  if (!s || !*s) return def;
+  return std::atoi(s);
+}
+
+// Blocks of `kernel` resident per SM with `threads` threads and `smem` bytes,
+// after opting the kernel into `smem` bytes of dynamic shared memory.
+inline cudaError_t kernel_occupancy(const void* kernel, int device, int threads, size_t smem, int* blocks) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, int, size_t>, int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_tuple(kernel, device, threads, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *blocks = it->second;
+    return cudaSuccess;
+  }
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  int nb = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kernel, threads, smem);
+  if (e != cudaSuccess) return e;
+  if (nb < 1) return cudaErrorInvalidConfiguration;
+  cache[key] = nb;
+  *blocks = nb;
+  return cudaSuccess;
+}
+
+inline int round_up(int v, int m) { return (v + m - 1) / m * m; }
+
+// Shared-memory stage geometry for tiles of `rt` rows.
+inline void stage_geometry(int row_bytes, int rt, int* stride, int* nstage) {
+  *stride = round_up(rt * row_bytes + 32, 128);
+  const int target = env_int("FRC_STAGE_BYTES", 64 * 1024);
+  int ns = target / *stride;
+  ns = ns < 2 ? 2 : (ns > 8 ? 8 : ns);
+  const int forced = env_int("FRC_NSTAGE", 0);
+  *nstage = forced > 0 ? forced : ns;
+}
+
+template <typename K>
+inline cudaError_t launch_persistent(K kernel, GemvParams p, int ncw, size_t smem, const GemvRequest& r) {
+  const int threads = (ncw + 1) * 32;
+  int per_sm = 0;
+  cudaError_t e = kernel_occupancy(reinterpret_cast<const void*>(kernel), r.device, threads, smem, &per_sm);
+  if (e != cudaSuccess) return e;
+  const int cap = env_int("FRC_CTAS_PER_SM", 0);
+  if (cap > 0 && cap < per_sm) per_sm = cap;
+  int64_t grid = static_cast<int64_t>(per_sm) * r.sms;
+  if (grid > p.n) grid = p.n;
+  if (grid < 1) grid = 1;
+  kernel<<<static_cast<unsigned>(grid), threads, smem, r.stream>>>(p);
+  return cudaGetLastError();
+}
+
+inline int rows_per_tile(int row_bytes);
+
+template <int Q, int UPT>
+inline cudaError_t launch_x1(GemvParams p, const GemvRequest& r, int ncw) {
+  const int rt = rows_per_tile(p.row_bytes);
+  stage_geometry(p.row_bytes, rt, &p.stage_stride, &p.nstage);
+  switch (rt) {
+    case 2: {
+      const size_t smem = smem_header_bytes<2>() + static_cast<size_t>(p.nstage) * p.stage_stride;
+      return launch_persistent(gemv_x1<Q, UPT, 2>, p, ncw, smem, r);
+    }
+    case 4: {
+      const size_t smem = smem_header_bytes<4>() + static_cast<size_t>(p.nstage) * p.stage_stride;
+      return launch_persistent(gemv_x1<Q, UPT, 4>, p, ncw, smem, r);
+    }
+    default: {
+      const size_t smem = smem_header_bytes<8>() + static_cast<size_t>(p.nstage) * p.stage_stride;
+      return launch_persistent(gemv_x1<Q, UPT, 8>, p, ncw, smem, r);
+    }
+  }
+}
+
+template <int Q, int RT, int BMAX>
+inline cudaError_t launch_xb_rt(GemvParams p, const GemvRequest& r) {
+  const int ncw = p.units >= 32 * kMaxConsumerWarps ? kMaxConsumerWarps : (p.units + 31) / 32;
+  stage_geometry(p.row_bytes, RT, &p.stage_stride, &p.nstage);
+  const size_t smem = smem_header_bytes<RT * BMAX>() + static_cast<size_t>(p.nstage) * p.stage_stride;
+  return launch_persistent(gemv_xb<Q, RT, BMAX>, p, ncw, smem, r);
+}
+
+// Rows per tile: as many as the accumulator budget (RT * BMAX <= 32) and
+// the row length allow.
+inline int rows_per_tile(int row_bytes) {
+  int rt = 8;
+  if (row_bytes > 4096) rt = 4;
+  if (row_bytes > 16384) rt = 2;
+  const int forced = env_int("FRC_RT", 0);
+  if (forced == 2 || forced == 4 || forced == 8) rt = forced;
+  return rt;
+}
+
+template <int Q, int BMAX>
+inline cudaError_t launch_xb(GemvParams p, const GemvRequest& r) {
+  int rt = rows_per_tile(p.row_bytes);
+  if (rt * BMAX > 32) rt = 32 / BMAX;
+  if constexpr (BMAX == 4) {
+    if (rt == 8) return launch_xb_rt<Q, 8, 4>(p, r);
+    if (rt == 4) return launch_xb_rt<Q, 4, 4>(p, r);
+    return launch_xb_rt<Q, 2, 4>(p, r);
+  } else if constexpr (BMAX == 8) {
+    if (rt == 4) return launch_xb_rt<Q, 4, 8>(p, r);
+    return launch_xb_rt<Q, 2, 8>(p, r);
+  } else {
+    return launch_xb_rt<Q, 2, 16>(p, r);
+  }
+}
+
+// Largest tile footprint must fit in shared memory with two stages.
+template <int Q>
+inline bool tiles_fit(int row_bytes) {
+  return 2 * (2 * row_bytes + 32) + 4096 <= 200 * 1024;
+}
+
+template <int Q>
+cudaError_t launch_gemv(const GemvRequest& r) {
+  using F = Fmt<Q>;
+  GemvParams p{};
+  p.w = r.w;
+  p.x = r.x;
+  p.y = r.y;
+  p.n = r.n;
+  p.k = r.k;
+  p.batch = r.batch;
+  p.row_bytes = (r.k / F::QK) * F::TS;
+  p.units = (r.k / F::QK) * F::UPB;
+  p.status = r.status;
+  if (!tiles_fit<Q>(p.row_bytes)) return cudaErrorInvalidValue;
+  constexpr int E = 16 * F::NRUN;
+  const bool force_xb = env_int("FRC_FORCE_XB", 0) != 0;
+  if (r.batch == 1 && !force_xb) {
+    const int cap1 = 32 * kMaxConsumerWarps;
+    if (p.units <= cap1) return launch_x1<Q, 1>(p, r, (p.units + 31) / 32);
+    if constexpr (E == 32) {
+      if (p.units <= 2 * cap1) return launch_x1<Q, 2>(p, r, (p.units + 63) / 64);
+    }
+  }
+  if (r.batch <= 4) return launch_xb<Q, 4>(p, r);
+  if (r.batch <= 8) return launch_xb<Q, 8>(p, r);
+  return launch_xb<Q, 16>(p, r);
+}
+
+// ---------------------------------------------------------------------------
+// Bit-exact dequantisation: thread i writes elements [4i, 4i+4).
+// ---------------------------------------------------------------------------
+template <int Q>
+__global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict__ w, int64_t n_elems,
+                                                     float* __restrict__ out) {
+  using F = Fmt<Q>;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * 4;
+  for (int64_t e0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; e0 < n_elems;
+       e0 += stride) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t e = e0 + i;
+      if (e < n_elems) {
+        const int64_t b = e / F::QK;
+        out[e] = dequant_elem<Q>(w + b * F::TS, static_cast<int>(e - b * F::QK));
+      }
+    }
+  }
+}
+
+template <int Q>
+cudaError_t launch_dequant(const DequantRequest& r) {
+  if (r.n_elems <= 0) return cudaSuccess;
+  const int64_t threads_needed = (r.n_elems + 3) / 4;
+  int64_t grid = (threads_needed + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(r.sms) * 16;
+  if (grid > cap) grid = cap;
+  dequant_kernel<Q><<<static_cast<unsigned>(grid), 256, 0, r.stream>>>(r.w, r.n_elems, r.out);
+  return cudaGetLastError();
+}
+
+}  // namespace frc

@@ -1,0 +1,146 @@
+/*
+ * frcuda.h - C ABI of libfrcuda.so, the B200 (sm_100a) backend for Flatrun's
+ * fused GGUF block-dequantise + matrix-vector product.
+ *
+ * The reference binds this path through pybind11 (module flatrun_native._C,
+ * src/flatrun_native/_C.cpp) and selects it through the backend slot
+ * (src/flatrun/runtime/backend.py).  Every reference entry point has a
+ * counterpart here with plain pointers and sizes, an int status instead of a
+ * C++ exception, and no torch or Python types:
+ *
+ *   reference (_C.cpp)                     here
+ *   matmul_q4_k        :99-138             frc_matmul_q4_k
+ *   matmul_q4_k_batched:154-197            frc_matmul_q4_k_batched
+ *   dequant_q4_k       :47-85              frc_dequant_q4_k
+ *   matmul_q8_0        :326-355            frc_matmul_q8_0
+ *   matmul_q8_0_batched:199-242            frc_matmul_q8_0_batched
+ *   dequant_q8_0       :285-320            frc_dequant_q8_0
+ *   matmul_q6_k        :404-433            frc_matmul_q6_k
+ *   matmul_q6_k_batched:244-283            frc_matmul_q6_k_batched
+ *   dequant_q6_k       :363-398            frc_dequant_q6_k
+ *   is_neon            :441-447            frc_is_neon (always 0)
+ *   version            :449-451            frc_version
+ *   (none: NumPy only, dequant/gguf.py:223, :266)
+ *                                          frc_matmul_q5_k[_batched], frc_dequant_q5_k,
+ *                                          frc_matmul_q1_0[_batched], frc_dequant_q1_0
+ *
+ * Those stateless entry points take host buffers, as the reference does, and
+ * copy the weight to the GPU on every call.  A backend that calls the same
+ * weight many times (the forwarder: once per projection per layer per token)
+ * uploads it once with frc_weight_create and then calls frc_weight_matmul,
+ * which moves only x and y across PCIe.  frc_gemv / frc_dequant_dev are the
+ * stream-ordered device-pointer kernels underneath both.
+ *
+ * Conventions (the reference's, _C.cpp:105-120 and python/__init__.py:145-153):
+ *  - weight: raw GGUF blocks of a row-major (n, k) matrix; row i occupies
+ *    bytes [i*(k/QK)*TS, (i+1)*(k/QK)*TS); k must be a multiple of QK.
+ *  - x: fp32, (k) or (seq, k) row-major; y: fp32, (n) or (seq, n).
+ *  - y[s][i] = sum_j W[i][j] * x[s][j].
+ * Every function returns FRC_OK (0) or a nonzero FRC_ERR_*; the message is
+ * available from frc_last_error (thread-local).
+ */
+#ifndef FRCUDA_H
+#define FRCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define FRC_OK              0
+#define FRC_ERR_INVALID     1  /* bad shape / size / alignment / quant (reference: RuntimeError) */
+#define FRC_ERR_CUDA        2  /* a CUDA runtime call failed */
+#define FRC_ERR_NOMEM       3  /* device or pinned allocation failed */
+#define FRC_ERR_DEVICE      4  /* a kernel reported a fault through its status word (e.g. a bounded wait ran out) */
+#define FRC_ERR_UNSUPPORTED 5  /* valid request this build does not implement */
+
+/* quant ids: the GGML type ids of src/flatrun/backend/gguf.py:59-86 */
+#define FRC_Q8_0  8
+#define FRC_Q4_K 12
+#define FRC_Q5_K 13
+#define FRC_Q6_K 14
+#define FRC_Q1_0 41
+
+/* ---- library / diagnostics -------------------------------------------- */
+
+/* Build identifier (reference: _C.version, _C.cpp:449). */
+int frc_version(char* buf, size_t len);
+/* Always 0 (reference: _C.is_neon, _C.cpp:441); kept so facades can probe it. */
+int frc_is_neon(void);
+/* Message of the last failed call on this thread ("" if none). */
+int frc_last_error(char* buf, size_t len);
+/* Number of visible CUDA devices. */
+int frc_device_count(int* count);
+/* Elements and bytes per block of a quant (GGML type table, backend/gguf.py:59-86). */
+int frc_block_geometry(int quant, int* elems_per_block, int* bytes_per_block);
+/* Bytes of an (n, k) weight: n * (k / QK) * TS.  FRC_ERR_INVALID if k % QK != 0. */
+int frc_weight_nbytes(int quant, int64_t n, int64_t k, size_t* nbytes);
+/* Reads and clears the device status word of `device` (set by kernels whose
+ * bounded waits ran out); *flags == 0 means no fault was recorded. */
+int frc_device_status(int device, uint32_t* flags);
+
+/* ---- stream-ordered device-pointer kernels ------------------------------ *
+ * No allocation, no synchronisation: the work is enqueued on `stream`
+ * (a cudaStream_t; NULL = legacy default stream) of the current device.
+ * w_dev must be 16-byte aligned.  frc_gemv computes y_dev (batch, n) from
+ * x_dev (batch, k), 1 <= batch <= 16.                                        */
+int frc_gemv(int quant, const void* w_dev, size_t w_bytes, int64_t n, int64_t k,
+             const float* x_dev, int64_t batch, float* y_dev, void* stream);
+/* Bit-exact dequantisation of n_elems elements (ceil(n_elems/QK) blocks) into
+ * out_dev (n_elems floats), matching the reference NumPy decoders
+ * (dequant/gguf.py) bit for bit. */
+int frc_dequant_dev(int quant, const void* w_dev, size_t w_bytes, int64_t n_elems,
+                    float* out_dev, void* stream);
+
+/* ---- device-resident weights (upload once, call many times) ------------- */
+typedef struct frc_weight frc_weight;
+
+/* Copies `nbytes` of raw GGUF blocks from host memory to `device`.  The
+ * host buffer is not retained. */
+int frc_weight_create(int device, int quant, const void* host, size_t nbytes,
+                      int64_t n, int64_t k, frc_weight** out);
+int frc_weight_free(frc_weight* w);
+/* Device address and size of the uploaded blocks. */
+int frc_weight_info(const frc_weight* w, const void** dev_ptr, size_t* nbytes,
+                    int* quant, int64_t* n, int64_t* k, int* device);
+/* y_host (seq, n) = x_host (seq, k) . W^T with host buffers: copies x in,
+ * runs frc_gemv (seq <= 16) or the batched prefill path (seq > 16), copies y
+ * out and synchronises.  seq >= 1.  (Reference: matmul_*[_batched].) */
+int frc_weight_matmul(frc_weight* w, const float* x_host, int64_t seq, float* y_host);
+/* Device-pointer variant on a caller stream; no synchronisation. */
+int frc_weight_matmul_dev(frc_weight* w, const float* x_dev, int64_t seq, float* y_dev,
+                          void* stream);
+/* Dequantise the whole weight to out_host (n*k floats).  (Reference: dequant_*.) */
+int frc_weight_dequant(frc_weight* w, float* out_host);
+
+/* ---- stateless host-buffer mirrors of flatrun_native._C ----------------- *
+ * w_bytes must equal n*(k/QK)*TS (reference: "weight byte size mismatch").  */
+int frc_matmul_q4_k(const float* x, const uint8_t* w, size_t w_bytes, int64_t n, int64_t k, float* y);
+int frc_matmul_q4_k_batched(const float* x, int64_t seq, const uint8_t* w, size_t w_bytes,
+                            int64_t n, int64_t k, float* y);
+int frc_dequant_q4_k(const uint8_t* w, size_t w_bytes, int64_t out_dim, int64_t in_dim, float* out);
+int frc_matmul_q8_0(const float* x, const uint8_t* w, size_t w_bytes, int64_t n, int64_t k, float* y);
+int frc_matmul_q8_0_batched(const float* x, int64_t seq, const uint8_t* w, size_t w_bytes,
+                            int64_t n, int64_t k, float* y);
+int frc_dequant_q8_0(const uint8_t* w, size_t w_bytes, int64_t out_dim, int64_t in_dim, float* out);
+int frc_matmul_q6_k(const float* x, const uint8_t* w, size_t w_bytes, int64_t n, int64_t k, float* y);
+int frc_matmul_q6_k_batched(const float* x, int64_t seq, const uint8_t* w, size_t w_bytes,
+                            int64_t n, int64_t k, float* y);
+int frc_dequant_q6_k(const uint8_t* w, size_t w_bytes, int64_t out_dim, int64_t in_dim, float* out);
+int frc_matmul_q5_k(const float* x, const uint8_t* w, size_t w_bytes, int64_t n, int64_t k, float* y);
+int frc_matmul_q5_k_batched(const float* x, int64_t seq, const uint8_t* w, size_t w_bytes,
+                            int64_t n, int64_t k, float* y);
+int frc_dequant_q5_k(const uint8_t* w, size_t w_bytes, int64_t out_dim, int64_t in_dim, float* out);
+int frc_matmul_q1_0(const float* x, const uint8_t* w, size_t w_bytes, int64_t n, int64_t k, float* y);
+int frc_matmul_q1_0_batched(const float* x, int64_t seq, const uint8_t* w, size_t w_bytes,
+                            int64_t n, int64_t k, float* y);
+int frc_dequant_q1_0(const uint8_t* w, size_t w_bytes, int64_t out_dim, int64_t in_dim, float* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FRCUDA_H */

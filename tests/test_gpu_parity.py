@@ -1,0 +1,267 @@
+"""Parity of the CUDA path with the CPU oracle, through the C ABI (GPU).
+
+Gates (the north star's): dequantised weights bit-exact against the reference
+NumPy decoders; matvec outputs within 1e-3 of the reference fp32 path, metric
+max|y - y_ref| / max|y_ref|.  The fp32 CUDA-core kernels are held to a much
+tighter bound, TOL = 2e-5 against the fp64 product of the same dequantised
+weights, so a regression shows long before it reaches the gate.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+from flatrun_b200 import _lib, synth
+from oracle import gguf_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+FMTS = list(O.FORMATS)
+GATE = 1e-3
+TOL = 2e-5
+
+
+def _golden(fmt):
+    return np.load(os.path.join(GOLDEN, f"golden_{fmt.lower()}.npz"))
+
+
+def _rows_oracle(fmt, raw, n, k, rows, x):
+    """fp64 oracle on a subset of rows (rows are independent)."""
+    rb = synth.row_bytes(fmt, k)
+    sub = raw.reshape(n, rb)[rows].reshape(-1)
+    return O.matvec_fp64(fmt, sub, x, len(rows), k)
+
+
+# ---- gate 1: bit-exact dequant --------------------------------------------
+
+@pytest.mark.parametrize("fmt", FMTS)
+def test_dequant_bits_vs_reference_fixture(cuda_backend, fmt):
+    g = _golden(fmt)
+    n, k = int(g["n"]), int(g["k"])
+    assert O.same_bits(cuda_backend.dequant(g["syn_raw"], (n, k), fmt), g["syn_deq"])
+    qk, ts = O.FORMATS[fmt]
+    raw = g["raw_raw"]
+    out = cuda_backend.dequant(raw, (raw.size // ts * qk,), fmt)
+    assert O.same_bits(out, g["raw_deq"])
+
+
+@pytest.mark.parametrize("fmt", FMTS)
+@pytest.mark.parametrize("seed", [0, 1])
+def test_dequant_bits_random_bytes(cuda_backend, fmt, seed):
+    qk, ts = O.FORMATS[fmt]
+    nb = 4099
+    raw = synth.make_random_blocks(fmt, nb, seed=100 + seed)
+    with np.errstate(all="ignore"):
+        ref = O.DEQUANT[fmt](raw, (nb * qk,))
+    assert O.same_bits(cuda_backend.dequant(raw, (nb * qk,), fmt), ref)
+
+
+@pytest.mark.parametrize("fmt", FMTS)
+def test_dequant_bits_synthetic_weight(cuda_backend, fmt):
+    qk, _ = O.FORMATS[fmt]
+    n, k = 77, qk * 9
+    raw = synth.make_weight(fmt, n, k, seed=5)
+    dw = cuda_backend.weight(raw, n, k, fmt)
+    assert O.same_bits(dw.dequant(), O.dequant(fmt, raw, n, k))
+
+
+def test_dequant_q1_0_tail(cuda_backend):
+    raw = (np.float16(0.5).tobytes() + bytes(16)) * 2
+    out = cuda_backend.dequant(np.frombuffer(raw, np.uint8), (130,), "Q1_0")
+    np.testing.assert_array_equal(out[128:], [-0.5, -0.5])
+
+
+# ---- gate 2: matvec ---------------------------------------------------------
+
+@pytest.mark.parametrize("fmt", FMTS)
+def test_matvec_vs_reference_fixture(cuda_backend, fmt):
+    g = _golden(fmt)
+    n, k = int(g["n"]), int(g["k"])
+    m = getattr(cuda_backend, {"Q4_K": "matmul_q4k", "Q6_K": "matmul_q6k", "Q8_0": "matmul_q8_0",
+                               "Q5_K": "matmul_q5k", "Q1_0": "matmul_q1_0"}[fmt])
+    y = m(g["syn_x"], g["syn_raw"], n, k)
+    assert y.shape == (n,)
+    assert O.rel_err(y, g["syn_mv"]) < GATE
+    assert O.rel_err(y, O.matvec_fp64(fmt, g["syn_raw"], g["syn_x"], n, k)) < TOL
+    yb = m(g["syn_x2"], g["syn_raw"], n, k)
+    assert yb.shape == (3, n)
+    assert O.rel_err(yb, g["syn_mvb"]) < GATE
+
+
+def _shapes(fmt):
+    qk, _ = O.FORMATS[fmt]
+    ks = sorted({qk, 3 * qk, 3584 if qk != 128 else 3584, 4096})
+    return [(n, k) for n in (1, 7, 37, 300) for k in ks]
+
+
+@pytest.mark.parametrize("fmt", FMTS)
+@pytest.mark.parametrize("batch", [1, 2, 3, 4, 5, 8, 11, 16, 17, 35])
+def test_matvec_shapes_and_batches(cuda_backend, fmt, batch):
+    for i, (n, k) in enumerate(_shapes(fmt)):
+        raw = synth.make_weight(fmt, n, k, seed=1000 + i)
+        x = synth.make_x(k, batch=None if batch == 1 else batch, seed=2000 + i)
+        y = cuda_backend.weight(raw, n, k, fmt).matmul(x)
+        ref = O.matvec_fp64(fmt, raw, x, n, k)
+        assert y.shape == ref.shape
+        err = O.rel_err(y, ref)
+        assert err < TOL, (fmt, n, k, batch, err)
+
+
+BASELINE_SHAPES = [
+    ("Q8_0", 4096, 4096),      # config 1
+    ("Q4_K", 3584, 3584),      # q/o
+    ("Q4_K", 512, 3584),       # k/v
+    ("Q4_K", 18944, 3584),     # gate/up
+    ("Q4_K", 3584, 18944),     # down
+    ("Q5_K", 3584, 18944),     # config 3 down
+    ("Q6_K", 3584, 18944),     # down variant
+    ("Q1_0", 4096, 4096),
+]
+
+
+@pytest.mark.parametrize("fmt,n,k", BASELINE_SHAPES)
+def test_matvec_baseline_shapes_full_oracle(cuda_backend, fmt, n, k):
+    raw = synth.make_weight(fmt, n, k, seed=7)
+    x = synth.make_x(k, seed=8)
+    y = cuda_backend.weight(raw, n, k, fmt).matmul(x)
+    ref32 = O.matvec_fp32(fmt, raw, x, n, k)
+    ref64 = O.matvec_fp64(fmt, raw, x, n, k)
+    assert O.rel_err(y, ref32) < GATE
+    assert O.rel_err(y, ref64) < TOL
+    cuda_backend.close()
+
+
+@pytest.mark.parametrize("batch", [1, 4, 16])
+def test_matvec_lm_head_q6_k_sampled_rows(cuda_backend, batch):
+    """lm_head 152064 x 3584 Q6_K (447 MB): every row on the GPU, an fp64
+    oracle on 512 sampled rows, plus linearity over the whole output."""
+    fmt, n, k = "Q6_K", 152064, 3584
+    raw = synth.make_weight(fmt, n, k, seed=9)
+    x = synth.make_x(k, batch=None if batch == 1 else batch, seed=10)
+    dw = cuda_backend.weight(raw, n, k, fmt)
+    y = dw.matmul(x)
+    rows = np.sort(np.random.default_rng(0).choice(n, 512, replace=False))
+    rows[0], rows[-1] = 0, n - 1
+    ref = _rows_oracle(fmt, raw, n, k, rows, x)
+    got = y[..., rows]
+    assert O.rel_err(got, ref) < TOL
+    # linearity: W(2 x1 - 3 x2) = 2 W x1 - 3 W x2
+    x2 = synth.make_x(k, batch=None if batch == 1 else batch, seed=11)
+    lhs = dw.matmul((2.0 * x - 3.0 * x2).astype(np.float32))
+    rhs = 2.0 * y.astype(np.float64) - 3.0 * dw.matmul(x2).astype(np.float64)
+    assert O.rel_err(lhs, rhs) < 1e-4
+    cuda_backend.close()
+
+
+@pytest.mark.parametrize("fmt,n,k", [("Q5_K", 3584, 18944), ("Q4_K", 18944, 3584)])
+@pytest.mark.parametrize("batch", [4, 16])
+def test_matvec_batched_baseline_shapes(cuda_backend, fmt, n, k, batch):
+    raw = synth.make_weight(fmt, n, k, seed=12)
+    x = synth.make_x(k, batch=batch, seed=13)
+    y = cuda_backend.weight(raw, n, k, fmt).matmul(x)
+    rows = np.sort(np.random.default_rng(1).choice(n, 256, replace=False))
+    assert O.rel_err(y[:, rows], _rows_oracle(fmt, raw, n, k, rows, x)) < TOL
+    cuda_backend.close()
+
+
+def test_prefill_512_tokens_gate_shape(cuda_backend):
+    """Batched prefill: 512 tokens x 3584 through gate 18944 x 3584 Q4_K."""
+    fmt, n, k, seq = "Q4_K", 18944, 3584, 512
+    raw = synth.make_weight(fmt, n, k, seed=14)
+    x = synth.make_x(k, batch=seq, seed=15)
+    y = cuda_backend.weight(raw, n, k, fmt).matmul(x)
+    assert y.shape == (seq, n)
+    rows = np.sort(np.random.default_rng(2).choice(n, 64, replace=False))
+    toks = np.sort(np.random.default_rng(3).choice(seq, 64, replace=False))
+    ref = _rows_oracle(fmt, raw, n, k, rows, x[toks])
+    assert O.rel_err(y[np.ix_(toks, rows)], ref) < 1e-3
+    cuda_backend.close()
+
+
+# ---- device-pointer entry point ---------------------------------------------
+
+@pytest.mark.parametrize("fmt", FMTS)
+def test_frc_gemv_device_pointers(cuda_backend, fmt):
+    import torch
+    lib = _lib.load()
+    qk, _ = O.FORMATS[fmt]
+    n, k, batch = 333, qk * 12, 3
+    raw = synth.make_weight(fmt, n, k, seed=21)
+    x = synth.make_x(k, batch=batch, seed=22)
+    w_d = torch.from_numpy(raw).cuda()
+    x_d = torch.from_numpy(x).cuda()
+    y_d = torch.full((batch, n), float("nan"), device="cuda")
+    stream = torch.cuda.current_stream()
+    rc = lib.frc_gemv(_lib.QUANT_IDS[fmt], w_d.data_ptr(), raw.nbytes, n, k, x_d.data_ptr(), batch,
+                      y_d.data_ptr(), stream.cuda_stream)
+    _lib.check(rc, lib)
+    torch.cuda.synchronize()
+    assert O.rel_err(y_d.cpu().numpy(), O.matvec_fp64(fmt, raw, x, n, k)) < TOL
+
+
+def test_stateless_mirrors(cuda_backend):
+    lib = _lib.load()
+    for fmt, suffix in (("Q4_K", "q4_k"), ("Q8_0", "q8_0"), ("Q6_K", "q6_k"), ("Q5_K", "q5_k"),
+                        ("Q1_0", "q1_0")):
+        qk, _ = O.FORMATS[fmt]
+        n, k = 40, qk * 4
+        raw = synth.make_weight(fmt, n, k, seed=31)
+        x = synth.make_x(k, seed=32)
+        y = np.empty(n, np.float32)
+        _lib.check(getattr(lib, f"frc_matmul_{suffix}")(x.ctypes.data, raw.ctypes.data, raw.nbytes, n, k,
+                                                         y.ctypes.data), lib)
+        assert O.rel_err(y, O.matvec_fp64(fmt, raw, x, n, k)) < TOL
+        xb = synth.make_x(k, batch=5, seed=33)
+        yb = np.empty((5, n), np.float32)
+        _lib.check(getattr(lib, f"frc_matmul_{suffix}_batched")(xb.ctypes.data, 5, raw.ctypes.data, raw.nbytes,
+                                                                 n, k, yb.ctypes.data), lib)
+        assert O.rel_err(yb, O.matvec_fp64(fmt, raw, xb, n, k)) < TOL
+        w = np.empty((n, k), np.float32)
+        _lib.check(getattr(lib, f"frc_dequant_{suffix}")(raw.ctypes.data, raw.nbytes, n, k, w.ctypes.data), lib)
+        assert O.same_bits(w, O.dequant(fmt, raw, n, k))
+
+
+# ---- error behaviour (reference: ValueError from the facade, RuntimeError
+# from the kernels; no fallback) ----------------------------------------------
+
+def test_errors_match_reference_behaviour(cuda_backend):
+    n, k = 16, 512
+    raw = synth.make_weight("Q4_K", n, k, seed=1)
+    with pytest.raises(ValueError):
+        cuda_backend.matmul_q4k(np.zeros(k + 1, np.float32), raw, n, k)
+    with pytest.raises(ValueError):
+        cuda_backend.matmul_q6k(np.zeros((1, 1, k), np.float32), raw, n, k)
+    with pytest.raises(ValueError):
+        cuda_backend.matmul_q8_0(np.float32(1.0), raw, n, k)
+    with pytest.raises(RuntimeError, match="byte size mismatch"):
+        cuda_backend.matmul_q4k(np.zeros(k, np.float32), raw[:-1], n, k)
+    with pytest.raises(RuntimeError, match="multiple of 256"):
+        cuda_backend.matmul_q4k(np.zeros(k - 1, np.float32), raw, n, k - 1)
+
+
+def test_injected_allocation_failure(cuda_backend, monkeypatch):
+    monkeypatch.setenv("FRC_FAULT_INJECT_OOM", "1")
+    lib = _lib.load()
+    h = ctypes.c_void_p()
+    raw = synth.make_weight("Q8_0", 4, 32, seed=1)
+    rc = lib.frc_weight_create(0, 8, raw.ctypes.data, raw.nbytes, 4, 32, ctypes.byref(h))
+    assert rc == _lib.FRC_ERR_NOMEM and not h.value
+
+
+def test_zero_sized_shapes(cuda_backend):
+    x = np.zeros(256, np.float32)
+    assert cuda_backend.matmul_q4k(x, np.zeros(0, np.uint8), 0, 256).shape == (0,)
+    y = cuda_backend.matmul_q4k(np.zeros(0, np.float32), np.zeros(0, np.uint8), 5, 0)
+    np.testing.assert_array_equal(y, np.zeros(5, np.float32))
+
+
+def test_no_device_status_raised(cuda_backend):
+    lib = _lib.load()
+    flags = ctypes.c_uint32(123)
+    _lib.check(lib.frc_device_status(0, ctypes.byref(flags)), lib)
+    assert flags.value == 0
