@@ -202,8 +202,12 @@ int gemv_device(DeviceState* ds, int quant, const uint8_t* w, int64_t n, int64_t
     FRC_CUDA(cudaMemsetAsync(y, 0, sizeof(float) * n * seq, stream), "cudaMemsetAsync");
     return FRC_OK;
   }
-  for (int64_t c0 = 0; c0 < seq; c0 += kMaxGemvBatch) {
-    const int64_t cb = seq - c0 < kMaxGemvBatch ? seq - c0 : kMaxGemvBatch;
+  // balanced chunks of at most kMaxGemvBatch columns, so a multi-column call
+  // never leaves a single column for the batch-1 kernel
+  const int64_t nchunk = (seq + kMaxGemvBatch - 1) / kMaxGemvBatch;
+  const int64_t csize = (seq + nchunk - 1) / nchunk;
+  for (int64_t c0 = 0; c0 < seq; c0 += csize) {
+    const int64_t cb = seq - c0 < csize ? seq - c0 : csize;
     frc::GemvRequest r{};
     r.w = w;
     r.x = x + c0 * k;

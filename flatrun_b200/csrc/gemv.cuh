@@ -28,6 +28,7 @@
 #pragma once
 
 #include "formats.cuh"
+#include "units_dp4a.cuh"
 
 namespace frc {
 
@@ -45,6 +46,7 @@ struct GemvParams {
   int units;          // units per row
   int stage_stride;   // bytes per shared-memory stage
   int nstage;
+  int wps;            // gemv_i8: warps per slot (one slot covers one row's units)
   uint32_t* status;   // device status word
 };
 
@@ -271,6 +273,188 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1) gemv_x1(GemvP
       if (!*abort) p.y[t0 + lane] = v;
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+// batch 1, activations quantised to a 16-bit integer split, dp4a dot products
+//
+// Every warp of the CTA computes; there is no producer warp.  The warps form
+// slots of p.wps warps, and each slot is an independent pipeline: it owns a
+// contiguous share of the CTA's rows, its own ring of p.nstage shared-memory
+// stages (RPS rows each) and its own mbarriers.  Thread st of a slot owns
+// units st, st + 32 wps, ... of every row.  Per tile: wait for the stage,
+// accumulate, reduce across the slot, pass the slot's named barrier, and then
+// the slot leader refills that stage with the tile NSTAGE ahead (every thread
+// of the slot has finished reading it) while the first RPS threads write y.
+// ---------------------------------------------------------------------------
+FRC_DEVICE_INLINE void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Issue the bulk copy of weight rows [t0, t1) into `dst` (a stage), with the
+// <16-byte tail copied by this thread; completion on `bar`.
+FRC_DEVICE_INLINE void issue_tile(const GemvParams& p, uint8_t* dst, uint64_t* bar, int64_t t0, int64_t t1) {
+  const uint64_t gs = static_cast<uint64_t>(t0) * p.row_bytes;
+  const uint64_t ge = static_cast<uint64_t>(t1) * p.row_bytes;
+  const uint64_t a0 = gs & ~uint64_t(15), a1 = ge & ~uint64_t(15);
+  for (uint64_t b = a1; b < ge; ++b) dst[b - a0] = p.w[b];
+  const uint32_t bulk = static_cast<uint32_t>(a1 - a0);
+  mbar_arrive_expect_tx(bar, bulk);
+  if (bulk) bulk_g2s(dst, p.w + a0, bulk, bar);
+}
+
+// Warps per CTA at most: 16 with one unit per thread (128 registers), 12 with
+// two (their activation registers need up to 168).
+template <int UPT>
+__host__ __device__ constexpr int i8_max_warps() {
+  return UPT == 1 ? 16 : 12;
+}
+
+FRC_DEVICE_INLINE void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+FRC_DEVICE_INLINE void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+template <int Q, int UPT, int RPS>
+__global__ void __launch_bounds__(i8_max_warps<UPT>() * 32, 1) gemv_i8(GemvParams p) {
+  using F = Fmt<Q>;
+  constexpr int RW = record_words<Q>();
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = static_cast<int>(blockDim.x >> 5);
+  const int slots = nwarps / p.wps;
+  const int nst = p.nstage;
+  // layout: full[slots][nst] | abort | red[slots][2][wps][RPS] | records | stages
+  uint64_t* full_all = reinterpret_cast<uint64_t*>(smem);
+  int* abort_flag = reinterpret_cast<int*>(full_all + slots * nst);
+  float* red_all = reinterpret_cast<float*>(smem + ((slots * nst * 8 + 4 + 15) / 16) * 16);
+  const int red_bytes = slots * 2 * p.wps * RPS * 4;
+  uint32_t* records = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(red_all) + ((red_bytes + 15) / 16) * 16);
+  uint8_t* stage_all = reinterpret_cast<uint8_t*>(records + p.units * RW);
+  stage_all = smem + ((stage_all - smem + 127) / 128) * 128;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < slots * nst; ++i) mbar_init(&full_all[i], 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  const int slot = warp / p.wps;
+  const int st = threadIdx.x - slot * p.wps * 32;
+  const int spt = p.wps * 32;
+  uint64_t* full = full_all + slot * nst;
+  uint8_t* stages = stage_all + static_cast<size_t>(slot) * nst * p.stage_stride;
+  float* red = red_all + slot * 2 * p.wps * RPS;
+  volatile int* abort = abort_flag;
+
+  // rows of this slot
+  int64_t c0, c1;
+  cta_rows(p.n, c0, c1);
+  const int64_t r0 = c0 + (c1 - c0) * slot / slots;
+  const int64_t r1 = c0 + (c1 - c0) * (slot + 1) / slots;
+  const int ntiles = slot < slots ? static_cast<int>((r1 - r0 + RPS - 1) / RPS) : 0;
+
+  // The weights are never written by another kernel: start streaming them
+  // before waiting for the previous kernel in the stream (programmatic
+  // dependent launch), which may still be producing x.
+  int issued = 0;  // tiles handed to the copy engine (leader only)
+  if (st == 0 && ntiles > 0) {
+    for (int i = 0; i < nst && i < ntiles; ++i, ++issued) {
+      const int64_t t0 = r0 + static_cast<int64_t>(i) * RPS;
+      issue_tile(p, stages + static_cast<size_t>(i) * p.stage_stride, &full[i], t0,
+                 t0 + RPS < r1 ? t0 + RPS : r1);
+    }
+  }
+  griddep_wait();
+  griddep_launch_dependents();
+
+  quantise_units<Q, I8<Q>::UPB, F::QK>(p.x, p.units, records);
+  __syncthreads();
+  if (ntiles == 0) return;  // the whole slot leaves together
+
+  UnitX<Q> xu[UPT];
+  UnitCtx cx[UPT];
+  int uoff[UPT];
+  bool uval[UPT];
+#pragma unroll
+  for (int i = 0; i < UPT; ++i) {
+    const int u = st + i * spt;
+    uval[i] = u < p.units;
+    const int b = uval[i] ? u / I8<Q>::UPB : 0;
+    const int j = uval[i] ? u % I8<Q>::UPB : 0;
+    cx[i] = make_ctx<Q>(j);
+    uoff[i] = b * F::TS;
+    if (uval[i]) {
+      xu[i].from_record(records + u * RW);
+    } else {
+      xu[i].zero();
+    }
+  }
+
+  const int wis = warp - slot * p.wps;  // warp index inside the slot
+  for (int it = 0; it < ntiles; ++it) {
+    const int s = it % nst;
+    const uint32_t ph = static_cast<uint32_t>(it / nst) & 1u;
+    const int64_t t0 = r0 + static_cast<int64_t>(it) * RPS;
+    const int rows = static_cast<int>((t0 + RPS < r1 ? t0 + RPS : r1) - t0);
+    float acc[RPS];
+#pragma unroll
+    for (int r = 0; r < RPS; ++r) acc[r] = 0.f;
+    if (wait_phase(&full[s], ph, abort)) {
+      const uint8_t* base = stages + static_cast<size_t>(s) * p.stage_stride +
+                            ((static_cast<uint64_t>(t0) * p.row_bytes) & 15u);
+#pragma unroll
+      for (int r = 0; r < RPS; ++r) {
+        if (r < rows) {
+          const uint8_t* row = base + r * p.row_bytes;
+#pragma unroll
+          for (int i = 0; i < UPT; ++i) {
+            if (uval[i]) acc[r] += UnitDotI8<Q>::dot(row + uoff[i], cx[i], xu[i]);
+          }
+        }
+      }
+    } else if (st == 0) {
+      atomicOr(p.status, kStatusFullWaitTimeout);
+    }
+
+    butterfly<RPS>(acc, lane);
+    float* rb = red + (it & 1) * p.wps * RPS;
+    constexpr int kLanesPerValue = 32 / RPS;
+    if ((lane & (kLanesPerValue - 1)) == 0) rb[wis * RPS + lane / kLanesPerValue] = acc[0];
+    if (p.wps == 1) {
+      __syncwarp();
+    } else {
+      named_barrier_sync(1 + slot, spt);
+    }
+    if (st == 0 && it + nst < ntiles && !*abort) {
+      const int64_t n0 = t0 + static_cast<int64_t>(nst) * RPS;
+      fence_proxy_async_smem();
+      issue_tile(p, stages + static_cast<size_t>(s) * p.stage_stride, &full[s], n0, n0 + RPS < r1 ? n0 + RPS : r1);
+      ++issued;
+    }
+    if (st < rows) {
+      float v = 0.f;
+      for (int w = 0; w < p.wps; ++w) v += rb[w * RPS + st];
+      if (!*abort) p.y[t0 + st] = v;
+    }
+  }
+
+  // on an abort, copies already issued must land before the CTA exits
+  if (st == 0 && *abort) {
+    const int first = issued > nst ? issued - nst : 0;
+    int zero = 0;
+    for (int i = first; i < issued; ++i) {
+      if (!wait_phase(&full[i % nst], static_cast<uint32_t>(i / nst) & 1u, &zero)) {
+        atomicOr(p.status, kStatusDrainTimeout);
+      }
+    }
+  }
+}
+
+// Bytes before the stages: barriers, reduction buffers, activation records.
+template <int Q, int RPS>
+__host__ __device__ constexpr int i8_smem_header(int slots, int nst, int wps, int units) {
+  return (((slots * nst * 8 + 4 + 15) / 16) * 16 + ((slots * 2 * wps * RPS * 4 + 15) / 16) * 16 +
+          units * record_words<Q>() * 4 + 127) / 128 * 128;
 }
 
 // ---------------------------------------------------------------------------

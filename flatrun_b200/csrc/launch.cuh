@@ -47,6 +47,9 @@ inline int env_int(const char* name, int def) {
 inline cudaError_t kernel_occupancy(const void* kernel, int device, int threads, size_t smem, int* blocks) {
   static std::mutex mu;
   static std::map<std::tuple<const void*, int, int, size_t>, int> cache;
+  // the opt-in is a per-(kernel, device) cap: only ever raise it, or a later
+  // smaller request would invalidate a cached larger configuration
+  static std::map<std::pair<const void*, int>, size_t> optin;
   std::lock_guard<std::mutex> lock(mu);
   const auto key = std::make_tuple(kernel, device, threads, smem);
   auto it = cache.find(key);
@@ -54,8 +57,13 @@ inline cudaError_t kernel_occupancy(const void* kernel, int device, int threads,
     *blocks = it->second;
     return cudaSuccess;
   }
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
+  size_t& cap = optin[std::make_pair(kernel, device)];
+  if (smem > cap) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    cap = smem;
+  }
+  cudaError_t e;
   int nb = 0;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kernel, threads, smem);
   if (e != cudaSuccess) return e;
@@ -149,6 +157,66 @@ inline cudaError_t launch_xb(GemvParams p, const GemvRequest& r) {
   }
 }
 
+// Batch-1 integer-dot kernel: slots of `wps` warps each cover one row's units
+// and run independent pipelines; up to 16 warps per CTA.
+template <int Q, int UPT, int RPS>
+inline cudaError_t launch_i8_rps(GemvParams p, const GemvRequest& r, int slots) {
+  p.stage_stride = round_up(RPS * p.row_bytes + 32, 128);
+  const int header = i8_smem_header<Q, RPS>(slots, 8, p.wps, p.units);
+  const int budget = env_int("FRC_SMEM_BYTES", 220 * 1024) - header;
+  int nst = budget / (slots * p.stage_stride);
+  nst = nst < 2 ? 2 : (nst > 8 ? 8 : nst);
+  const int forced = env_int("FRC_NSTAGE", 0);
+  if (forced > 0) nst = forced;
+  p.nstage = nst;
+  const size_t smem =
+      i8_smem_header<Q, RPS>(slots, nst, p.wps, p.units) + static_cast<size_t>(slots) * nst * p.stage_stride;
+  const int threads = slots * p.wps * 32;
+  const void* fn = reinterpret_cast<const void*>(gemv_i8<Q, UPT, RPS>);
+  int per_sm = 0;
+  cudaError_t e = kernel_occupancy(fn, r.device, threads, smem, &per_sm);
+  if (e != cudaSuccess) return e;
+  int64_t grid = static_cast<int64_t>(per_sm) * r.sms;
+  const int64_t useful = (p.n + slots - 1) / slots;
+  if (grid > useful) grid = useful;
+  if (grid < 1) grid = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = r.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = env_int("FRC_PDL", 1) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemv_i8<Q, UPT, RPS>, p);
+}
+
+template <int Q, int UPT>
+inline cudaError_t launch_i8(GemvParams p, const GemvRequest& r) {
+  const int spt = 32 * UPT;
+  p.wps = (p.units + spt - 1) / spt;
+  constexpr int kMaxW = i8_max_warps<UPT>();
+  const int warps = env_int("FRC_NWARPS", kMaxW);
+  int slots = warps / p.wps;
+  if (slots < 1) slots = 1;
+  if (slots * p.wps > kMaxW) slots = kMaxW / p.wps;
+  // rows per slot per tile: the largest power of two whose tile stays within
+  // the target (a long row gets one row per tile)
+  const int tile_target = env_int("FRC_TILE_BYTES", 8 * 1024);
+  int rps = 1;
+  while (rps < 8 && 2 * rps * p.row_bytes <= tile_target) rps *= 2;
+  const int forced = env_int("FRC_RPS", 0);
+  if (forced == 1 || forced == 2 || forced == 4 || forced == 8) rps = forced;
+  switch (rps) {
+    case 1: return launch_i8_rps<Q, UPT, 1>(p, r, slots);
+    case 2: return launch_i8_rps<Q, UPT, 2>(p, r, slots);
+    case 4: return launch_i8_rps<Q, UPT, 4>(p, r, slots);
+    default: return launch_i8_rps<Q, UPT, 8>(p, r, slots);
+  }
+}
+
 // Largest tile footprint must fit in shared memory with two stages.
 template <int Q>
 inline bool tiles_fit(int row_bytes) {
@@ -171,6 +239,15 @@ cudaError_t launch_gemv(const GemvRequest& r) {
   if (!tiles_fit<Q>(p.row_bytes)) return cudaErrorInvalidValue;
   constexpr int E = 16 * F::NRUN;
   const bool force_xb = env_int("FRC_FORCE_XB", 0) != 0;
+  if (r.batch == 1 && !force_xb && env_int("FRC_GEMV_FP32", 0) == 0) {
+    const int units = (r.k / F::QK) * I8<Q>::UPB;
+    p.units = units;
+    const int upt = env_int("FRC_UPT", 0);
+    // one unit per thread while a slot has at most 8 warps, then two
+    if ((upt == 1 || (upt == 0 && units <= 256)) && units <= 512) return launch_i8<Q, 1>(p, r);
+    if (units <= 64 * i8_max_warps<2>()) return launch_i8<Q, 2>(p, r);
+    p.units = (r.k / F::QK) * F::UPB;
+  }
   if (r.batch == 1 && !force_xb) {
     const int cap1 = 32 * kMaxConsumerWarps;
     if (p.units <= cap1) return launch_x1<Q, 1>(p, r, (p.units + 31) / 32);

@@ -179,6 +179,21 @@ def rel_err(y, y_ref) -> float:
     return float(np.max(np.abs(y - y_ref))) / denom
 
 
+def term_scale(fmt: str, raw, x: np.ndarray, n: int, k: int) -> float:
+    """max over rows of sum_j |w_ij x_j|: the magnitude of the terms a row
+    sums, a denominator that stays meaningful when outputs cancel (few rows)."""
+    w = np.abs(dequant(fmt, raw, n, k).astype(np.float64))
+    xa = np.abs(np.asarray(x, dtype=np.float64))
+    s = w @ xa if xa.ndim == 1 else xa @ w.T
+    return float(np.max(s)) if s.size else 0.0
+
+
+def norm_err(y, y_ref, scale: float) -> float:
+    """max|y - y_ref| / scale (see term_scale)."""
+    d = np.max(np.abs(np.asarray(y, np.float64) - np.asarray(y_ref, np.float64))) if np.size(y_ref) else 0.0
+    return float(d / scale) if scale > 0 else float(d)
+
+
 def same_bits(a: np.ndarray, b: np.ndarray) -> bool:
     """Bit-for-bit float32 equality, with every NaN treated as equal."""
     a = np.asarray(a, dtype=np.float32)

@@ -2,9 +2,17 @@
 
 Gates (the north star's): dequantised weights bit-exact against the reference
 NumPy decoders; matvec outputs within 1e-3 of the reference fp32 path, metric
-max|y - y_ref| / max|y_ref|.  The fp32 CUDA-core kernels are held to a much
-tighter bound, TOL = 2e-5 against the fp64 product of the same dequantised
-weights, so a regression shows long before it reaches the gate.
+max|y - y_ref| / max|y_ref|.  The kernels are held to much tighter bounds
+against the fp64 product of the same dequantised weights, so a regression shows
+long before it reaches the gate:
+
+* TOL = 2e-5 for the fp32 CUDA-core kernels (batch > 1, and batch 1 with
+  FRC_GEMV_FP32=1);
+* TOL_I8 = 1e-4 for the default batch-1 kernel, whose activations are
+  quantised to a 16-bit integer grid per 64 (or 32) elements before the
+  dp4a dot products (measured 2e-5 .. 4e-5 on the benchmark shapes; the
+  reference's own native C++ kernel is 3.9e-4 from fp64 on the Q4_K down
+  shape).
 """
 
 from __future__ import annotations
@@ -24,6 +32,11 @@ GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 FMTS = list(O.FORMATS)
 GATE = 1e-3
 TOL = 2e-5
+TOL_I8 = 1e-4
+
+
+def _tol(batch):
+    return TOL_I8 if batch == 1 else TOL
 
 
 def _golden(fmt):
@@ -87,7 +100,7 @@ def test_matvec_vs_reference_fixture(cuda_backend, fmt):
     y = m(g["syn_x"], g["syn_raw"], n, k)
     assert y.shape == (n,)
     assert O.rel_err(y, g["syn_mv"]) < GATE
-    assert O.rel_err(y, O.matvec_fp64(fmt, g["syn_raw"], g["syn_x"], n, k)) < TOL
+    assert O.rel_err(y, O.matvec_fp64(fmt, g["syn_raw"], g["syn_x"], n, k)) < TOL_I8
     yb = m(g["syn_x2"], g["syn_raw"], n, k)
     assert yb.shape == (3, n)
     assert O.rel_err(yb, g["syn_mvb"]) < GATE
@@ -102,14 +115,18 @@ def _shapes(fmt):
 @pytest.mark.parametrize("fmt", FMTS)
 @pytest.mark.parametrize("batch", [1, 2, 3, 4, 5, 8, 11, 16, 17, 35])
 def test_matvec_shapes_and_batches(cuda_backend, fmt, batch):
+    """Edge shapes (1 row, 1 block, rows not a multiple of any tile).  With
+    so few rows max|y_ref| can be a cancelled sum, so the error is normalised
+    by the term magnitude max_i sum_j |w_ij x_j| (worst case for the 16-bit
+    activation grid: 0.5/32767 x max/mean |x| ~ 5e-5)."""
     for i, (n, k) in enumerate(_shapes(fmt)):
         raw = synth.make_weight(fmt, n, k, seed=1000 + i)
         x = synth.make_x(k, batch=None if batch == 1 else batch, seed=2000 + i)
         y = cuda_backend.weight(raw, n, k, fmt).matmul(x)
         ref = O.matvec_fp64(fmt, raw, x, n, k)
         assert y.shape == ref.shape
-        err = O.rel_err(y, ref)
-        assert err < TOL, (fmt, n, k, batch, err)
+        err = O.norm_err(y, ref, O.term_scale(fmt, raw, x, n, k))
+        assert err < (5e-5 if batch == 1 else 2e-6), (fmt, n, k, batch, err)
 
 
 BASELINE_SHAPES = [
@@ -132,7 +149,7 @@ def test_matvec_baseline_shapes_full_oracle(cuda_backend, fmt, n, k):
     ref32 = O.matvec_fp32(fmt, raw, x, n, k)
     ref64 = O.matvec_fp64(fmt, raw, x, n, k)
     assert O.rel_err(y, ref32) < GATE
-    assert O.rel_err(y, ref64) < TOL
+    assert O.rel_err(y, ref64) < TOL_I8
     cuda_backend.close()
 
 
@@ -149,12 +166,12 @@ def test_matvec_lm_head_q6_k_sampled_rows(cuda_backend, batch):
     rows[0], rows[-1] = 0, n - 1
     ref = _rows_oracle(fmt, raw, n, k, rows, x)
     got = y[..., rows]
-    assert O.rel_err(got, ref) < TOL
+    assert O.rel_err(got, ref) < _tol(batch)
     # linearity: W(2 x1 - 3 x2) = 2 W x1 - 3 W x2
     x2 = synth.make_x(k, batch=None if batch == 1 else batch, seed=11)
     lhs = dw.matmul((2.0 * x - 3.0 * x2).astype(np.float32))
     rhs = 2.0 * y.astype(np.float64) - 3.0 * dw.matmul(x2).astype(np.float64)
-    assert O.rel_err(lhs, rhs) < 1e-4
+    assert O.rel_err(lhs, rhs) < 3 * _tol(batch)
     cuda_backend.close()
 
 
@@ -180,6 +197,38 @@ def test_prefill_512_tokens_gate_shape(cuda_backend):
     toks = np.sort(np.random.default_rng(3).choice(seq, 64, replace=False))
     ref = _rows_oracle(fmt, raw, n, k, rows, x[toks])
     assert O.rel_err(y[np.ix_(toks, rows)], ref) < 1e-3
+    cuda_backend.close()
+
+
+@pytest.mark.parametrize("fmt", FMTS)
+def test_batch1_exact_fp32_kernel(cuda_backend, fmt, monkeypatch):
+    """FRC_GEMV_FP32=1 selects the batch-1 kernel that keeps activations in
+    fp32 (no integer grid): held to the fp32 tolerance."""
+    monkeypatch.setenv("FRC_GEMV_FP32", "1")
+    qk, _ = O.FORMATS[fmt]
+    for i, (n, k) in enumerate([(300, qk * 14), (1000, 3584 if qk != 32 else 4096), (37, 18944)]):
+        if k % qk:
+            continue
+        raw = synth.make_weight(fmt, n, k, seed=400 + i)
+        x = synth.make_x(k, seed=500 + i)
+        y = cuda_backend.weight(raw, n, k, fmt).matmul(x)
+        assert O.rel_err(y, O.matvec_fp64(fmt, raw, x, n, k)) < TOL, (fmt, n, k)
+    cuda_backend.close()
+
+
+@pytest.mark.parametrize("fmt", FMTS)
+def test_batch1_activation_outliers(cuda_backend, fmt):
+    """Activations with 50x outliers and an all-zero unit still meet the
+    1e-3 gate on the integer-grid kernel."""
+    qk, _ = O.FORMATS[fmt]
+    n, k = 512, qk * 32
+    raw = synth.make_weight(fmt, n, k, seed=41)
+    x = synth.make_x(k, seed=42)
+    x[::97] *= 50.0
+    x[:qk] = 0.0
+    y = cuda_backend.weight(raw, n, k, fmt).matmul(x)
+    assert O.rel_err(y, O.matvec_fp32(fmt, raw, x, n, k)) < GATE
+    assert O.rel_err(y, O.matvec_fp64(fmt, raw, x, n, k)) < 3 * TOL_I8
     cuda_backend.close()
 
 
@@ -215,7 +264,7 @@ def test_stateless_mirrors(cuda_backend):
         y = np.empty(n, np.float32)
         _lib.check(getattr(lib, f"frc_matmul_{suffix}")(x.ctypes.data, raw.ctypes.data, raw.nbytes, n, k,
                                                          y.ctypes.data), lib)
-        assert O.rel_err(y, O.matvec_fp64(fmt, raw, x, n, k)) < TOL
+        assert O.rel_err(y, O.matvec_fp64(fmt, raw, x, n, k)) < TOL_I8
         xb = synth.make_x(k, batch=5, seed=33)
         yb = np.empty((5, n), np.float32)
         _lib.check(getattr(lib, f"frc_matmul_{suffix}_batched")(xb.ctypes.data, 5, raw.ctypes.data, raw.nbytes,
