@@ -83,8 +83,16 @@ WORKLOADS = {
 }
 
 
-def algorithmic_bytes(mats, batch: int) -> int:
-    return sum(synth.weight_bytes(q, n, k) + batch * (k + n) * 4 for _, q, n, k, _ in mats)
+def algorithmic_bytes(mats, batch: int, fused: bool = True) -> int:
+    """Weights + activations read + outputs written; projections sharing an
+    x (same group tag) read it once when they are fused."""
+    total, seen = 0, set()
+    for _, q, n, k, g in mats:
+        total += synth.weight_bytes(q, n, k) + batch * n * 4
+        if not fused or (g, k) not in seen:
+            total += batch * k * 4
+            seen.add((g, k))
+    return total
 
 
 def peaks() -> tuple[float, str]:
@@ -222,6 +230,8 @@ def main() -> None:
     ap.add_argument("--copies", type=int, default=0, help="distinct weight copies rotated (0 = auto, > 3x L2)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--unfused", action="store_true",
+                    help="one launch per projection, each with its own x (no shared-x fusion)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -231,7 +241,7 @@ def main() -> None:
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     wl = WORKLOADS[args.workload]
     mats, batch = wl["mats"], wl["batch"]
-    step_bytes = algorithmic_bytes(mats, batch)
+    step_bytes = algorithmic_bytes(mats, batch, fused=not getattr(args, "unfused", False))
 
     if args.impl == "reference":
         if rank != 0:
@@ -314,6 +324,21 @@ def main() -> None:
     qid = [_lib.QUANT_IDS[q] for _, q, _, _, _ in mats]
     mbytes = [synth.weight_bytes(q, n, k) for _, q, n, k, _ in mats]
 
+    # launch groups: projections that share x run as one fused launch
+    # (frc_gemv_multi), the forwarder's dataflow (q/k/v, gate/up)
+    lgroups = []
+    for i, m in enumerate(mats):
+        if not args.unfused and lgroups and mats[lgroups[-1][0]][4] == m[4] and mats[lgroups[-1][0]][1] == m[1] \
+                and mats[lgroups[-1][0]][3] == m[3] and len(lgroups[-1]) < 4:
+            lgroups[-1].append(i)
+        else:
+            lgroups.append([i])
+    # the members of a group read the same x
+    for g in lgroups:
+        for i in g[1:]:
+            xs_dev[i] = xs_dev[g[0]]
+            xs_host[i] = xs_host[g[0]]
+
     # all-gather groups (N > 1)
     groups = []
     if world > 1:
@@ -338,11 +363,26 @@ def main() -> None:
         if rc:
             _lib.check(rc, lib)
 
+    def gemv_group(g: list, step: int) -> None:
+        if len(g) == 1:
+            gemv(g[0], step)
+            return
+        cnt = len(g)
+        wp = (ctypes.c_void_p * cnt)(*[pools[i][0].data_ptr() + (step % pools[i][2]) * pools[i][1] for i in g])
+        wb = (ctypes.c_size_t * cnt)(*[mbytes[i] for i in g])
+        nn = (ctypes.c_int64 * cnt)(*[mats[i][2] for i in g])
+        yp = (ctypes.c_void_p * cnt)(*[ys_dev[i].data_ptr() for i in g])
+        rc = lib.frc_gemv_multi(qid[g[0]], cnt, wp, wb, nn, mats[g[0]][3], xs_dev[g[0]].data_ptr(), batch, yp,
+                                ctypes.c_void_p(stream.cuda_stream))
+        if rc:
+            _lib.check(rc, lib)
+
     def launch(step: int, only=None) -> None:
-        for i in range(len(mats)):
-            if only is not None and i not in only:
+        for g in lgroups:
+            if only is not None and g[0] not in only:
                 continue
-            gemv(i, step)
+            gemv_group(g, step)
+            i = g[-1]
             for last, sendbuf, recvbuf, idx in groups:
                 if only is None and last == i:
                     off = 0
@@ -404,25 +444,20 @@ def main() -> None:
     ms_step = elapsed_ms / K
     value = step_bytes * world / (ms_step / 1e3) / 1e9
 
-    # per-projection launch time: K back-to-back launches of one projection
-    # (rotating its copies), one graph replay bracketed by CUDA events
+    # per-launch time: K back-to-back launches of one group (a fused launch
+    # or a single projection), one graph replay bracketed by CUDA events
     per = {}
-    for i, (name, q, n, k, _) in enumerate(mats):
-        gi = capture(only={i})
+    for g in lgroups:
+        name = "+".join(mats[i][0] for i in g)
+        gi = capture(only={g[0]})
         replay_ms(gi)
         us = replay_ms(gi) * 1e3 / K
-        b = mbytes[i] + batch * (k + n) * 4
+        b = sum(mbytes[i] + batch * (mats[i][3] + mats[i][2]) * 4 for i in g) - (len(g) - 1) * batch * mats[g[0]][3] * 4
         per[name] = {"us": round(us, 3), "gbs": round(b / (us / 1e6) / 1e9, 1), "bytes": b}
         del gi
-    # dominant kernel: the launches sharing the first projection's k (one
-    # kernel instantiation), timed together the same way
-    dom = [i for i, m in enumerate(mats) if m[3] == mats[0][3]]
-    gd = capture(only=set(dom))
-    replay_ms(gd)
-    dom_ms = replay_ms(gd)
-    del gd
-    dom_bytes = sum(mbytes[i] + batch * (mats[i][3] + mats[i][2]) * 4 for i in dom)
-    achieved = dom_bytes * K / (dom_ms / 1e3) / 1e9
+    # dominant kernel: the launch carrying the most bytes
+    dom_name = max(per, key=lambda nm: per[nm]["bytes"])
+    achieved = per[dom_name]["bytes"] / (per[dom_name]["us"] / 1e6) / 1e9
     peak, peak_src = peaks()
     traffic = ncu_traffic(args.workload)
 
@@ -475,16 +510,17 @@ def main() -> None:
             "frac_of_8tbs": round(value / world / 8000.0, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": f"gemv_x1 <{mats[dom[0]][1]}> over the k={mats[dom[0]][3]} projections "
-                                   f"({'+'.join(mats[i][0] for i in dom)})",
-                         "timing": "K back-to-back launches of the dominant kernel's projections, one CUDA graph "
-                                   "replay bracketed by CUDA events on the launching stream",
+                         "kernel": f"gemv_i8 <{mats[0][1]}> launch '{dom_name}' "
+                                   f"({per[dom_name]['bytes'] / 1e6:.1f} MB per launch)",
+                         "timing": "K back-to-back launches of the dominant launch, one CUDA graph replay bracketed "
+                                   "by CUDA events on the launching stream",
                          "peak_source": peak_src},
-            "per_projection": per,
+            "per_launch": per,
+            "launches_per_step": len(lgroups),
             "cpu_baseline": cpu,
             "e2e": e2e,
             "clocks": clk,
-            "gpu_launches": K * len(mats),
+            "gpu_launches": K * len(lgroups),
         }
         print(json.dumps(out), flush=True)
 

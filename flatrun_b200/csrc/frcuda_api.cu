@@ -418,6 +418,53 @@ int frc_gemv(int quant, const void* w_dev, size_t w_bytes, int64_t n, int64_t k,
                      static_cast<cudaStream_t>(stream));
 }
 
+int frc_gemv_multi(int quant, int count, const void* const* w_dev, const size_t* w_bytes, const int64_t* n,
+                   int64_t k, const float* x_dev, int64_t batch, float* const* y_dev, void* stream) {
+  if (count < 1 || count > 4) return fail(FRC_ERR_INVALID, "frc_gemv_multi: count must be 1..4 (got %d)", count);
+  if (!w_dev || !w_bytes || !n || !y_dev) return fail(FRC_ERR_INVALID, "null array");
+  if (batch < 1 || batch > kMaxGemvBatch) return fail(FRC_ERR_INVALID, "frc_gemv_multi: batch must be 1..%d", kMaxGemvBatch);
+  for (int m = 0; m < count; ++m) {
+    int rc = check_matmul(quant, w_bytes[m], n[m], k, batch);
+    if (rc) return rc;
+    if ((w_bytes[m] && !w_dev[m]) || (batch * n[m] && !y_dev[m])) return fail(FRC_ERR_INVALID, "null buffer");
+    if (!aligned(w_dev[m], 16)) return fail(FRC_ERR_INVALID, "frc_gemv_multi: weight %d must be 16-byte aligned", m);
+    if (!aligned(y_dev[m], 4)) return fail(FRC_ERR_INVALID, "frc_gemv_multi: y %d must be 4-byte aligned", m);
+  }
+  if ((batch * k && !x_dev) || !aligned(x_dev, 16)) return fail(FRC_ERR_INVALID, "frc_gemv_multi: x must be 16-byte aligned");
+  DeviceState* ds;
+  int rc = current_device_state(&ds);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int64_t total = 0;
+  for (int m = 0; m < count; ++m) total += n[m];
+  if (batch == 1 && count > 1 && k > 0 && total > 0) {
+    frc::GemvRequest r{};
+    r.k = static_cast<int>(k);
+    r.x = x_dev;
+    r.batch = 1;
+    r.status = ds->status;
+    r.stream = st;
+    r.device = ds->device;
+    r.sms = ds->sms;
+    r.nmat = count;
+    for (int m = 0; m < count; ++m) {
+      r.mat_w[m] = static_cast<const uint8_t*>(w_dev[m]);
+      r.mat_y[m] = y_dev[m];
+      r.mat_n[m] = n[m];
+    }
+    r.n = total;
+    rc = launch_gemv_quant(quant, r);
+    if (rc == FRC_OK) return FRC_OK;
+    g_err.clear();  // not fusable with this shape: one launch per matrix
+    (void)cudaGetLastError();
+  }
+  for (int m = 0; m < count; ++m) {
+    rc = gemv_device(ds, quant, static_cast<const uint8_t*>(w_dev[m]), n[m], k, x_dev, batch, y_dev[m], st);
+    if (rc) return rc;
+  }
+  return FRC_OK;
+}
+
 int frc_dequant_dev(int quant, const void* w_dev, size_t w_bytes, int64_t n_elems, float* out_dev, void* stream) {
   int rc = check_dequant(quant, w_bytes, n_elems, false);
   if (rc) return rc;

@@ -48,7 +48,15 @@ struct GemvParams {
   int nstage;
   int wps;            // gemv_i8: warps per slot (one slot covers one row's units)
   uint32_t* status;   // device status word
+  // gemv_i8 row space: nmat matrices sharing x and k, rows concatenated;
+  // matrix m covers rows [mat_end[m-1], mat_end[m]) of the n rows
+  int nmat;
+  int64_t mat_end[4];
+  const uint8_t* mat_w[4];  // each 16-byte aligned
+  float* mat_y[4];
 };
+
+constexpr int kMaxMats = 4;
 
 FRC_DEVICE_INLINE uint64_t global_ns() {
   uint64_t t;
@@ -291,30 +299,64 @@ FRC_DEVICE_INLINE void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// Issue the bulk copy of weight rows [t0, t1) into `dst` (a stage), with the
-// <16-byte tail copied by this thread; completion on `bar`.
-FRC_DEVICE_INLINE void issue_tile(const GemvParams& p, uint8_t* dst, uint64_t* bar, int64_t t0, int64_t t1) {
-  const uint64_t gs = static_cast<uint64_t>(t0) * p.row_bytes;
-  const uint64_t ge = static_cast<uint64_t>(t1) * p.row_bytes;
+// Issue the bulk copy of rows [l0, l1) of the matrix at `w` into `dst` (a
+// stage), with the <16-byte tail copied by this thread; completion on `bar`.
+FRC_DEVICE_INLINE void issue_tile(const GemvParams& p, const uint8_t* w, uint8_t* dst, uint64_t* bar, int64_t l0,
+                                  int64_t l1) {
+  const uint64_t gs = static_cast<uint64_t>(l0) * p.row_bytes;
+  const uint64_t ge = static_cast<uint64_t>(l1) * p.row_bytes;
   const uint64_t a0 = gs & ~uint64_t(15), a1 = ge & ~uint64_t(15);
-  for (uint64_t b = a1; b < ge; ++b) dst[b - a0] = p.w[b];
+  for (uint64_t b = a1; b < ge; ++b) dst[b - a0] = w[b];
   const uint32_t bulk = static_cast<uint32_t>(a1 - a0);
   mbar_arrive_expect_tx(bar, bulk);
-  if (bulk) bulk_g2s(dst, p.w + a0, bulk, bar);
+  if (bulk) bulk_g2s(dst, w + a0, bulk, bar);
 }
 
-// Warps per CTA at most: 16 with one unit per thread (128 registers), 12 with
-// two (their activation registers need up to 168).
-template <int UPT>
+// A tile of at most `rps` rows starting at global row t0, clipped to the end of
+// its matrix and to r1.
+struct Tile {
+  int64_t t1;     // global end row
+  int64_t local;  // first row inside matrix m
+  int m;
+};
+
+FRC_DEVICE_INLINE Tile tile_at(const GemvParams& p, int64_t t0, int64_t r1, int rps) {
+  int m = 0;
+  while (m + 1 < p.nmat && t0 >= p.mat_end[m]) ++m;
+  const int64_t start = m ? p.mat_end[m - 1] : 0;
+  int64_t end = p.mat_end[m] < r1 ? p.mat_end[m] : r1;
+  Tile t;
+  t.t1 = t0 + rps < end ? t0 + rps : end;
+  t.local = t0 - start;
+  t.m = m;
+  return t;
+}
+
+FRC_DEVICE_INLINE int count_tiles(const GemvParams& p, int64_t r0, int64_t r1, int rps) {
+  int n = 0;
+  int64_t start = 0;
+  for (int m = 0; m < p.nmat; ++m) {
+    const int64_t a = r0 > start ? r0 : start;
+    const int64_t b = r1 < p.mat_end[m] ? r1 : p.mat_end[m];
+    if (b > a) n += static_cast<int>((b - a + rps - 1) / rps);
+    start = p.mat_end[m];
+  }
+  return n;
+}
+
+// Warps per CTA at most, from the activation registers a thread holds (UPT
+// records of 2 E/4 + NG + 1 words): 16 warps (128 registers each) up to 72
+// activation registers, 12 warps (168 registers) beyond.
+template <int Q, int UPT>
 __host__ __device__ constexpr int i8_max_warps() {
-  return UPT == 1 ? 16 : 12;
+  return UPT * (2 * I8<Q>::E / 4 + I8<Q>::NG + 1) <= 72 ? 16 : 12;
 }
 
 FRC_DEVICE_INLINE void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 FRC_DEVICE_INLINE void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 template <int Q, int UPT, int RPS>
-__global__ void __launch_bounds__(i8_max_warps<UPT>() * 32, 1) gemv_i8(GemvParams p) {
+__global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvParams p) {
   using F = Fmt<Q>;
   constexpr int RW = record_words<Q>();
   extern __shared__ __align__(128) uint8_t smem[];
@@ -351,23 +393,31 @@ __global__ void __launch_bounds__(i8_max_warps<UPT>() * 32, 1) gemv_i8(GemvParam
   cta_rows(p.n, c0, c1);
   const int64_t r0 = c0 + (c1 - c0) * slot / slots;
   const int64_t r1 = c0 + (c1 - c0) * (slot + 1) / slots;
-  const int ntiles = slot < slots ? static_cast<int>((r1 - r0 + RPS - 1) / RPS) : 0;
+  const int ntiles = slot < slots ? count_tiles(p, r0, r1, RPS) : 0;
 
   // The weights are never written by another kernel: start streaming them
   // before waiting for the previous kernel in the stream (programmatic
   // dependent launch), which may still be producing x.
   int issued = 0;  // tiles handed to the copy engine (leader only)
-  if (st == 0 && ntiles > 0) {
+  const int leader = p.wps == 1 ? 0 : spt - 32;  // lane 0 of the slot's last warp
+  int64_t next_issue = r0;  // leader's cursor over the slot's tiles
+  if (st == leader && ntiles > 0) {
     for (int i = 0; i < nst && i < ntiles; ++i, ++issued) {
-      const int64_t t0 = r0 + static_cast<int64_t>(i) * RPS;
-      issue_tile(p, stages + static_cast<size_t>(i) * p.stage_stride, &full[i], t0,
-                 t0 + RPS < r1 ? t0 + RPS : r1);
+      const Tile t = tile_at(p, next_issue, r1, RPS);
+      issue_tile(p, p.mat_w[t.m], stages + static_cast<size_t>(i) * p.stage_stride, &full[i], t.local,
+                 t.local + (t.t1 - next_issue));
+      next_issue = t.t1;
     }
   }
   griddep_wait();
   griddep_launch_dependents();
 
-  quantise_units<Q, I8<Q>::UPB, F::QK>(p.x, p.units, records);
+  {
+    constexpr int NQ = I8<Q>::E / 16;
+    int P = NQ;
+    while (P > 1 && p.units * P > static_cast<int>(blockDim.x)) P >>= 1;
+    quantise_units<Q, I8<Q>::UPB, F::QK>(p.x, p.units, records, P);
+  }
   __syncthreads();
   if (ntiles == 0) return;  // the whole slot leaves together
 
@@ -391,24 +441,39 @@ __global__ void __launch_bounds__(i8_max_warps<UPT>() * 32, 1) gemv_i8(GemvParam
   }
 
   const int wis = warp - slot * p.wps;  // warp index inside the slot
+  int64_t t0 = r0;  // consumers' cursor
   for (int it = 0; it < ntiles; ++it) {
     const int s = it % nst;
     const uint32_t ph = static_cast<uint32_t>(it / nst) & 1u;
-    const int64_t t0 = r0 + static_cast<int64_t>(it) * RPS;
-    const int rows = static_cast<int>((t0 + RPS < r1 ? t0 + RPS : r1) - t0);
+    const Tile tile = tile_at(p, t0, r1, RPS);
+    const int rows = static_cast<int>(tile.t1 - t0);
+    float* ym = p.mat_y[tile.m] + tile.local;
     float acc[RPS];
 #pragma unroll
     for (int r = 0; r < RPS; ++r) acc[r] = 0.f;
     if (wait_phase(&full[s], ph, abort)) {
       const uint8_t* base = stages + static_cast<size_t>(s) * p.stage_stride +
-                            ((static_cast<uint64_t>(t0) * p.row_bytes) & 15u);
+                            ((static_cast<uint64_t>(tile.local) * p.row_bytes) & 15u);
+      if (rows == RPS) {
+        // full tile: no per-row guard, so the rows' independent instruction
+        // streams can be interleaved
 #pragma unroll
-      for (int r = 0; r < RPS; ++r) {
-        if (r < rows) {
-          const uint8_t* row = base + r * p.row_bytes;
+        for (int i = 0; i < UPT; ++i) {
+          if (uval[i]) {
 #pragma unroll
-          for (int i = 0; i < UPT; ++i) {
-            if (uval[i]) acc[r] += UnitDotI8<Q>::dot(row + uoff[i], cx[i], xu[i]);
+            for (int r = 0; r < RPS; ++r)
+              acc[r] += UnitDotI8<Q>::dot(base + r * p.row_bytes + uoff[i], cx[i], xu[i]);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < RPS; ++r) {
+          if (r < rows) {
+            const uint8_t* row = base + r * p.row_bytes;
+#pragma unroll
+            for (int i = 0; i < UPT; ++i) {
+              if (uval[i]) acc[r] += UnitDotI8<Q>::dot(row + uoff[i], cx[i], xu[i]);
+            }
           }
         }
       }
@@ -417,29 +482,42 @@ __global__ void __launch_bounds__(i8_max_warps<UPT>() * 32, 1) gemv_i8(GemvParam
     }
 
     butterfly<RPS>(acc, lane);
-    float* rb = red + (it & 1) * p.wps * RPS;
     constexpr int kLanesPerValue = 32 / RPS;
-    if ((lane & (kLanesPerValue - 1)) == 0) rb[wis * RPS + lane / kLanesPerValue] = acc[0];
+    const bool refill = st == leader && it + nst < ntiles && !*abort;
     if (p.wps == 1) {
-      __syncwarp();
+      // one warp owns the row: lane l holds row l / kLanesPerValue
+      __syncwarp();  // every lane has finished reading stage s
     } else {
+      float* rb = red + (it & 1) * p.wps * RPS;
+      if ((lane & (kLanesPerValue - 1)) == 0) rb[wis * RPS + lane / kLanesPerValue] = acc[0];
       named_barrier_sync(1 + slot, spt);
+      if (st < rows) {
+        float v = 0.f;
+        for (int w = 0; w < p.wps; ++w) v += rb[w * RPS + st];
+        acc[0] = v;
+      }
     }
-    if (st == 0 && it + nst < ntiles && !*abort) {
-      const int64_t n0 = t0 + static_cast<int64_t>(nst) * RPS;
+    if (refill) {
+      // the stage is free: every thread of the slot has passed the barrier
+      const Tile nt = tile_at(p, next_issue, r1, RPS);
       fence_proxy_async_smem();
-      issue_tile(p, stages + static_cast<size_t>(s) * p.stage_stride, &full[s], n0, n0 + RPS < r1 ? n0 + RPS : r1);
+      issue_tile(p, p.mat_w[nt.m], stages + static_cast<size_t>(s) * p.stage_stride, &full[s], nt.local,
+                 nt.local + (nt.t1 - next_issue));
+      next_issue = nt.t1;
       ++issued;
     }
-    if (st < rows) {
-      float v = 0.f;
-      for (int w = 0; w < p.wps; ++w) v += rb[w * RPS + st];
-      if (!*abort) p.y[t0 + st] = v;
+    if (p.wps == 1) {
+      if ((lane & (kLanesPerValue - 1)) == 0 && lane / kLanesPerValue < rows && !*abort) {
+        ym[lane / kLanesPerValue] = acc[0];
+      }
+    } else if (st < rows && !*abort) {
+      ym[st] = acc[0];
     }
+    t0 = tile.t1;
   }
 
   // on an abort, copies already issued must land before the CTA exits
-  if (st == 0 && *abort) {
+  if (st == leader && *abort) {
     const int first = issued > nst ? issued - nst : 0;
     int zero = 0;
     for (int i = first; i < issued; ++i) {

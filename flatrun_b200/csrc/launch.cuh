@@ -25,6 +25,12 @@ struct GemvRequest {
   cudaStream_t stream;
   int device;
   int sms;
+  // batch-1 fused launch over several matrices sharing x (nmat > 1): rows
+  // are concatenated; w, y, n then describe nothing and these arrays are used
+  int nmat;
+  const uint8_t* mat_w[4];
+  float* mat_y[4];
+  int64_t mat_n[4];
 };
 
 struct DequantRequest {
@@ -160,14 +166,8 @@ inline cudaError_t launch_xb(GemvParams p, const GemvRequest& r) {
 // Batch-1 integer-dot kernel: slots of `wps` warps each cover one row's units
 // and run independent pipelines; up to 16 warps per CTA.
 template <int Q, int UPT, int RPS>
-inline cudaError_t launch_i8_rps(GemvParams p, const GemvRequest& r, int slots) {
+inline cudaError_t launch_i8_rps(GemvParams p, const GemvRequest& r, int slots, int nst) {
   p.stage_stride = round_up(RPS * p.row_bytes + 32, 128);
-  const int header = i8_smem_header<Q, RPS>(slots, 8, p.wps, p.units);
-  const int budget = env_int("FRC_SMEM_BYTES", 220 * 1024) - header;
-  int nst = budget / (slots * p.stage_stride);
-  nst = nst < 2 ? 2 : (nst > 8 ? 8 : nst);
-  const int forced = env_int("FRC_NSTAGE", 0);
-  if (forced > 0) nst = forced;
   p.nstage = nst;
   const size_t smem =
       i8_smem_header<Q, RPS>(slots, nst, p.wps, p.units) + static_cast<size_t>(slots) * nst * p.stage_stride;
@@ -193,28 +193,53 @@ inline cudaError_t launch_i8_rps(GemvParams p, const GemvRequest& r, int slots) 
   return cudaLaunchKernelEx(&cfg, gemv_i8<Q, UPT, RPS>, p);
 }
 
+// Shared memory available to one block (B200: 227 KB opt-in).
+constexpr int kSmemBudget = 227 * 1024;
+
+// Choose slots (independent pipelines of wps warps), rows per tile and stages
+// so the block fits in shared memory: prefer the requested tile size and as
+// many warps as the register budget allows, then shrink tiles, then warps.
 template <int Q, int UPT>
 inline cudaError_t launch_i8(GemvParams p, const GemvRequest& r) {
   const int spt = 32 * UPT;
   p.wps = (p.units + spt - 1) / spt;
-  constexpr int kMaxW = i8_max_warps<UPT>();
+  constexpr int kMaxW = i8_max_warps<Q, UPT>();
   const int warps = env_int("FRC_NWARPS", kMaxW);
   int slots = warps / p.wps;
   if (slots < 1) slots = 1;
   if (slots * p.wps > kMaxW) slots = kMaxW / p.wps;
-  // rows per slot per tile: the largest power of two whose tile stays within
-  // the target (a long row gets one row per tile)
-  const int tile_target = env_int("FRC_TILE_BYTES", 8 * 1024);
+  // ~8 KB tiles for short rows; long rows (k > ~14K for Q4_K) do better
+  // with two-row tiles up to 32 KB
+  const int tile_target = env_int("FRC_TILE_BYTES", p.row_bytes > 8192 ? 32 * 1024 : 8 * 1024);
   int rps = 1;
   while (rps < 8 && 2 * rps * p.row_bytes <= tile_target) rps *= 2;
   const int forced = env_int("FRC_RPS", 0);
   if (forced == 1 || forced == 2 || forced == 4 || forced == 8) rps = forced;
-  switch (rps) {
-    case 1: return launch_i8_rps<Q, UPT, 1>(p, r, slots);
-    case 2: return launch_i8_rps<Q, UPT, 2>(p, r, slots);
-    case 4: return launch_i8_rps<Q, UPT, 4>(p, r, slots);
-    default: return launch_i8_rps<Q, UPT, 8>(p, r, slots);
+  const int budget = env_int("FRC_SMEM_BYTES", kSmemBudget);
+  const int want_nst = env_int("FRC_NSTAGE", 0);
+  for (; slots >= 1; --slots) {
+    for (int rr = rps; rr >= 1; rr /= 2) {
+      const int stride = round_up(rr * p.row_bytes + 32, 128);
+      int header = 0;
+      switch (rr) {
+        case 1: header = i8_smem_header<Q, 1>(slots, 8, p.wps, p.units); break;
+        case 2: header = i8_smem_header<Q, 2>(slots, 8, p.wps, p.units); break;
+        case 4: header = i8_smem_header<Q, 4>(slots, 8, p.wps, p.units); break;
+        default: header = i8_smem_header<Q, 8>(slots, 8, p.wps, p.units); break;
+      }
+      int nst = (budget - header) / (slots * stride);
+      if (nst > 8) nst = 8;
+      if (want_nst > 0 && want_nst < nst) nst = want_nst;
+      if (nst < 2) continue;
+      switch (rr) {
+        case 1: return launch_i8_rps<Q, UPT, 1>(p, r, slots, nst);
+        case 2: return launch_i8_rps<Q, UPT, 2>(p, r, slots, nst);
+        case 4: return launch_i8_rps<Q, UPT, 4>(p, r, slots, nst);
+        default: return launch_i8_rps<Q, UPT, 8>(p, r, slots, nst);
+      }
+    }
   }
+  return cudaErrorInvalidValue;
 }
 
 // Largest tile footprint must fit in shared memory with two stages.
@@ -236,18 +261,48 @@ cudaError_t launch_gemv(const GemvRequest& r) {
   p.row_bytes = (r.k / F::QK) * F::TS;
   p.units = (r.k / F::QK) * F::UPB;
   p.status = r.status;
+  if (r.nmat > 1) {
+    p.nmat = r.nmat;
+    int64_t end = 0;
+    for (int m = 0; m < r.nmat; ++m) {
+      end += r.mat_n[m];
+      p.mat_end[m] = end;
+      p.mat_w[m] = r.mat_w[m];
+      p.mat_y[m] = r.mat_y[m];
+    }
+    p.n = end;
+  } else {
+    p.nmat = 1;
+    p.mat_end[0] = r.n;
+    p.mat_w[0] = r.w;
+    p.mat_y[0] = r.y;
+  }
   if (!tiles_fit<Q>(p.row_bytes)) return cudaErrorInvalidValue;
   constexpr int E = 16 * F::NRUN;
   const bool force_xb = env_int("FRC_FORCE_XB", 0) != 0;
   if (r.batch == 1 && !force_xb && env_int("FRC_GEMV_FP32", 0) == 0) {
     const int units = (r.k / F::QK) * I8<Q>::UPB;
     p.units = units;
-    const int upt = env_int("FRC_UPT", 0);
-    // one unit per thread while a slot has at most 8 warps, then two
-    if ((upt == 1 || (upt == 0 && units <= 256)) && units <= 512) return launch_i8<Q, 1>(p, r);
-    if (units <= 64 * i8_max_warps<2>()) return launch_i8<Q, 2>(p, r);
+    // Units per thread (measured on B200, batch 1): 32-element units (Q8_0,
+    // Q1_0) use one warp per row with up to 4 units per thread; Q6_K rows of
+    // up to 64 units use one warp per row with 2; Q4_K/Q5_K rows of up to 64
+    // units use 1 unit per thread in two-warp slots; longer rows use 2 units
+    // per thread in multi-warp slots.
+    int upt = env_int("FRC_UPT", 0);
+    if (upt == 0) {
+      if (I8<Q>::E == 32) upt = units <= 128 ? 4 : 2;
+      else if (units <= 64) upt = Q == kQ6_K ? 2 : 1;
+      else upt = 2;
+    }
+    if constexpr (I8<Q>::E == 32) {
+      if (upt == 4 && units <= 128) return launch_i8<Q, 4>(p, r);
+    }
+    if (upt >= 2 && units <= 64 * i8_max_warps<Q, 2>()) return launch_i8<Q, 2>(p, r);
+    if (units <= 32 * i8_max_warps<Q, 1>()) return launch_i8<Q, 1>(p, r);
+    if (units <= 64 * i8_max_warps<Q, 2>()) return launch_i8<Q, 2>(p, r);
     p.units = (r.k / F::QK) * F::UPB;
   }
+  if (r.nmat > 1) return cudaErrorNotSupported;  // callers fall back to one launch per matrix
   if (r.batch == 1 && !force_xb) {
     const int cap1 = 32 * kMaxConsumerWarps;
     if (p.units <= cap1) return launch_x1<Q, 1>(p, r, (p.units + 31) / 32);

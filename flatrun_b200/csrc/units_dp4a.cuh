@@ -103,65 +103,108 @@ struct UnitX {
   }
 };
 
-// Quantise the activations of every unit of a row into shared records, four
-// (or two) threads per unit, 16 elements each; all threads of the block call
-// this the same number of times (it uses full-warp shuffles).
+// Quantise the activations of every unit of a row into shared records.  P
+// threads share a unit (P = 1, 2 or 4 for 64-element units; 1 or 2 for 32),
+// each taking E / P consecutive elements in x-word order: more threads per
+// unit shorten the serial path when units are few, one thread per unit keeps
+// every load of a long row in flight at once.  Every thread of the block calls
+// this with the same arguments (it uses full-warp shuffles).
 template <int Q, int UPB, int QK>
-FRC_DEVICE_INLINE void quantise_units(const float* x, int units, uint32_t* records) {
-  constexpr int E = I8<Q>::E, P = E / 16, NW = E / 4, NG = I8<Q>::NG, RW = record_words<Q>();
+FRC_DEVICE_INLINE void quantise_units(const float* x, int units, uint32_t* records, int P) {
+  constexpr int E = I8<Q>::E, NQ = E / 16, NW = E / 4, NG = I8<Q>::NG, RW = record_words<Q>();
+  const int per = NQ / P;  // 16-element quarters per thread
   const int total = units * P;
   for (int base = 0; base < total; base += blockDim.x) {
     const int t = base + static_cast<int>(threadIdx.x);
     const bool active = t < total;
-    const int u = active ? t / P : 0, qi = t % P;
+    const int u = active ? t / P : 0, part = t % P;
     const int b = u / UPB, j = u % UPB;
-    float v[16];
-    if (active) {
-      const float4* s4 = reinterpret_cast<const float4*>(x + static_cast<int64_t>(b) * QK + i8_pos<Q>(j, 16 * qi));
+    float v[NQ][16];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 tt = __ldg(s4 + q);
-        v[4 * q] = tt.x; v[4 * q + 1] = tt.y; v[4 * q + 2] = tt.z; v[4 * q + 3] = tt.w;
+    for (int qq = 0; qq < NQ; ++qq) {
+      const int quarter = part * per + qq;
+      if (active && qq < per) {
+        const float4* s4 = reinterpret_cast<const float4*>(x + static_cast<int64_t>(b) * QK + i8_pos<Q>(j, 16 * quarter));
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 tt = __ldg(s4 + q);
+          v[qq][4 * q] = tt.x; v[qq][4 * q + 1] = tt.y; v[qq][4 * q + 2] = tt.z; v[qq][4 * q + 3] = tt.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[qq][i] = 0.f;
+      }
+    }
+    // tree-shaped max over the thread's quarters (short dependency chain)
+    float m16[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) m16[i] = fabsf(v[0][i]);
+#pragma unroll
+    for (int qq = 1; qq < NQ; ++qq) {
+      if (qq < per) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) m16[i] = fmaxf(m16[i], fabsf(v[qq][i]));
+      }
+    }
+#pragma unroll
+    for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+      for (int i = 0; i < w; ++i) m16[i] = fmaxf(m16[i], m16[i + w]);
+    float amax = m16[0];
+    if (P >= 2) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    if (P >= 4) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float inv = amax > 0.f ? static_cast<float>(kXqMax) / amax : 0.0f;
+    uint32_t* rec = records + u * RW;
+    int qsum[NQ];
+#pragma unroll
+    for (int qq = 0; qq < NQ; ++qq) {
+      qsum[qq] = 0;
+      if (qq >= per) continue;  // uniform: every thread has the same `per`
+      const int quarter = part * per + qq;
+      uint32_t hw[4], lw[4];
+      int psum = 0;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        uint32_t h = 0, l = 0;
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb) {
+          int q = __float2int_rn(v[qq][4 * w + bb] * inv);
+          q = q > kXqMax ? kXqMax : (q < -kXqMax ? -kXqMax : q);
+          psum += q;
+          const int qh = (q + 128) >> 8;  // xq = 256 qh + ql, ql in [-128, 127]
+          const int ql = q - 256 * qh;
+          h |= (static_cast<uint32_t>(qh) & 0xFFu) << (8 * bb);
+          l |= (static_cast<uint32_t>(ql) & 0xFFu) << (8 * bb);
+        }
+        hw[w] = h;
+        lw[w] = l;
+      }
+      qsum[qq] = psum;
+      if (active) {
+        *reinterpret_cast<uint4*>(rec + 4 * quarter) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(rec + NW + 4 * quarter) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      }
+    }
+    // scale-group sums: a group spans QPG quarters; a thread holds `per`
+    // consecutive quarters, so it owns whole groups (per >= QPG) or a group is
+    // split over QPG / per neighbouring lanes (summed by shuffles)
+    constexpr int QPG = NQ / NG;
+    if (per >= QPG) {
+#pragma unroll
+      for (int qq = 0; qq < NQ; qq += QPG) {
+        if (active && qq < per) {
+          int g = 0;
+#pragma unroll
+          for (int i = 0; i < QPG; ++i) g += qsum[qq + i];
+          rec[2 * NW + (part * per + qq) / QPG] = static_cast<uint32_t>(g);
+        }
       }
     } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = 0.f;
+      int g = qsum[0];
+      for (int o = 1; o < QPG / per; o <<= 1) g += __shfl_xor_sync(0xffffffffu, g, o);
+      if (active && (part * per) % QPG == 0) rec[2 * NW + (part * per) / QPG] = static_cast<uint32_t>(g);
     }
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-    for (int o = 1; o < P; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float inv = amax > 0.f ? static_cast<float>(kXqMax) / amax : 0.0f;
-    uint32_t hw[4], lw[4];
-    int psum = 0;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      uint32_t h = 0, l = 0;
-#pragma unroll
-      for (int bb = 0; bb < 4; ++bb) {
-        int q = __float2int_rn(v[4 * w + bb] * inv);
-        q = q > kXqMax ? kXqMax : (q < -kXqMax ? -kXqMax : q);
-        psum += q;
-        const int qh = (q + 128) >> 8;  // xq = 256 qh + ql, ql in [-128, 127]
-        const int ql = q - 256 * qh;
-        h |= (static_cast<uint32_t>(qh) & 0xFFu) << (8 * bb);
-        l |= (static_cast<uint32_t>(ql) & 0xFFu) << (8 * bb);
-      }
-      hw[w] = h;
-      lw[w] = l;
-    }
-    // sums over scale groups of P / NG quarters
-    constexpr int QPG = P / NG;
-#pragma unroll
-    for (int o = 1; o < QPG; o <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
-    if (active) {
-      uint32_t* rec = records + u * RW;
-      *reinterpret_cast<uint4*>(rec + 4 * qi) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      *reinterpret_cast<uint4*>(rec + NW + 4 * qi) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-      if (qi % QPG == 0) rec[2 * NW + qi / QPG] = static_cast<uint32_t>(psum);
-      if (qi == 0) rec[2 * NW + NG] = __float_as_uint(amax > 0.f ? amax / static_cast<float>(kXqMax) : 1.0f);
-    }
+    if (active && part == 0) rec[2 * NW + NG] = __float_as_uint(amax > 0.f ? amax / static_cast<float>(kXqMax) : 1.0f);
   }
 }
 
@@ -220,18 +263,23 @@ template <> struct UnitDotI8<kQ4_K> {
     const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * c.j);
     const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * c.j);
     const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    int lh = 0, ll = 0, hh = 0, hl = 0;
+    // two accumulator chains per sum for instruction-level parallelism; the
+    // high nibbles stay in place (16 * nibble, unsigned) and the factor 16 is
+    // shifted out of the exact integer sum
+    int lh0 = 0, ll0 = 0, hh0 = 0, hl0 = 0, lh1 = 0, ll1 = 0, hh1 = 0, hl1 = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t lo = q[i] & 0x0F0F0F0Fu;
-      const uint32_t hi = (q[i] >> 4) & 0x0F0F0F0Fu;
-      lh = dp4a_ss(lo, x.xh[i], lh);
-      ll = dp4a_ss(lo, x.xl[i], ll);
-      hh = dp4a_ss(hi, x.xh[8 + i], hh);
-      hl = dp4a_ss(hi, x.xl[8 + i], hl);
+    for (int i = 0; i < 8; i += 2) {
+      lh0 = dp4a_ss(q[i] & 0x0F0F0F0Fu, x.xh[i], lh0);
+      ll0 = dp4a_ss(q[i] & 0x0F0F0F0Fu, x.xl[i], ll0);
+      hh0 = dp4a_us(q[i] & 0xF0F0F0F0u, x.xh[8 + i], hh0);
+      hl0 = dp4a_us(q[i] & 0xF0F0F0F0u, x.xl[8 + i], hl0);
+      lh1 = dp4a_ss(q[i + 1] & 0x0F0F0F0Fu, x.xh[i + 1], lh1);
+      ll1 = dp4a_ss(q[i + 1] & 0x0F0F0F0Fu, x.xl[i + 1], ll1);
+      hh1 = dp4a_us(q[i + 1] & 0xF0F0F0F0u, x.xh[9 + i], hh1);
+      hl1 = dp4a_us(q[i + 1] & 0xF0F0F0F0u, x.xl[9 + i], hl1);
     }
-    const int t0 = lh * 256 + ll;
-    const int t1 = hh * 256 + hl;
+    const int t0 = (lh0 + lh1) * 256 + (ll0 + ll1);
+    const int t1 = ((hh0 + hh1) * 256 + (hl0 + hl1)) >> 4;  // exact: a multiple of 16
     uint32_t sc, mn;
     k_scales(c, hdr.y, hdr.z, hdr.w, sc, mn);
     const int u = static_cast<int>(sc & 0xFFFFu) * t0 + static_cast<int>(sc >> 16) * t1;

@@ -89,6 +89,14 @@ int frc_device_status(int device, uint32_t* flags);
  * x_dev (batch, k), 1 <= batch <= 16.                                        */
 int frc_gemv(int quant, const void* w_dev, size_t w_bytes, int64_t n, int64_t k,
              const float* x_dev, int64_t batch, float* y_dev, void* stream);
+/* One launch for up to 4 weights of the same quant and k that share x
+ * (q/k/v, or gate/up, of a layer): y_dev[m] (batch, n[m]) = x . W_m^T.  At
+ * batch 1 the rows of all matrices form one row space of a single kernel
+ * launch; otherwise, or when the shape does not allow it, one launch per
+ * matrix.  Same alignment rules as frc_gemv.  (No reference counterpart: the
+ * reference dispatches one projection per call, flatrun/model/qwen2.py:1510-1519.) */
+int frc_gemv_multi(int quant, int count, const void* const* w_dev, const size_t* w_bytes, const int64_t* n,
+                   int64_t k, const float* x_dev, int64_t batch, float* const* y_dev, void* stream);
 /* Bit-exact dequantisation of n_elems elements (ceil(n_elems/QK) blocks) into
  * out_dev (n_elems floats), matching the reference NumPy decoders
  * (dequant/gguf.py) bit for bit. */

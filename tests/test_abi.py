@@ -81,6 +81,18 @@ def test_gemv_rejects_misaligned_and_oversized(lib):
     assert lib.frc_gemv(7, 16, 144, 1, 256, 16, 1, 16, None) == _lib.FRC_ERR_INVALID
 
 
+def test_gemv_multi_argument_checks(lib):
+    two = (ctypes.c_void_p * 2)(16, 32)
+    sizes = (ctypes.c_size_t * 2)(144, 144)
+    ns = (ctypes.c_int64 * 2)(1, 1)
+    ys = (ctypes.c_void_p * 2)(16, 32)
+    assert lib.frc_gemv_multi(12, 5, two, sizes, ns, 256, 16, 1, ys, None) == _lib.FRC_ERR_INVALID
+    assert "count" in _lib.last_error(lib)
+    bad = (ctypes.c_size_t * 2)(144, 143)
+    assert lib.frc_gemv_multi(12, 2, two, bad, ns, 256, 16, 1, ys, None) == _lib.FRC_ERR_INVALID
+    assert "mismatch" in _lib.last_error(lib)
+
+
 def test_q1_0_dequant_accepts_numpy_tail_rule(lib):
     """Q1_0 follows the NumPy rule (ceil blocks, tail dropped, gguf.py:266-299):
     130 elements need 2 blocks; a 1-block buffer is a size mismatch."""

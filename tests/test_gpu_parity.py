@@ -253,6 +253,39 @@ def test_frc_gemv_device_pointers(cuda_backend, fmt):
     assert O.rel_err(y_d.cpu().numpy(), O.matvec_fp64(fmt, raw, x, n, k)) < TOL
 
 
+@pytest.mark.parametrize("fmt,ns,k", [("Q4_K", (3584, 512, 512), 3584), ("Q4_K", (18944, 18944), 3584),
+                                      ("Q6_K", (512, 7, 1000), 3584), ("Q8_0", (4096, 33), 4096),
+                                      ("Q5_K", (100, 3584), 18944), ("Q1_0", (5, 6, 7, 8), 512)])
+@pytest.mark.parametrize("batch", [1, 3])
+def test_frc_gemv_multi_fused(cuda_backend, fmt, ns, k, batch):
+    """One launch over several matrices sharing x (the q/k/v and gate/up
+    dataflow) equals one launch per matrix, and the oracle."""
+    import torch
+    lib = _lib.load()
+    raws = [synth.make_weight(fmt, n, k, seed=60 + i) for i, n in enumerate(ns)]
+    x = synth.make_x(k, batch=None if batch == 1 else batch, seed=70)
+    w_d = [torch.from_numpy(r).cuda() for r in raws]
+    x_d = torch.from_numpy(x).cuda()
+    y_f = [torch.full((batch, n), float("nan"), device="cuda") for n in ns]
+    y_s = [torch.full((batch, n), float("nan"), device="cuda") for n in ns]
+    c = len(ns)
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = lib.frc_gemv_multi(_lib.QUANT_IDS[fmt], c, (ctypes.c_void_p * c)(*[t.data_ptr() for t in w_d]),
+                            (ctypes.c_size_t * c)(*[r.nbytes for r in raws]), (ctypes.c_int64 * c)(*ns), k,
+                            x_d.data_ptr(), batch, (ctypes.c_void_p * c)(*[t.data_ptr() for t in y_f]), stream)
+    _lib.check(rc, lib)
+    for i, n in enumerate(ns):
+        _lib.check(lib.frc_gemv(_lib.QUANT_IDS[fmt], w_d[i].data_ptr(), raws[i].nbytes, n, k, x_d.data_ptr(), batch,
+                                y_s[i].data_ptr(), stream), lib)
+    torch.cuda.synchronize()
+    for i, n in enumerate(ns):
+        yf, ys = y_f[i].cpu().numpy(), y_s[i].cpu().numpy()
+        ref = O.matvec_fp64(fmt, raws[i], x, n, k)
+        scale = O.term_scale(fmt, raws[i], x, n, k)
+        assert O.norm_err(yf, ref.reshape(yf.shape), scale) < (5e-5 if batch == 1 else 2e-6), (i, n)
+        np.testing.assert_allclose(yf, ys, rtol=0, atol=1e-6 * scale)
+
+
 def test_stateless_mirrors(cuda_backend):
     lib = _lib.load()
     for fmt, suffix in (("Q4_K", "q4_k"), ("Q8_0", "q8_0"), ("Q6_K", "q6_k"), ("Q5_K", "q5_k"),
