@@ -16,6 +16,7 @@ enum : uint32_t {
   kStatusFullWaitTimeout  = 1u << 0,  // a consumer gave up waiting for a tile
   kStatusEmptyWaitTimeout = 1u << 1,  // the producer gave up waiting for a free stage
   kStatusDrainTimeout     = 1u << 2,  // the producer gave up draining its copies
+  kStatusSmemMisaligned   = 1u << 3,  // dynamic shared memory not 128-byte aligned (kernel skipped)
 };
 
 // Upper bound on polls of one mbarrier phase.  Each poll is a try_wait with

@@ -118,6 +118,13 @@ struct DeviceState {
   size_t cap_x = 0;
   float* scratch_y = nullptr;
   size_t cap_y = 0;
+  // activation records of the batched tensor-core kernel: grown on demand and
+  // never freed while the process runs, so work already queued (or captured
+  // in a graph) keeps a valid pointer after a larger call replaces it
+  std::mutex rec_mu;
+  uint8_t* scratch_rec = nullptr;
+  size_t cap_rec = 0;
+  std::vector<void*> retired;
 };
 
 std::mutex g_dev_mu;
@@ -180,6 +187,22 @@ int ensure(T** buf, size_t* cap, size_t bytes, const char* what) {
   return FRC_OK;
 }
 
+// Activation-record scratch of at least `bytes` on ds's device (current).
+int record_scratch(DeviceState* ds, size_t bytes, uint8_t** out) {
+  std::lock_guard<std::mutex> lock(ds->rec_mu);
+  if (bytes > ds->cap_rec) {
+    size_t want = ds->cap_rec ? 2 * ds->cap_rec : (size_t(2) << 20);
+    while (want < bytes) want *= 2;
+    void* p = nullptr;
+    FRC_CUDA(cudaMalloc(&p, want), "cudaMalloc(activation records)");
+    if (ds->scratch_rec) ds->retired.push_back(ds->scratch_rec);
+    ds->scratch_rec = static_cast<uint8_t*>(p);
+    ds->cap_rec = want;
+  }
+  *out = ds->scratch_rec;
+  return FRC_OK;
+}
+
 int launch_gemv_quant(int quant, const frc::GemvRequest& r) {
   cudaError_t e;
   switch (quant) {
@@ -219,6 +242,10 @@ int gemv_device(DeviceState* ds, int quant, const uint8_t* w, int64_t n, int64_t
     r.stream = stream;
     r.device = ds->device;
     r.sms = ds->sms;
+    if (cb > 1) {
+      const int rc = record_scratch(ds, static_cast<size_t>(frc::mma_scratch_bytes(k, static_cast<int>(cb))), &r.xrec);
+      if (rc != FRC_OK) return rc;
+    }
     const int rc = launch_gemv_quant(quant, r);
     if (rc != FRC_OK) return rc;
   }

@@ -2,15 +2,19 @@
 // shared-memory opt-in and occupancy, cached per (device, kernel).
 #pragma once
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
 #include <cstdlib>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <tuple>
 
 #include "gemv.cuh"
+#include "gemv_mma.cuh"
 
 namespace frc {
 
@@ -31,6 +35,10 @@ struct GemvRequest {
   const uint8_t* mat_w[4];
   float* mat_y[4];
   int64_t mat_n[4];
+  // batch 2..16: activation records of the tensor-core kernel (at least
+  // mma_scratch_bytes(k, batch) bytes, 256-byte aligned); null selects the
+  // fp32 CUDA-core kernel
+  uint8_t* xrec;
 };
 
 struct DequantRequest {
@@ -242,6 +250,158 @@ inline cudaError_t launch_i8(GemvParams p, const GemvRequest& r) {
   return cudaErrorInvalidValue;
 }
 
+// Bytes of activation records the tensor-core batched kernel needs.
+inline int64_t mma_scratch_bytes(int64_t k, int batch) {
+  const int ng = batch <= 4 ? 1 : (batch <= 8 ? 2 : 4);
+  return (k + kMmaKC - 1) / kMmaKC * 4 * ng * kMmaColBytes;
+}
+
+// Launch with programmatic dependent launch allowed (FRC_PDL=0 turns it off).
+template <typename... P, typename... A>
+inline cudaError_t launch_pdl(void (*kernel)(P...), unsigned grid, unsigned threads, size_t smem, cudaStream_t st,
+                              A... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = env_int("FRC_PDL", 1) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// cuTensorMapEncodeTiled from the driver, looked up once.
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
+
+// Tile geometry of the batched kernel for rows of `row_bytes` and full chunks
+// of `chunk_bytes`: G = rows per tensor row (G * row_bytes % 16 == 0) and box
+// width W (covers a chunk from its 16-byte-aligned start, and an odd multiple
+// of 16 bytes so eight consecutive box rows start in distinct bank groups).
+inline void mma_geometry(int row_bytes, int chunk_bytes, int* G, int* W) {
+  int g = 1;
+  while ((g * row_bytes) % 16 != 0) g *= 2;
+  int mis = 0;
+  for (int a = 0; a < 16; ++a)
+    for (int c = 0; c < 16; ++c) {
+      const int m = (a * row_bytes + c * chunk_bytes) & 15;
+      mis = m > mis ? m : mis;
+    }
+  int w = round_up(chunk_bytes + mis, 16);
+  if ((w / 16) % 2 == 0) w += 16;
+  *G = g;
+  *W = w;
+}
+
+// Tensor-core batched kernel: pre-pass over x, then persistent CTAs of one
+// producer and eight consumer warps over row blocks of 16 MT rows.
+template <int Q, int NG, int MT>
+inline cudaError_t launch_mma_cfg(MmaParams p, const GemvRequest& r, int grid) {
+  constexpr int RM = 16 * MT;
+  if (RM % (8 * p.G) != 0) return cudaErrorInvalidValue;
+  p.R = RM / p.G;
+  p.logG = 0;
+  while ((1 << p.logG) < p.G) ++p.logG;
+  p.logR = 0;
+  while ((1 << p.logR) < p.R) ++p.logR;
+  p.JS = round_up(p.R * p.W, 128);
+  p.n_full = r.n / p.G * p.G;
+  p.WT = round_up(p.chunk_bytes + 32, 16);
+  p.tail_off = p.G * p.JS;
+  p.x_off = round_up(p.tail_off + (p.G - 1) * p.WT, 128);
+  const int xbytes = 4 * NG * kMmaColBytes;
+  p.stage_stride = round_up(p.x_off + xbytes, 128);
+  constexpr int header = mma_header_bytes<Q, NG, MT>();
+  const int budget = env_int("FRC_SMEM_BYTES", kSmemBudget);
+  int nst = (budget - header) / p.stage_stride;
+  if (nst > 6) nst = 6;
+  const int want = env_int("FRC_NSTAGE", 0);
+  if (want > 0 && want < nst) nst = want;
+  if (nst < 2) return cudaErrorInvalidValue;
+  p.nstage = nst;
+  const size_t smem = header + static_cast<size_t>(nst) * p.stage_stride;
+  const int threads = (kMmaWarps + 1) * 32;
+  int per_sm = 0;
+  cudaError_t e = kernel_occupancy(reinterpret_cast<const void*>(gemv_mma<Q, NG, MT>), r.device, threads, smem,
+                                   &per_sm);
+  if (e != cudaSuccess) return e;
+  CUtensorMap map;
+  std::memset(&map, 0, sizeof(map));
+  if (p.n_full > 0) {
+    auto encode = tensor_map_encoder();
+    if (!encode) return cudaErrorNotSupported;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.G) * p.row_bytes / 8,
+                                static_cast<cuuint64_t>(p.n_full / p.G)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(p.G) * p.row_bytes};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(p.W / 8), static_cast<cuuint32_t>(p.R)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(p.w), dims, strides,
+                               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  }
+  const int64_t qthreads = static_cast<int64_t>(p.nchunk) * p.ncols * (kMmaKC / 32);
+  e = launch_pdl(mma_quantise_x, static_cast<unsigned>((qthreads + 255) / 256), 256, 0, r.stream, r.x, p.k,
+                 p.batch, p.ncols, p.nchunk, r.xrec);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(gemv_mma<Q, NG, MT>, static_cast<unsigned>(grid), threads, smem, r.stream, map, p);
+}
+
+template <int Q, int NG>
+inline cudaError_t launch_mma_ng(MmaParams p, const GemvRequest& r) {
+  mma_geometry(p.row_bytes, p.chunk_bytes, &p.G, &p.W);
+  // smallest row block whose boxes hold whole 8-row half tiles
+  const int mt_min = p.G >= 8 ? 4 : (p.G == 4 ? 2 : 1);
+  int64_t grid = env_int("FRC_MMA_GRID", r.sms);
+  const int64_t useful = (p.n + 16 * mt_min - 1) / (16 * mt_min);
+  if (grid > useful) grid = useful;
+  if (grid < 1) grid = 1;
+  const int64_t per_cta = (p.n + grid - 1) / grid;
+  int mt = env_int("FRC_MMA_MT", per_cta <= 16 ? 1 : (per_cta <= 32 ? 2 : 4));
+  if (mt < mt_min) mt = mt_min;
+  if (mt == 1) return launch_mma_cfg<Q, NG, 1>(p, r, static_cast<int>(grid));
+  if (mt == 2) return launch_mma_cfg<Q, NG, 2>(p, r, static_cast<int>(grid));
+  return launch_mma_cfg<Q, NG, 4>(p, r, static_cast<int>(grid));
+}
+
+template <int Q>
+inline cudaError_t launch_mma(const GemvRequest& r) {
+  using F = Fmt<Q>;
+  MmaParams p{};
+  p.w = r.w;
+  p.y = r.y;
+  p.n = r.n;
+  p.k = r.k;
+  p.batch = r.batch;
+  p.row_bytes = (r.k / F::QK) * F::TS;
+  p.chunk_bytes = kMmaKC / F::QK * F::TS;
+  p.nchunk = (r.k + kMmaKC - 1) / kMmaKC;
+  p.xrec = r.xrec;
+  p.status = r.status;
+  if (r.batch <= 4) {
+    p.ncols = 4;
+    return launch_mma_ng<Q, 1>(p, r);
+  }
+  if (r.batch <= 8) {
+    p.ncols = 8;
+    return launch_mma_ng<Q, 2>(p, r);
+  }
+  p.ncols = 16;
+  return launch_mma_ng<Q, 4>(p, r);
+}
+
 // Largest tile footprint must fit in shared memory with two stages.
 template <int Q>
 inline bool tiles_fit(int row_bytes) {
@@ -303,6 +463,7 @@ cudaError_t launch_gemv(const GemvRequest& r) {
     p.units = (r.k / F::QK) * F::UPB;
   }
   if (r.nmat > 1) return cudaErrorNotSupported;  // callers fall back to one launch per matrix
+  if (r.batch > 1 && r.xrec && !force_xb && env_int("FRC_GEMV_FP32", 0) == 0) return launch_mma<Q>(r);
   if (r.batch == 1 && !force_xb) {
     const int cap1 = 32 * kMaxConsumerWarps;
     if (p.units <= cap1) return launch_x1<Q, 1>(p, r, (p.units + 31) / 32);
