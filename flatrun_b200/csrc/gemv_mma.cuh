@@ -6,8 +6,8 @@
 // two signed byte planes xq = 256 xh + xl.  The records are written to scratch
 // memory chunk-major: for every k-chunk of kMmaKC elements, every column's
 // record holds the h plane, the l plane (words permuted so a thread's two
-// fragment words are adjacent) and per group a float4
-// (sx, sx*sum32(xq), sx*sum16a(xq), sx*sum16b(xq)).
+// fragment words are adjacent) and per group 32 bytes of sums:
+// (sx, sx*sum(xq), then for each 16-element half -32*sum(xh), -32*sum(xl)).
 //
 // Main kernel (gemv_mma): persistent CTAs own contiguous rows, processed in
 // row blocks of 16*MT rows.  One producer thread streams, per (row block,
@@ -21,14 +21,17 @@
 // groups) with the raw quant values as A (Q4_K: one mask per word) and the x
 // byte planes as B: columns 2c and 2c+1 of an 8-wide N tile are the h and l
 // planes of activation column c, so a thread's accumulator pair combines to
-// T = 256 c0 + c1 = sum(q * xq) exactly.  Each (row, step, column) then adds
+// T = 256 c0 + c1 = sum(q * xq) (accumulators seeded so each plane's sum
+// reads back as a float after one add).  Each (row, step, column) then adds
 // sx * (ds * T - dm * X) in fp32, with (ds, dm) from a per-warp shared table
-// (K-quants: d*sc and dmin*m; Q6_K: d*sc and 32 d*sc; Q8_0: d and 0; Q1_0,
-// whose bits enter as +1/-1 bytes: d and 0).  At the end of a row block the warps' partial sums are reduced
+// (K-quants: d*sc and dmin*m; Q8_0: d and 0; Q1_0, whose bits enter as +1/-1
+// bytes: d and 0; Q6_K: d*sc, its -32 offset folded into the seeds).  At the end of a row block the warps' partial sums are reduced
 // through shared memory and written to y.
 #pragma once
 
 #include <cuda.h>
+
+#include <type_traits>
 
 #include "gemv.cuh"
 
@@ -36,7 +39,13 @@ namespace frc {
 
 constexpr int kMmaKC = 512;                                     // k elements per chunk
 constexpr int kMmaPlane = kMmaKC + 32;                          // bytes per byte plane (padded)
-constexpr int kMmaColBytes = 2 * kMmaPlane + (kMmaKC / 32) * 16;  // 1344: per column per chunk
+constexpr int kMmaMeta = 32;                                    // bytes of sums per 32-element group
+constexpr int kMmaColBytes = 2 * kMmaPlane + (kMmaKC / 32) * kMmaMeta;  // 1600: per column per chunk
+// Accumulator seed: the int32 bits of 1.5 * 2^23.  An MMA started from it
+// leaves bits that read as the float 1.5 * 2^23 + sum for |sum| < 2^22, so one
+// FADD recovers each plane's exact integer sum (no int->float conversion).
+constexpr int kMagicBits = 0x4B400000;
+constexpr float kMagicF = 12582912.0f;
 constexpr int kMmaWarps = 8;                                    // consumer warps
 
 struct MmaParams {
@@ -98,7 +107,7 @@ static __global__ void __launch_bounds__(256) mma_quantise_x(const float* __rest
   const float sx = amax > 0.f ? amax / static_cast<float>(kXqMax) : 1.0f;
   const float inv = amax > 0.f ? static_cast<float>(kXqMax) / amax : 0.0f;
   uint32_t hw[8], lw[8];
-  int s16a = 0, s16b = 0;
+  int ssum = 0, sh[2] = {0, 0}, sl[2] = {0, 0};
 #pragma unroll
   for (int w = 0; w < 8; ++w) {
     uint32_t h = 0, l = 0;
@@ -106,9 +115,11 @@ static __global__ void __launch_bounds__(256) mma_quantise_x(const float* __rest
     for (int b = 0; b < 4; ++b) {
       int q = __float2int_rn(v[4 * w + b] * inv);
       q = q > kXqMax ? kXqMax : (q < -kXqMax ? -kXqMax : q);
-      if (w < 4) s16a += q; else s16b += q;
       const int qh = (q + 128) >> 8;
       const int ql = q - 256 * qh;
+      ssum += q;
+      sh[w >> 2] += qh;
+      sl[w >> 2] += ql;
       h |= (static_cast<uint32_t>(qh) & 0xFFu) << (8 * b);
       l |= (static_cast<uint32_t>(ql) & 0xFFu) << (8 * b);
     }
@@ -123,9 +134,10 @@ static __global__ void __launch_bounds__(256) mma_quantise_x(const float* __rest
   ph[1] = make_uint4(hw[2], hw[6], hw[3], hw[7]);
   pl[0] = make_uint4(lw[0], lw[4], lw[1], lw[5]);
   pl[1] = make_uint4(lw[2], lw[6], lw[3], lw[7]);
-  reinterpret_cast<float4*>(rec + 2 * kMmaPlane)[gi] =
-      make_float4(sx, sx * static_cast<float>(s16a + s16b), sx * static_cast<float>(s16a),
-                  sx * static_cast<float>(s16b));
+  uint4* pm = reinterpret_cast<uint4*>(rec + 2 * kMmaPlane + gi * kMmaMeta);
+  pm[0] = make_uint4(__float_as_uint(sx), __float_as_uint(sx * static_cast<float>(ssum)),
+                     static_cast<uint32_t>(-32 * sh[0]), static_cast<uint32_t>(-32 * sl[0]));
+  pm[1] = make_uint4(static_cast<uint32_t>(-32 * sh[1]), static_cast<uint32_t>(-32 * sl[1]), 0u, 0u);
 }
 
 // ---------------------------------------------------------------------------
@@ -135,12 +147,12 @@ template <bool AU8>
 FRC_DEVICE_INLINE void mma_k32(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                uint32_t b1) {
   if constexpr (AU8) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   } else {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -148,12 +160,19 @@ FRC_DEVICE_INLINE void mma_k32(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a
 }
 
 FRC_DEVICE_INLINE void mma_k16(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
-  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+  asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
                : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
                : "r"(a0), "r"(a1), "r"(b0));
 }
 
 FRC_DEVICE_INLINE uint32_t ld32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// Four bytes at a 2-byte aligned shared-memory address, as two 16-bit loads
+// and one byte permute (no branch on the alignment: rows of one warp differ).
+FRC_DEVICE_INLINE uint32_t ld32_h2(const uint8_t* p) {
+  const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
+  return __byte_perm(static_cast<uint32_t>(q[0]), static_cast<uint32_t>(q[1]), 0x5410);
+}
 
 // Spread bits 0..3 of `nib` to bit 0 of bytes 0..3.
 FRC_DEVICE_INLINE uint32_t spread4(uint32_t nib) { return ((nib & 0xFu) * 0x00204081u) & 0x01010101u; }
@@ -164,7 +183,8 @@ FRC_DEVICE_INLINE uint32_t spread4(uint32_t nib) { return ((nib & 0xFu) * 0x0020
 //   elem(w, j)          first element of step j inside the chunk
 //   xgroup(w, j)        the step's 32-element activation group
 //   xhalf(w)            KSTEP 16: which half of that group (warp-constant)
-//   scales(row, w, tab) (ds, dm) per step: y += sx * (ds * T - dm * X)
+//   scales(row, w, ds, dm)  per step: y += sx * (ds * T - dm * X); dm only
+//                       for formats with mins (HAS_MIN)
 //   decode(row, w, t, lo, hi)  this thread's A-fragment words per step:
 //                       elements 4t..4t+3 (lo) and 16+4t..16+4t+3 (hi)
 // `row` points at the row's chunk in shared memory (2-byte aligned; 16-byte
@@ -181,14 +201,17 @@ template <> struct Mm<kQ4_K> {
   static FRC_DEVICE_INLINE int elem(int w, int j) { return 32 * (2 * w + j); }
   static FRC_DEVICE_INLINE int xgroup(int w, int j) { return 2 * w + j; }
   static FRC_DEVICE_INLINE int xhalf(int) { return 0; }
-  static FRC_DEVICE_INLINE void scales(const uint8_t* row, int w, float2 (&tab)[SPW]) {
+  static constexpr bool HAS_MIN = true;
+  static FRC_DEVICE_INLINE void scales(const uint8_t* row, int w, float (&ds)[SPW], float (&dm)[SPW]) {
     const uint4 hdr = *reinterpret_cast<const uint4*>(row + 144 * (w >> 2));
     const float d = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
     float sc0, m0, sc1, m1;
     scale_min_k4_words(2 * (w & 3), hdr.y, hdr.z, hdr.w, sc0, m0);
     scale_min_k4_words(2 * (w & 3) + 1, hdr.y, hdr.z, hdr.w, sc1, m1);
-    tab[0] = make_float2(d * sc0, dmin * m0);
-    tab[1] = make_float2(d * sc1 * 0.0625f, dmin * m1);
+    ds[0] = d * sc0;
+    dm[0] = dmin * m0;
+    ds[1] = d * sc1 * 0.0625f;
+    dm[1] = dmin * m1;
   }
   static FRC_DEVICE_INLINE void decode(const uint8_t* row, int w, int t, uint32_t (&lo)[SPW], uint32_t (&hi)[SPW]) {
     const uint8_t* qs = row + 144 * (w >> 2) + 16 + 32 * (w & 3) + 4 * t;
@@ -207,14 +230,17 @@ template <> struct Mm<kQ5_K> {
   static FRC_DEVICE_INLINE int elem(int w, int j) { return 32 * (2 * w + j); }
   static FRC_DEVICE_INLINE int xgroup(int w, int j) { return 2 * w + j; }
   static FRC_DEVICE_INLINE int xhalf(int) { return 0; }
-  static FRC_DEVICE_INLINE void scales(const uint8_t* row, int w, float2 (&tab)[SPW]) {
+  static constexpr bool HAS_MIN = true;
+  static FRC_DEVICE_INLINE void scales(const uint8_t* row, int w, float (&ds)[SPW], float (&dm)[SPW]) {
     const uint4 hdr = *reinterpret_cast<const uint4*>(row + 176 * (w >> 2));
     const float d = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
     float sc0, m0, sc1, m1;
     scale_min_k4_words(2 * (w & 3), hdr.y, hdr.z, hdr.w, sc0, m0);
     scale_min_k4_words(2 * (w & 3) + 1, hdr.y, hdr.z, hdr.w, sc1, m1);
-    tab[0] = make_float2(d * sc0, dmin * m0);
-    tab[1] = make_float2(d * sc1, dmin * m1);
+    ds[0] = d * sc0;
+    dm[0] = dmin * m0;
+    ds[1] = d * sc1;
+    dm[1] = dmin * m1;
   }
   static FRC_DEVICE_INLINE void decode(const uint8_t* row, int w, int t, uint32_t (&lo)[SPW], uint32_t (&hi)[SPW]) {
     const uint8_t* blk = row + 176 * (w >> 2);
@@ -237,16 +263,17 @@ template <> struct Mm<kQ8_0> {
   static FRC_DEVICE_INLINE int elem(int w, int j) { return 32 * (2 * w + j); }
   static FRC_DEVICE_INLINE int xgroup(int w, int j) { return 2 * w + j; }
   static FRC_DEVICE_INLINE int xhalf(int) { return 0; }
-  static FRC_DEVICE_INLINE void scales(const uint8_t* row, int w, float2 (&tab)[SPW]) {
+  static constexpr bool HAS_MIN = false;
+  static FRC_DEVICE_INLINE void scales(const uint8_t* row, int w, float (&ds)[SPW], float (&)[SPW]) {
 #pragma unroll
-    for (int j = 0; j < SPW; ++j) tab[j] = make_float2(half_bits_to_float(ld_u16(row + 34 * (2 * w + j))), 0.f);
+    for (int j = 0; j < SPW; ++j) ds[j] = half_bits_to_float(ld_u16(row + 34 * (2 * w + j)));
   }
   static FRC_DEVICE_INLINE void decode(const uint8_t* row, int w, int t, uint32_t (&lo)[SPW], uint32_t (&hi)[SPW]) {
 #pragma unroll
     for (int j = 0; j < SPW; ++j) {
       const uint8_t* qs = row + 34 * (2 * w + j) + 2 + 4 * t;
-      lo[j] = ld_u32_a2(qs);
-      hi[j] = ld_u32_a2(qs + 16);
+      lo[j] = ld32_h2(qs);
+      hi[j] = ld32_h2(qs + 16);
     }
   }
 };
@@ -259,16 +286,17 @@ template <> struct Mm<kQ1_0> {
   static FRC_DEVICE_INLINE int elem(int w, int j) { return 128 * (w >> 1) + 32 * (2 * (w & 1) + j); }
   static FRC_DEVICE_INLINE int xgroup(int w, int j) { return 4 * (w >> 1) + 2 * (w & 1) + j; }
   static FRC_DEVICE_INLINE int xhalf(int) { return 0; }
-  static FRC_DEVICE_INLINE void scales(const uint8_t* row, int w, float2 (&tab)[SPW]) {
+  static constexpr bool HAS_MIN = false;
+  static FRC_DEVICE_INLINE void scales(const uint8_t* row, int w, float (&ds)[SPW], float (&)[SPW]) {
     const float d = half_bits_to_float(ld_u16(row + 18 * (w >> 1)));
 #pragma unroll
-    for (int j = 0; j < SPW; ++j) tab[j] = make_float2(d, 0.f);
+    for (int j = 0; j < SPW; ++j) ds[j] = d;
   }
   static FRC_DEVICE_INLINE void decode(const uint8_t* row, int w, int t, uint32_t (&lo)[SPW], uint32_t (&hi)[SPW]) {
     const uint8_t* bits = row + 18 * (w >> 1) + 2 + 8 * (w & 1);
 #pragma unroll
     for (int j = 0; j < SPW; ++j) {
-      const uint32_t v = ld_u32_a2(bits + 4 * j);
+      const uint32_t v = ld32_h2(bits + 4 * j);
       lo[j] = ~(spread4(v >> (4 * t)) * 0xFEu);
       hi[j] = ~(spread4(v >> (4 * t + 16)) * 0xFEu);
     }
@@ -285,7 +313,8 @@ template <> struct Mm<kQ6_K> {
   static FRC_DEVICE_INLINE int elem(int w, int j) { return 256 * (w >> 2) + 128 * ((w >> 1) & 1) + 32 * j + 16 * (w & 1); }
   static FRC_DEVICE_INLINE int xgroup(int w, int j) { return 8 * (w >> 2) + 4 * ((w >> 1) & 1) + j; }
   static FRC_DEVICE_INLINE int xhalf(int w) { return w & 1; }
-  static FRC_DEVICE_INLINE void scales(const uint8_t* row, int w, float2 (&tab)[SPW]) {
+  static constexpr bool HAS_MIN = false;
+  static FRC_DEVICE_INLINE void scales(const uint8_t* row, int w, float (&ds)[SPW], float (&)[SPW]) {
     const uint8_t* blk = row + 210 * (w >> 2);
     const float d = half_bits_to_float(ld_u16(blk + 208));
     uint32_t sw[2];
@@ -294,16 +323,15 @@ template <> struct Mm<kQ6_K> {
     for (int j = 0; j < SPW; ++j) {
       const int byte = 2 * j + (w & 1);  // scales[8h + 2r + lh]
       const int sc = static_cast<int>(static_cast<int8_t>((sw[byte >> 2] >> (8 * (byte & 3))) & 0xFFu));
-      const float ds = d * static_cast<float>(sc);
-      tab[j] = make_float2(ds, 32.0f * ds);
+      ds[j] = d * static_cast<float>(sc);
     }
   }
   static FRC_DEVICE_INLINE void decode(const uint8_t* row, int w, int t, uint32_t (&lo)[SPW], uint32_t (&hi)[SPW]) {
     const int h = (w >> 1) & 1, lh = w & 1;
     const uint8_t* blk = row + 210 * (w >> 2);
-    const uint32_t ql0 = ld_u32_a2(blk + 64 * h + 16 * lh + 4 * t);
-    const uint32_t ql1 = ld_u32_a2(blk + 64 * h + 32 + 16 * lh + 4 * t);
-    const uint32_t qh = ld_u32_a2(blk + 128 + 32 * h + 16 * lh + 4 * t);
+    const uint32_t ql0 = ld32_h2(blk + 64 * h + 16 * lh + 4 * t);
+    const uint32_t ql1 = ld32_h2(blk + 64 * h + 32 + 16 * lh + 4 * t);
+    const uint32_t qh = ld32_h2(blk + 128 + 32 * h + 16 * lh + 4 * t);
     // bits 2r, 2r+1 of every qh byte moved to bits 4, 5 of that byte
     lo[0] = (ql0 & 0x0F0F0F0Fu) | ((qh << 4) & 0x30303030u);
     lo[1] = (ql1 & 0x0F0F0F0Fu) | ((qh << 2) & 0x30303030u);
@@ -329,21 +357,24 @@ FRC_DEVICE_INLINE int64_t slot_row(const MmaParams& p, int64_t row0, int L) {
   return row0 + (static_cast<int64_t>(L & (p.R - 1)) << p.logG) + (L >> p.logR);
 }
 
-// Start of row q's current chunk inside stage `st`.  Rows of a box share the
-// offset of their chunk inside its 16-byte granule, (q * row_bytes + choff) % 16.
-// The < G rows in [n_full, n) have their own slots; slots of rows past n
-// (padding of the last row block, computed and discarded) stay in the boxes.
-FRC_DEVICE_INLINE const uint8_t* slot_ptr(const MmaParams& p, const uint8_t* st, int64_t q, int L, uint64_t choff) {
-  const uint32_t mis = static_cast<uint32_t>((static_cast<uint64_t>(q) * p.row_bytes + choff) & 15u);
-  if (q >= p.n_full && q < p.n) return st + p.tail_off + (q - p.n_full) * p.WT + mis;
-  return st + (L >> p.logR) * p.JS + (L & (p.R - 1)) * p.W + mis;
+// Stage-relative slot of row-block slot L (matrix row q), without the
+// chunk's 16-byte phase (q * row_bytes + choff) % 16.  Rows of a box share
+// that phase.  The < G rows in [n_full, n) have their own slots; slots of
+// rows past n (padding of the last row block, computed and discarded) stay
+// in the boxes.
+FRC_DEVICE_INLINE int slot_offset(const MmaParams& p, int64_t q, int L) {
+  if (q >= p.n_full && q < p.n) return p.tail_off + static_cast<int>(q - p.n_full) * p.WT;
+  return (L >> p.logR) * p.JS + (L & (p.R - 1)) * p.W;
 }
 
 // Shared memory: [mbarriers | abort] 256 B, reduction [W][RM][NC] floats,
-// scale tables [W][RM][SPW] float2 (rounded to 128 B), then the stages.
+// per-warp scale tables [SPW][RM] of ds (float) or, for formats with mins,
+// (ds, dm) (float2), step-major so a warp's lanes touch consecutive words;
+// rounded to 128 B; then the stages.
 template <int Q, int NG, int MT>
 __host__ __device__ constexpr int mma_header_bytes() {
-  return (256 + kMmaWarps * 16 * MT * 4 * NG * 4 + kMmaWarps * 16 * MT * Mm<Q>::SPW * 8 + 127) / 128 * 128;
+  return (256 + kMmaWarps * 16 * MT * 4 * NG * 4 + kMmaWarps * 16 * MT * Mm<Q>::SPW * 4 * (Mm<Q>::HAS_MIN ? 2 : 1) +
+          127) / 128 * 128;
 }
 
 template <int Q, int NG, int MT>
@@ -357,7 +388,9 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 1)
   uint64_t* empty = full + p.nstage;
   int* abort_flag = reinterpret_cast<int*>(empty + p.nstage);
   float* red = reinterpret_cast<float*>(smem + 256);
-  float2* tab_all = reinterpret_cast<float2*>(smem + 256 + kMmaWarps * RM * NC * 4);
+  constexpr int TABW = SPW * RM * (M::HAS_MIN ? 2 : 1);  // floats per warp
+  float* tab_all = reinterpret_cast<float*>(smem + 256 + kMmaWarps * RM * NC * 4);
+  using TabT = typename std::conditional<M::HAS_MIN, float2, float>::type;
   uint8_t* stages = smem + mma_header_bytes<Q, NG, MT>();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -501,7 +534,7 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 1)
     for (int h = 0; h < 2; ++h)
 #pragma unroll
       for (int ng = 0; ng < NG; ++ng) acc[mt][h][ng] = 0.f;
-  float2* tab = tab_all + warp * RM * SPW;
+  TabT* tab = reinterpret_cast<TabT*>(tab_all + warp * TABW);  // [SPW][RM]
   const int lh = M::xhalf(warp);
   // this warp's steps inside a full chunk and inside the last chunk
   int nvj_full = 0, nvj_last = 0;
@@ -515,6 +548,35 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 1)
   int ch = 0;
   int64_t row0 = r0;
   uint64_t choff = 0;
+  // Rows of the current row block this thread touches, fixed for the block:
+  // decode rows L = 16 mt + 8 h + g and scale rows L = lane, lane + 32, as
+  // stage-relative slot offsets plus the rows' own 16-byte phase
+  // (q * row_bytes) % 16 (zero for Q4_K/Q5_K, whose blocks are 16-byte
+  // multiples); a chunk adds its phase choff % 16.
+  constexpr bool kPhase = F::TS % 16 != 0;
+  int doff[MT][2], dmis[MT][2];
+  int soff[2], smis[2];
+  bool sval[2];
+  auto setup_block = [&]() {
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int L = 16 * mt + 8 * h + g;
+        const int64_t q = slot_row(p, row0, L);
+        doff[mt][h] = slot_offset(p, q, L);
+        dmis[mt][h] = kPhase ? static_cast<int>((static_cast<uint64_t>(q) * p.row_bytes) & 15u) : 0;
+      }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int L = lane + 32 * u;
+      const int64_t q = slot_row(p, row0, L);
+      sval[u] = L < RM && q < r1;
+      soff[u] = slot_offset(p, q, L);
+      smis[u] = kPhase ? static_cast<int>((static_cast<uint64_t>(q) * p.row_bytes) & 15u) : 0;
+    }
+  };
+  setup_block();
 
   for (int i = 0; i < items; ++i) {
     const bool ok = __all_sync(0xffffffffu, wait_phase(&full[s], ph, abort));
@@ -522,68 +584,106 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 1)
       const int nvj = ch == p.nchunk - 1 ? nvj_last : nvj_full;
       const uint8_t* st = stages + static_cast<size_t>(s) * p.stage_stride;
       const uint8_t* xs = st + p.x_off;
+      const int chmis = static_cast<int>(choff & 15u);
       if (nvj > 0) {
-        for (int L = lane; L < RM; L += 32) {
-          const int64_t q = slot_row(p, row0, L);
-          if (q < r1) {
-            float2 tr[SPW];
-            M::scales(slot_ptr(p, st, q, L, choff), warp, tr);
 #pragma unroll
-            for (int j = 0; j < SPW; ++j) tab[L * SPW + j] = tr[j];
+        for (int u = 0; u < 2; ++u) {
+          if (sval[u]) {
+            float ds[SPW], dm[SPW];
+            M::scales(st + soff[u] + (kPhase ? ((smis[u] + chmis) & 15) : 0), warp, ds, dm);
+#pragma unroll
+            for (int j = 0; j < SPW; ++j) {
+              if constexpr (M::HAS_MIN) {
+                tab[j * RM + lane + 32 * u] = make_float2(ds[j], dm[j]);
+              } else {
+                tab[j * RM + lane + 32 * u] = ds[j];
+              }
+            }
           }
         }
         __syncwarp();
-        // activation fragments of this warp's steps, shared by all row tiles
-        uint32_t b0[SPW][NG], b1[SPW][NG];
-        float sx[SPW][NG], sxx[SPW][NG];
-#pragma unroll
-        for (int j = 0; j < SPW; ++j) {
+        // Activation fragments of step j, column group ng: B words, the group
+        // scale sx, sx*sum(xq) (K-quants' min term) and the accumulator seeds
+        // (Q6_K: seeds carry -32*sum of each plane, so the MMA sums
+        // (q - 32) * x directly).  Loaded once for all row tiles when they
+        // fit in registers (HOIST), else per row tile.
+        struct BFrag {
+          uint32_t b0, b1;
+          float sx, sxx;
+          int ch, cl;
+        };
+        auto load_b = [&](int j, int ng) {
+          BFrag f;
           const int grp = M::xgroup(warp, j);
-#pragma unroll
-          for (int ng = 0; ng < NG; ++ng) {
-            const uint8_t* pb = xs + (4 * ng + (g >> 1)) * kMmaColBytes + (g & 1) * kMmaPlane + grp * 32 + 8 * t;
-            if constexpr (M::KSTEP == 32) {
-              const uint2 bb = *reinterpret_cast<const uint2*>(pb);
-              b0[j][ng] = bb.x;
-              b1[j][ng] = bb.y;
-            } else {
-              b0[j][ng] = *reinterpret_cast<const uint32_t*>(pb + 4 * lh);
-              b1[j][ng] = 0u;
-            }
-            const float4 f4 = reinterpret_cast<const float4*>(xs + (4 * ng + t) * kMmaColBytes + 2 * kMmaPlane)[grp];
-            sx[j][ng] = f4.x;
-            sxx[j][ng] = M::KSTEP == 32 ? f4.y : (lh ? f4.w : f4.z);
+          const uint8_t* pb = xs + (4 * ng + (g >> 1)) * kMmaColBytes + (g & 1) * kMmaPlane + grp * 32 + 8 * t;
+          const uint8_t* pm = xs + (4 * ng + t) * kMmaColBytes + 2 * kMmaPlane + grp * kMmaMeta;
+          if constexpr (M::KSTEP == 32) {
+            const uint2 bb = *reinterpret_cast<const uint2*>(pb);
+            f.b0 = bb.x;
+            f.b1 = bb.y;
+            const float2 m2 = *reinterpret_cast<const float2*>(pm);
+            f.sx = m2.x;
+            f.sxx = m2.y;
+            f.ch = kMagicBits;
+            f.cl = kMagicBits;
+          } else {
+            f.b0 = *reinterpret_cast<const uint32_t*>(pb + 4 * lh);
+            f.b1 = 0u;
+            f.sx = *reinterpret_cast<const float*>(pm);
+            f.sxx = 0.f;
+            const int2 k2 = *reinterpret_cast<const int2*>(pm + 8 + 8 * lh);
+            f.ch = kMagicBits + k2.x;
+            f.cl = kMagicBits + k2.y;
           }
+          return f;
+        };
+        constexpr bool HOIST = SPW * NG <= 8;
+        BFrag bh[HOIST ? SPW : 1][HOIST ? NG : 1];
+        if constexpr (HOIST) {
+#pragma unroll
+          for (int j = 0; j < SPW; ++j)
+#pragma unroll
+            for (int ng = 0; ng < NG; ++ng) bh[j][ng] = load_b(j, ng);
         }
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
           const int la = mt * 16 + g, lb = la + 8;
-          const uint8_t* pa = slot_ptr(p, st, slot_row(p, row0, la), la, choff);
-          const uint8_t* pc = slot_ptr(p, st, slot_row(p, row0, lb), lb, choff);
+          const uint8_t* pa = st + doff[mt][0] + (kPhase ? ((dmis[mt][0] + chmis) & 15) : 0);
+          const uint8_t* pc = st + doff[mt][1] + (kPhase ? ((dmis[mt][1] + chmis) & 15) : 0);
           uint32_t lo0[SPW], hi0[SPW], lo1[SPW], hi1[SPW];
           M::decode(pa, warp, t, lo0, hi0);
           M::decode(pc, warp, t, lo1, hi1);
 #pragma unroll
           for (int j = 0; j < SPW; ++j) {
             if (j >= nvj) break;
-            const float2 sc0 = tab[la * SPW + j];
-            const float2 sc1 = tab[lb * SPW + j];
+            float ds0, ds1, dm0 = 0.f, dm1 = 0.f;
+            if constexpr (M::HAS_MIN) {
+              const float2 e0 = tab[j * RM + la], e1 = tab[j * RM + lb];
+              ds0 = e0.x;
+              dm0 = e0.y;
+              ds1 = e1.x;
+              dm1 = e1.y;
+            } else {
+              ds0 = tab[j * RM + la];
+              ds1 = tab[j * RM + lb];
+            }
 #pragma unroll
             for (int ng = 0; ng < NG; ++ng) {
-              int c[4] = {0, 0, 0, 0};
+              const BFrag f = HOIST ? bh[HOIST ? j : 0][HOIST ? ng : 0] : load_b(j, ng);
+              int c[4] = {f.ch, f.cl, f.ch, f.cl};
               if constexpr (M::KSTEP == 32) {
-                mma_k32<M::AU8>(c, lo0[j], lo1[j], hi0[j], hi1[j], b0[j][ng], b1[j][ng]);
+                mma_k32<M::AU8>(c, lo0[j], lo1[j], hi0[j], hi1[j], f.b0, f.b1);
               } else {
-                mma_k16(c, lo0[j], lo1[j], b0[j][ng]);
+                mma_k16(c, lo0[j], lo1[j], f.b0);
               }
-              const float t0 = static_cast<float>(c[0] * 256 + c[1]);
-              const float t1 = static_cast<float>(c[2] * 256 + c[3]);
-              if constexpr (Q == kQ8_0 || Q == kQ1_0) {
-                acc[mt][0][ng] = fmaf(sx[j][ng] * sc0.x, t0, acc[mt][0][ng]);
-                acc[mt][1][ng] = fmaf(sx[j][ng] * sc1.x, t1, acc[mt][1][ng]);
+              const float t0 = fmaf(256.0f, __int_as_float(c[0]) - kMagicF, __int_as_float(c[1]) - kMagicF);
+              const float t1 = fmaf(256.0f, __int_as_float(c[2]) - kMagicF, __int_as_float(c[3]) - kMagicF);
+              if constexpr (!M::HAS_MIN) {
+                acc[mt][0][ng] = fmaf(f.sx * ds0, t0, acc[mt][0][ng]);
+                acc[mt][1][ng] = fmaf(f.sx * ds1, t1, acc[mt][1][ng]);
               } else {
-                acc[mt][0][ng] = fmaf(sx[j][ng] * sc0.x, t0, fmaf(-sc0.y, sxx[j][ng], acc[mt][0][ng]));
-                acc[mt][1][ng] = fmaf(sx[j][ng] * sc1.x, t1, fmaf(-sc1.y, sxx[j][ng], acc[mt][1][ng]));
+                acc[mt][0][ng] = fmaf(f.sx * ds0, t0, fmaf(-dm0, f.sxx, acc[mt][0][ng]));
+                acc[mt][1][ng] = fmaf(f.sx * ds1, t1, fmaf(-dm1, f.sxx, acc[mt][1][ng]));
               }
             }
           }
@@ -628,6 +728,7 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 1)
       }
       named_barrier_sync(1, kMmaWarps * 32);  // red is rewritten by the next row block
       row0 += RM;
+      setup_block();
     }
   }
 }
