@@ -40,6 +40,7 @@ SIGNATURES: dict[str, list] = {
     "frc_weight_nbytes": [_i, _i64, _i64, ctypes.POINTER(_sz)],
     "frc_device_status": [_i, ctypes.POINTER(ctypes.c_uint32)],
     "frc_gemv": [_i, _p, _sz, _i64, _i64, _p, _i64, _p, _p],
+    "frc_gemv_noalloc": [_i, _p, _sz, _i64, _i64, _p, _i64, _p, _p],
     "frc_dequant_dev": [_i, _p, _sz, _i64, _p, _p],
     "frc_gemv_multi": [_i, _i, ctypes.POINTER(_p), ctypes.POINTER(_sz), ctypes.POINTER(_i64), _i64, _p, _i64,
                        ctypes.POINTER(_p), _p],

@@ -373,6 +373,55 @@ int stateless_dequant(int quant, const uint8_t* w, size_t w_bytes, int64_t out_d
   return host_dequant(ds, quant, nullptr, w, w_bytes, n_elems, out);
 }
 
+// ---- fixed activation-record region for frc_gemv_noalloc -----------------
+// The batched tensor-core kernel stages x as 16-bit integer records
+// (frc::mma_scratch_bytes(k, batch) bytes).  frc_gemv keeps them in a
+// per-device buffer it allocates and grows; frc_gemv_noalloc uses this static
+// region instead: the module's own device memory, one instance per device,
+// never allocated or freed by the library.  Every call rewrites the records
+// it reads, so its contents need no initial value.
+constexpr size_t kNoAllocRecordBytes = FRC_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) uint8_t g_noalloc_records[kNoAllocRecordBytes];
+// Bounded-wait status of the kernels this entry point launches; zero when the
+// module loads (kernels only OR bits into it).
+static __device__ uint32_t g_noalloc_status;
+
+struct NoAllocDevice {
+  bool ready;
+  uint8_t* records;  // device address of g_noalloc_records on this device
+  uint32_t* status;
+  int sms;
+};
+constexpr int kNoAllocMaxDevices = 64;
+NoAllocDevice g_noalloc[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
+
+// Device addresses of the static region on the current device, looked up on
+// the first call for that device (the host-side names are not device
+// addresses).
+int noalloc_device(int* dev_out, NoAllocDevice** out) {
+  int dev = 0;
+  FRC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(FRC_ERR_INVALID, "frc_gemv_noalloc: device %d unsupported", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  NoAllocDevice& d = g_noalloc[dev];
+  if (!d.ready) {
+    void* rec = nullptr;
+    void* st = nullptr;
+    int sms = 0;
+    FRC_CUDA(cudaGetSymbolAddress(&rec, g_noalloc_records), "cudaGetSymbolAddress(activation records)");
+    FRC_CUDA(cudaGetSymbolAddress(&st, g_noalloc_status), "cudaGetSymbolAddress(status word)");
+    FRC_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
+    d.records = static_cast<uint8_t*>(rec);
+    d.status = static_cast<uint32_t*>(st);
+    d.sms = sms;
+    d.ready = true;
+  }
+  *dev_out = dev;
+  *out = &d;
+  return FRC_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -443,6 +492,52 @@ int frc_gemv(int quant, const void* w_dev, size_t w_bytes, int64_t n, int64_t k,
   if (rc) return rc;
   return gemv_device(ds, quant, static_cast<const uint8_t*>(w_dev), n, k, x_dev, batch, y_dev,
                      static_cast<cudaStream_t>(stream));
+}
+
+int frc_gemv_noalloc(int quant, const void* w_dev, size_t w_bytes, int64_t n, int64_t k, const float* x_dev,
+                     int64_t batch, float* y_dev, void* stream) {
+  int rc = check_matmul(quant, w_bytes, n, k, batch);
+  if (rc) return rc;
+  if (batch < 2 || batch > kMaxGemvBatch)
+    return fail(FRC_ERR_INVALID, "frc_gemv_noalloc: batch must be 2..%d (got %lld); batch 1 is frc_gemv", kMaxGemvBatch,
+                (long long)batch);
+  if ((w_bytes && !w_dev) || (batch * k && !x_dev) || (batch * n && !y_dev)) return fail(FRC_ERR_INVALID, "null buffer");
+  if (!aligned(w_dev, 16)) return fail(FRC_ERR_INVALID, "frc_gemv_noalloc: weight must be 16-byte aligned");
+  if (!aligned(x_dev, 16)) return fail(FRC_ERR_INVALID, "frc_gemv_noalloc: x must be 16-byte aligned");
+  if (!aligned(y_dev, 4)) return fail(FRC_ERR_INVALID, "frc_gemv_noalloc: y must be 4-byte aligned");
+  const size_t need = static_cast<size_t>(frc::mma_scratch_bytes(k, static_cast<int>(batch)));
+  if (need > kNoAllocRecordBytes) {
+    int64_t kmax = 0;
+    while (static_cast<size_t>(frc::mma_scratch_bytes(kmax + 512, static_cast<int>(batch))) <= kNoAllocRecordBytes)
+      kmax += 512;
+    return fail(FRC_ERR_INVALID,
+                "frc_gemv_noalloc: k=%lld at batch %lld needs %zu bytes of activation records, more than the fixed "
+                "%zu (k <= %lld at this batch); use frc_gemv",
+                (long long)k, (long long)batch, need, kNoAllocRecordBytes, (long long)kmax);
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n == 0) return FRC_OK;
+  if (k == 0) {
+    FRC_CUDA(cudaMemsetAsync(y_dev, 0, sizeof(float) * n * batch, st), "cudaMemsetAsync");
+    return FRC_OK;
+  }
+  int dev = 0;
+  NoAllocDevice* d = nullptr;
+  rc = noalloc_device(&dev, &d);
+  if (rc) return rc;
+  frc::GemvRequest r{};
+  r.w = static_cast<const uint8_t*>(w_dev);
+  r.x = x_dev;
+  r.y = y_dev;
+  r.n = n;
+  r.k = static_cast<int>(k);
+  r.batch = static_cast<int>(batch);
+  r.status = d->status;
+  r.stream = st;
+  r.device = dev;
+  r.sms = d->sms;
+  r.xrec = d->records;
+  return launch_gemv_quant(quant, r);
 }
 
 int frc_gemv_multi(int quant, int count, const void* const* w_dev, const size_t* w_bytes, const int64_t* n,

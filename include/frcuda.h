@@ -83,12 +83,39 @@ int frc_weight_nbytes(int quant, int64_t n, int64_t k, size_t* nbytes);
 int frc_device_status(int device, uint32_t* flags);
 
 /* ---- stream-ordered device-pointer kernels ------------------------------ *
- * No allocation, no synchronisation: the work is enqueued on `stream`
- * (a cudaStream_t; NULL = legacy default stream) of the current device.
- * w_dev must be 16-byte aligned.  frc_gemv computes y_dev (batch, n) from
- * x_dev (batch, k), 1 <= batch <= 16.                                        */
+ * No synchronisation: the work is enqueued on `stream` (a cudaStream_t;
+ * NULL = legacy default stream) of the current device.  w_dev must be
+ * 16-byte aligned.  frc_gemv computes y_dev (batch, n) from x_dev (batch, k),
+ * 1 <= batch <= 16.  For 2 <= batch <= 16 the kernel first writes x as
+ * 16-bit integer records into a per-device buffer the library owns; that
+ * buffer is allocated on the first such call and grown (old buffers are kept
+ * until exit) when a later call needs more.  Calls with batch >= 2 on one
+ * device share it, so they must not overlap in time across streams. */
 int frc_gemv(int quant, const void* w_dev, size_t w_bytes, int64_t n, int64_t k,
              const float* x_dev, int64_t batch, float* y_dev, void* stream);
+/* Batched GEMV that allocates no device memory (no counterpart in the
+ * reference).  Same arguments and result as frc_gemv for 2 <= batch <= 16,
+ * but the activation records live in a fixed region of
+ * FRC_NOALLOC_SCRATCH_BYTES of the library's own static device memory (one
+ * per device) instead of a buffer allocated on demand.  It serves callers
+ * that cannot allocate once they run: an engine that has committed all of
+ * HBM to weights and KV cache, a device-memory pool policy that forbids
+ * cudaMalloc after start-up, or a decode loop that cannot take the
+ * device-wide synchronisation cudaMalloc/cudaFree may cause.
+ * Limit: the records take ceil(k/512) * C * 1600 bytes, C = 4, 8 or 16 (batch
+ * rounded up to one of those), i.e. k <= 167424 at batch <= 4, 83456 at <= 8
+ * and 41472 at <= 16; larger k, batch 1 or batch > 16 return FRC_ERR_INVALID
+ * with a message.  The first call on each device (with that
+ * device current) looks up the region's device address; make that first call
+ * before any stream capture.  No memory needs to start at zero: each call
+ * rewrites the records it reads.  All calls on one device share the region,
+ * so two calls that can overlap in time (streams without ordering between
+ * them) race and give wrong results.  A bounded wait that runs out sets a bit
+ * in a status word of this entry point that frc_device_status does not read;
+ * y is then incomplete. */
+#define FRC_NOALLOC_SCRATCH_BYTES 2097152
+int frc_gemv_noalloc(int quant, const void* w_dev, size_t w_bytes, int64_t n, int64_t k,
+                     const float* x_dev, int64_t batch, float* y_dev, void* stream);
 /* One launch for up to 4 weights of the same quant and k that share x
  * (q/k/v, or gate/up, of a layer): y_dev[m] (batch, n[m]) = x . W_m^T.  At
  * batch 1 the rows of all matrices form one row space of a single kernel
