@@ -30,6 +30,11 @@ extern template cudaError_t launch_dequant<kQ4_K>(const DequantRequest&);
 extern template cudaError_t launch_dequant<kQ5_K>(const DequantRequest&);
 extern template cudaError_t launch_dequant<kQ6_K>(const DequantRequest&);
 extern template cudaError_t launch_dequant<kQ1_0>(const DequantRequest&);
+extern template cudaError_t launch_gemm_tc<kQ8_0>(const GemvRequest&);
+extern template cudaError_t launch_gemm_tc<kQ4_K>(const GemvRequest&);
+extern template cudaError_t launch_gemm_tc<kQ5_K>(const GemvRequest&);
+extern template cudaError_t launch_gemm_tc<kQ6_K>(const GemvRequest&);
+extern template cudaError_t launch_gemm_tc<kQ1_0>(const GemvRequest&);
 }  // namespace frc
 
 struct frc_weight {
@@ -224,6 +229,35 @@ int gemv_device(DeviceState* ds, int quant, const uint8_t* w, int64_t n, int64_t
   if (k == 0) {
     FRC_CUDA(cudaMemsetAsync(y, 0, sizeof(float) * n * seq, stream), "cudaMemsetAsync");
     return FRC_OK;
+  }
+  // more than kMaxGemvBatch columns: the tensor-core prefill GEMM, if the
+  // shape suits it (FRC_TC=0 turns it off)
+  if (seq > kMaxGemvBatch && frc::env_int("FRC_TC", 1)) {
+    frc::GemvRequest r{};
+    r.w = w;
+    r.x = x;
+    r.y = y;
+    r.n = n;
+    r.k = static_cast<int>(k);
+    r.batch = static_cast<int>(seq);
+    r.status = ds->status;
+    r.stream = stream;
+    r.device = ds->device;
+    r.sms = ds->sms;
+    int rc = record_scratch(ds, static_cast<size_t>(frc::tc_scratch_bytes(k, seq)), &r.xrec);
+    if (rc != FRC_OK) return rc;
+    cudaError_t e;
+    switch (quant) {
+      case FRC_Q8_0: e = frc::launch_gemm_tc<frc::kQ8_0>(r); break;
+      case FRC_Q4_K: e = frc::launch_gemm_tc<frc::kQ4_K>(r); break;
+      case FRC_Q5_K: e = frc::launch_gemm_tc<frc::kQ5_K>(r); break;
+      case FRC_Q6_K: e = frc::launch_gemm_tc<frc::kQ6_K>(r); break;
+      case FRC_Q1_0: e = frc::launch_gemm_tc<frc::kQ1_0>(r); break;
+      default: return fail(FRC_ERR_INVALID, "unsupported quant id %d", quant);
+    }
+    if (e == cudaSuccess) return FRC_OK;
+    if (e != cudaErrorNotSupported) return cuda_fail(e, "prefill launch");
+    (void)cudaGetLastError();
   }
   // balanced chunks of at most kMaxGemvBatch columns, so a multi-column call
   // never leaves a single column for the batch-1 kernel

@@ -5,4 +5,5 @@
 namespace frc {
 template cudaError_t launch_gemv<kQ4_K>(const GemvRequest&);
 template cudaError_t launch_dequant<kQ4_K>(const DequantRequest&);
+template cudaError_t launch_gemm_tc<kQ4_K>(const GemvRequest&);
 }  // namespace frc

@@ -5,4 +5,5 @@
 namespace frc {
 template cudaError_t launch_gemv<kQ5_K>(const GemvRequest&);
 template cudaError_t launch_dequant<kQ5_K>(const DequantRequest&);
+template cudaError_t launch_gemm_tc<kQ5_K>(const GemvRequest&);
 }  // namespace frc

@@ -5,4 +5,5 @@
 namespace frc {
 template cudaError_t launch_gemv<kQ6_K>(const GemvRequest&);
 template cudaError_t launch_dequant<kQ6_K>(const DequantRequest&);
+template cudaError_t launch_gemm_tc<kQ6_K>(const GemvRequest&);
 }  // namespace frc

@@ -14,6 +14,7 @@
 #include <tuple>
 
 #include "gemv.cuh"
+#include "gemm_tc.cuh"
 #include "gemv_mma.cuh"
 
 namespace frc {
@@ -400,6 +401,76 @@ inline cudaError_t launch_mma(const GemvRequest& r) {
   }
   p.ncols = 16;
   return launch_mma_ng<Q, 4>(p, r);
+}
+
+// Bytes of fp16 activations the tensor-core prefill stages.
+inline int64_t tc_scratch_bytes(int64_t k, int64_t seq) { return seq * k * 2; }
+
+// Tensor-core prefill (seq > 16): x -> fp16 pre-pass, then one CTA per
+// 256-row x 256-token tile.  cudaErrorNotSupported when the shape does not
+// fit this kernel (the caller then runs 16-column chunks).
+template <int Q>
+inline cudaError_t launch_gemm_tc(const GemvRequest& r) {
+  using F = Fmt<Q>;
+  constexpr int RAWK = TcRaw<Q>::K;
+  TcParams p{};
+  p.y = r.y;
+  p.n = r.n;
+  p.k = r.k;
+  p.seq = r.batch;
+  p.row_bytes = (r.k / F::QK) * F::TS;
+  p.chunk_bytes = RAWK / F::QK * F::TS;
+  p.nchunk = (r.k + RAWK - 1) / RAWK;
+  p.status = r.status;
+  mma_geometry(p.row_bytes, p.chunk_bytes, &p.G, &p.W);
+  if (r.n % p.G != 0 || r.k % kTcK != 0 || !r.xrec) return cudaErrorNotSupported;
+  p.R = kTcM / p.G;
+  p.logG = 0;
+  while ((1 << p.logG) < p.G) ++p.logG;
+  p.logR = 0;
+  while ((1 << p.logR) < p.R) ++p.logR;
+  p.JS = round_up(p.R * p.W, 128);
+  p.raw_stride = round_up(p.G * p.JS, 1024);
+  // + 1 KB slack: the dequant's word loads may run a few bytes past the last
+  // raw row; at least ~120 KB so two CTAs never share an SM (each takes all
+  // of TMEM)
+  int smem = tc_smem_bytes(p.raw_stride) + 1024;
+  if (smem < 120 * 1024) smem = 120 * 1024;
+  if (smem > kSmemBudget) return cudaErrorNotSupported;
+  int per_sm = 0;
+  cudaError_t e = kernel_occupancy(reinterpret_cast<const void*>(gemm_tc<Q>), r.device, kTcThreads, smem, &per_sm);
+  if (e != cudaSuccess) return e;
+  auto encode = tensor_map_encoder();
+  if (!encode) return cudaErrorNotSupported;
+  CUtensorMap wmap, xmap;
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.G) * p.row_bytes / 8, static_cast<cuuint64_t>(r.n / p.G)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(p.G) * p.row_bytes};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(p.W / 8), static_cast<cuuint32_t>(p.R)};
+    const cuuint32_t estr[2] = {1, 1};
+    if (encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(r.w), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(r.k), static_cast<cuuint64_t>(r.batch)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(r.k) * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTcK), static_cast<cuuint32_t>(kTcN)};
+    const cuuint32_t estr[2] = {1, 1};
+    if (encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, r.xrec, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  const int64_t count = static_cast<int64_t>(r.batch) * r.k;
+  tc_convert_x<<<static_cast<unsigned>((count / 8 + 255) / 256), 256, 0, r.stream>>>(r.x, count,
+                                                                                       reinterpret_cast<__half*>(r.xrec));
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const dim3 grid(static_cast<unsigned>((r.n + kTcM - 1) / kTcM), static_cast<unsigned>((r.batch + kTcN - 1) / kTcN));
+  gemm_tc<Q><<<grid, kTcThreads, smem, r.stream>>>(wmap, xmap, p);
+  return cudaGetLastError();
 }
 
 // Largest tile footprint must fit in shared memory with two stages.
