@@ -100,97 +100,123 @@ FRC_DEVICE_INLINE void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// ---- dequantisation of 8 consecutive elements -------------------------------
-// Elements e .. e+7 (e a multiple of 8, relative to the raw chunk) of one row
-// whose raw chunk starts at `row`, as fp32 w = scale * q - offset.
-FRC_DEVICE_INLINE float nib_f(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.0f; }
+// ---- dequantisation of one 32-element slice of a row ------------------------
+// Elements e0 .. e0+31 (e0 a multiple of 32, relative to the raw chunk) of a
+// row whose raw chunk starts at `row`, as 16 packed fp16 pairs of
+// w = scale * q - offset (fp32 arithmetic, one rounding to fp16).
+FRC_DEVICE_INLINE uint32_t pack_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Byte b of word t as the float 2^23 + byte (one permute).
+template <int B>
+FRC_DEVICE_INLINE float byte_f(uint32_t t) {
+  return __uint_as_float(__byte_perm(t, 0x4B000000u, 0x7650u + B));
+}
+
+// 32 unsigned byte values (8 words) -> fp16 pairs of s * (v - bias) - off,
+// with v read as 2^23 + v and the 2^23 folded into the bias.
+FRC_DEVICE_INLINE void bytes_to_h2(const uint32_t (&v)[8], float s, float bias, float off, uint32_t (&h)[16]) {
+  const float b = 8388608.0f + bias;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    h[2 * i] = pack_h2(fmaf(s, byte_f<0>(v[i]) - b, -off), fmaf(s, byte_f<1>(v[i]) - b, -off));
+    h[2 * i + 1] = pack_h2(fmaf(s, byte_f<2>(v[i]) - b, -off), fmaf(s, byte_f<3>(v[i]) - b, -off));
+  }
+}
 
 template <int Q> struct TcDeq;
 
 template <> struct TcDeq<kQ4_K> {
-  static FRC_DEVICE_INLINE void run(const uint8_t* row, int e, float (&w)[8]) {
-    const int sb = e >> 5, c = (e & 31) >> 3;
+  // one sub-block: low (even) or high (odd) nibbles of 32 qs bytes
+  static FRC_DEVICE_INLINE void slice(const uint8_t* row, int e0, uint32_t (&h)[16]) {
+    const int sb = e0 >> 5;
     const uint4 hdr = *reinterpret_cast<const uint4*>(row);
     float sc, m;
     scale_min_k4_words(sb, hdr.y, hdr.z, hdr.w, sc, m);
     const float ds = half_bits_to_float(hdr.x) * sc, dm = half_bits_to_float(hdr.x >> 16) * m;
-    const uint2 q = *reinterpret_cast<const uint2*>(row + 16 + 32 * (sb >> 1) + 8 * c);
+    const uint4* qs = reinterpret_cast<const uint4*>(row + 16 + 32 * (sb >> 1));
+    const uint4 q0 = qs[0], q1 = qs[1];
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
     const int sh = 4 * (sb & 1);
+    uint32_t v[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t v = ((i < 4 ? q.x : q.y) >> (8 * (i & 3) + sh)) & 0xFu;
-      w[i] = fmaf(ds, nib_f(v), -dm);
-    }
+    for (int i = 0; i < 8; ++i) v[i] = (w[i] >> sh) & 0x0F0F0F0Fu;
+    bytes_to_h2(v, ds, 0.f, dm, h);
   }
 };
 
 template <> struct TcDeq<kQ5_K> {
-  static FRC_DEVICE_INLINE void run(const uint8_t* row, int e, float (&w)[8]) {
-    const int sb = e >> 5, c = (e & 31) >> 3;
+  static FRC_DEVICE_INLINE void slice(const uint8_t* row, int e0, uint32_t (&h)[16]) {
+    const int sb = e0 >> 5;
     const uint4 hdr = *reinterpret_cast<const uint4*>(row);
     float sc, m;
     scale_min_k4_words(sb, hdr.y, hdr.z, hdr.w, sc, m);
     const float ds = half_bits_to_float(hdr.x) * sc, dm = half_bits_to_float(hdr.x >> 16) * m;
-    const uint2 q = *reinterpret_cast<const uint2*>(row + 48 + 32 * (sb >> 1) + 8 * c);
-    const uint2 h = *reinterpret_cast<const uint2*>(row + 16 + 8 * c);
+    const uint4* qs = reinterpret_cast<const uint4*>(row + 48 + 32 * (sb >> 1));
+    const uint4* qhp = reinterpret_cast<const uint4*>(row + 16);
+    const uint4 q0 = qs[0], q1 = qs[1], h0 = qhp[0], h1 = qhp[1];
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    const uint32_t hb[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
     const int sh = 4 * (sb & 1);
+    uint32_t v[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t qq = ((i < 4 ? q.x : q.y) >> (8 * (i & 3) + sh)) & 0xFu;
-      const uint32_t hb = ((i < 4 ? h.x : h.y) >> (8 * (i & 3) + sb)) & 1u;
-      w[i] = fmaf(ds, nib_f(qq | (hb << 4)), -dm);
-    }
+    for (int i = 0; i < 8; ++i) v[i] = ((w[i] >> sh) & 0x0F0F0F0Fu) | (((hb[i] >> sb) & 0x01010101u) << 4);
+    bytes_to_h2(v, ds, 0.f, dm, h);
   }
 };
 
 template <> struct TcDeq<kQ6_K> {
-  static FRC_DEVICE_INLINE void run(const uint8_t* row, int e, float (&w)[8]) {
-    const int hh = e >> 7, r = (e & 127) >> 5, l0 = e & 31;
+  // one quarter (hh, r) of a block: two 16-element scale groups
+  static FRC_DEVICE_INLINE void slice(const uint8_t* row, int e0, uint32_t (&h)[16]) {
+    const int hh = e0 >> 7, r = (e0 & 127) >> 5;
     const float d = half_bits_to_float(ld_u16(row + 208));
-    const int sc = static_cast<int>(static_cast<int8_t>(row[192 + 8 * hh + 2 * r + (l0 >> 4)]));
-    const float ds = d * static_cast<float>(sc);
-    const uint8_t* ql = row + 64 * hh + 32 * (r & 1) + l0;
-    const uint8_t* qh = row + 128 + 32 * hh + l0;
-    uint32_t a[2], b[2];
-    lds_words_a2<2>(ql, a);
-    lds_words_a2<2>(qh, b);
+    const uint8_t* scp = row + 192 + 8 * hh + 2 * r;
+    const float ds0 = d * static_cast<float>(static_cast<int8_t>(scp[0]));
+    const float ds1 = d * static_cast<float>(static_cast<int8_t>(scp[1]));
+    uint32_t ql[8], qh[8];
+    lds_words_a2<8>(row + 64 * hh + 32 * (r & 1), ql);
+    lds_words_a2<8>(row + 128 + 32 * hh, qh);
+    uint32_t v[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t lo = (a[i >> 2] >> (8 * (i & 3) + (r >= 2 ? 4 : 0))) & 0xFu;
-      const uint32_t hi = (b[i >> 2] >> (8 * (i & 3) + 2 * r)) & 3u;
-      w[i] = ds * (nib_f(lo | (hi << 4)) - 32.0f);
+    for (int i = 0; i < 8; ++i)
+      v[i] = ((ql[i] >> (r >= 2 ? 4 : 0)) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * r)) & 0x03030303u) << 4);
+    uint32_t lo[16], hi[16];
+    bytes_to_h2(v, ds0, 32.f, 0.f, lo);
+    bytes_to_h2(v, ds1, 32.f, 0.f, hi);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {  // elements 0..15 use scale 0, 16..31 scale 1
+      h[i] = lo[i];
+      h[8 + i] = hi[8 + i];
     }
   }
 };
 
 template <> struct TcDeq<kQ8_0> {
-  static FRC_DEVICE_INLINE void run(const uint8_t* row, int e, float (&w)[8]) {
-    const uint8_t* blk = row + 34 * (e >> 5);
+  // one block: int8 values read as unsigned after flipping the sign bit
+  static FRC_DEVICE_INLINE void slice(const uint8_t* row, int e0, uint32_t (&h)[16]) {
+    const uint8_t* blk = row + 34 * (e0 >> 5);
     const float d = half_bits_to_float(ld_u16(blk));
-    uint32_t q[2];
-    lds_words_a2<2>(blk + 2 + (e & 31), q);
+    uint32_t q[8];
+    lds_words_a2<8>(blk + 2, q);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int v = static_cast<int>(static_cast<int8_t>((q[i >> 2] >> (8 * (i & 3))) & 0xFFu));
-      w[i] = d * static_cast<float>(v);
-    }
+    for (int i = 0; i < 8; ++i) q[i] ^= 0x80808080u;
+    bytes_to_h2(q, d, 128.f, 0.f, h);
   }
 };
 
 template <> struct TcDeq<kQ1_0> {
-  static FRC_DEVICE_INLINE void run(const uint8_t* row, int e, float (&w)[8]) {
-    const uint8_t* blk = row + 18 * (e >> 7);
+  static FRC_DEVICE_INLINE void slice(const uint8_t* row, int e0, uint32_t (&h)[16]) {
+    const uint8_t* blk = row + 18 * (e0 >> 7);
     const float d = half_bits_to_float(ld_u16(blk));
-    const uint32_t bits = blk[2 + ((e & 127) >> 3)];
+    const uint32_t bits = ld_u16(blk + 2 + ((e0 & 127) >> 3)) | (ld_u16(blk + 4 + ((e0 & 127) >> 3)) << 16);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) w[i] = (bits >> i) & 1u ? d : -d;
+    for (int i = 0; i < 16; ++i)
+      h[i] = pack_h2((bits >> (2 * i)) & 1u ? d : -d, (bits >> (2 * i + 1)) & 1u ? d : -d);
   }
 };
 
-FRC_DEVICE_INLINE uint32_t pack_h2(float a, float b) {
-  const __half2 h = __floats2half2_rn(a, b);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
 
 // Shared memory: barriers and the TMEM address (1 KB), then the A, B and raw
 // rings, every stage 1024-byte aligned.
@@ -338,8 +364,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     // ---- dequantisation into the swizzled fp16 A stages ----------------------------
-    const int wt = threadIdx.x - 3 * 32;  // 0 .. 255
-    const int ch = wt & 3;                 // 16-byte chunk (8 elements) of a 64-byte row
+    const int L = threadIdx.x - 3 * 32;  // this thread's tile row, 0 .. 255
+    const int64_t q = row0 + (static_cast<int64_t>(L & (p.R - 1)) << p.logG) + (L >> p.logR);
+    const int slot = (L >> p.logR) * p.JS + (L & (p.R - 1)) * p.W;
+    const uint32_t qmis = static_cast<uint32_t>((static_cast<uint64_t>(q) * p.row_bytes) & 15u);
+    const int swz = (L >> 1) & 3;
     bool ok = true;
     for (int s = 0; s < nslice && ok; ++s) {
       const int c = s / SPC, a = s % kTcAStages, rs = c % kTcRawStages;
@@ -353,20 +382,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       }
       const uint8_t* raw = raw_ring + static_cast<size_t>(rs) * p.raw_stride;
-      uint8_t* at = a_ring + a * kTcTileBytes;
-      const uint64_t choff = static_cast<uint64_t>(c) * p.chunk_bytes;
-      const int e = (s % SPC) * kTcK + 8 * ch;  // element offset in the raw chunk
-#pragma unroll 1
-      for (int L = wt >> 2; L < kTcM; L += 64) {
-        const int64_t q = row0 + (static_cast<int64_t>(L & (p.R - 1)) << p.logG) + (L >> p.logR);
-        const uint8_t* row = raw + (L >> p.logR) * p.JS + (L & (p.R - 1)) * p.W +
-                             static_cast<uint32_t>((static_cast<uint64_t>(q) * p.row_bytes + choff) & 15u);
-        float w[8];
-        TcDeq<Q>::run(row, e, w);
-        const uint4 v = make_uint4(pack_h2(w[0], w[1]), pack_h2(w[2], w[3]), pack_h2(w[4], w[5]), pack_h2(w[6], w[7]));
-        // 64-byte swizzle: 16-byte chunk index ^= (row / 2) % 4 within 512-byte atoms
-        *reinterpret_cast<uint4*>(at + L * 64 + ((ch ^ ((L >> 1) & 3)) << 4)) = v;
-      }
+      const uint32_t chmis = static_cast<uint32_t>((static_cast<uint64_t>(c) * p.chunk_bytes) & 15u);
+      uint32_t h[16];
+      TcDeq<Q>::slice(raw + slot + ((qmis + chmis) & 15u), (s % SPC) * kTcK, h);
+      // 64-byte swizzle: 16-byte chunk index ^= (row / 2) % 4 within 512-byte atoms
+      uint8_t* line = a_ring + a * kTcTileBytes + L * 64;
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch)
+        *reinterpret_cast<uint4*>(line + ((ch ^ swz) << 4)) =
+            make_uint4(h[4 * ch], h[4 * ch + 1], h[4 * ch + 2], h[4 * ch + 3]);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {

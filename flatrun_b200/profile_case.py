@@ -8,6 +8,9 @@ Weights are synthetic (flatrun_b200.synth), resident on cuda:0, rotated over
 ``-k regex:gemv -s <skip> -c <count>`` sees exactly these launches.  With
 ``--mats M`` each launch is one fused frc_gemv_multi over M (n, k) matrices
 sharing x (the gate+up launch of a layer is ``--n 18944 --k 3584 --mats 2``).
+With ``--batch`` above 16 (prefill) the weights are uploaded with
+frc_weight_create and each launch is frc_weight_matmul_dev (the tensor-core
+GEMM: an fp16 conversion of x, then ``gemm_tc``).
 """
 
 from __future__ import annotations
@@ -36,6 +39,24 @@ def main() -> None:
     lib = _lib.load()
     raw = synth.make_weight(a.quant, a.n, a.k, seed=0)
     x = synth.make_x(a.k, batch=None if a.batch == 1 else a.batch, seed=1)
+    if a.batch > 16:
+        handles = []
+        for _ in range(a.copies):
+            h = ctypes.c_void_p()
+            _lib.check(lib.frc_weight_create(0, _lib.QUANT_IDS[a.quant], raw.ctypes.data, raw.nbytes, a.n, a.k,
+                                             ctypes.byref(h)), lib)
+            handles.append(h)
+        x_d = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+        y_d = torch.empty((a.batch, a.n), device="cuda")
+        stream = torch.cuda.current_stream()
+        for i in range(a.launches):
+            _lib.check(lib.frc_weight_matmul_dev(handles[i % a.copies], x_d.data_ptr(), a.batch, y_d.data_ptr(),
+                                                 ctypes.c_void_p(stream.cuda_stream)), lib)
+        torch.cuda.synchronize()
+        for h in handles:
+            lib.frc_weight_free(h)
+        print(f"ok {a.quant} n={a.n} k={a.k} batch={a.batch} launches={a.launches}")
+        return
     stride = (raw.nbytes + 255) // 256 * 256
     nbuf = a.copies * a.mats
     buf = torch.empty(nbuf * stride, dtype=torch.uint8, device="cuda")
