@@ -80,6 +80,8 @@ WORKLOADS = {
                      desc="Q6_K down 3584x18944, batch 1"),
     "q1_0": dict(mats=[("w", "Q1_0", 4096, 4096, "w")], batch=1, desc="Q1_0 4096x4096, batch 1"),
     "gate_q4k": dict(mats=[("gate", "Q4_K", 18944, 3584, "w")], batch=1, desc="Q4_K gate 18944x3584, batch 1"),
+    "prefill_gate_q4k": dict(mats=[("gate", "Q4_K", 18944, 3584, "w")], batch=512,
+                             desc="config 3: batched prefill, 512 tokens x 3584 through gate 18944x3584 Q4_K"),
 }
 
 
@@ -102,6 +104,23 @@ def peaks() -> tuple[float, str]:
             return float(json.load(f)["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
     except (OSError, KeyError, ValueError):
         return 6650.0, "fallback 6.65 TB/s"
+
+
+def tensor_peak() -> tuple[float, str]:
+    """Dense 16-bit tensor-core peak for a kernel timed alone (fp16 and bf16
+    run at the same rate on B200)."""
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback 1.59 PFLOP/s"
+
+
+# Prefill batches: the reference's batched kernels re-read the whole weight
+# per token (_C.cpp:154-283), so the CPU legs time a sample of this many
+# tokens and scale linearly to the full batch.
+CPU_SAMPLE_TOKENS = 16
 
 
 def ncu_traffic(workload: str):
@@ -201,6 +220,14 @@ def cpu_reference_step_fn(mats, batch, host_w, xs):
 
 
 def run_cpu(mats, batch, steps, warmup, host_w, xs):
+    """Median seconds of one reference step at `batch`; above
+    CPU_SAMPLE_TOKENS tokens the step runs on the first CPU_SAMPLE_TOKENS rows
+    of x and is scaled by batch / CPU_SAMPLE_TOKENS."""
+    scale = 1.0
+    if batch > CPU_SAMPLE_TOKENS:
+        xs = [np.ascontiguousarray(x[:CPU_SAMPLE_TOKENS]) for x in xs]
+        scale = batch / CPU_SAMPLE_TOKENS
+        batch = CPU_SAMPLE_TOKENS
     step, kind = cpu_reference_step_fn(mats, batch, host_w, xs)
     for _ in range(warmup):
         step()
@@ -208,7 +235,7 @@ def run_cpu(mats, batch, steps, warmup, host_w, xs):
     for _ in range(steps):
         t0 = time.perf_counter()
         step()
-        times.append(time.perf_counter() - t0)
+        times.append((time.perf_counter() - t0) * scale)
     return statistics.median(times), sum(times), kind
 
 
@@ -259,7 +286,9 @@ def main() -> None:
             "config": {"workload": wl["desc"], "global_batch": batch},
             "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": 1, "kind": kind,
                              "sample": f"{steps} timed steps of the full workload (median), reference "
-                                       "flatrun_native._C scalar kernels (single-threaded on x86)"},
+                                       "flatrun_native._C scalar kernels (single-threaded on x86)"
+                                       + (f"; {CPU_SAMPLE_TOKENS} of the {batch} tokens per step, time scaled "
+                                          f"by {batch / CPU_SAMPLE_TOKENS:g}" if batch > CPU_SAMPLE_TOKENS else "")},
             "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }), flush=True)
         return
@@ -493,14 +522,41 @@ def main() -> None:
         med, total, kind = run_cpu(mats, batch, 3, 1, base, xs_host)
         cpu = {"value": round(step_bytes / med / 1e9, 4), "unit": UNIT, "cores": 1, "kind": kind,
                "sample": "3 timed passes over the full workload (median) after 1 warm-up, reference "
-                         "flatrun_native._C built from its sources (scalar, single-threaded on x86)"}
+                         "flatrun_native._C built from its sources (scalar, single-threaded on x86)"
+                         + (f"; {CPU_SAMPLE_TOKENS} of the {batch} tokens per pass, time scaled by "
+                            f"{batch / CPU_SAMPLE_TOKENS:g}" if batch > CPU_SAMPLE_TOKENS else "")}
 
     if rank == 0:
+        # the kernel family each call runs: batch 1 dp4a GEMV, 2..16 int8
+        # tensor-core GEMV (pre-pass + main), more: tcgen05 GEMM (fp16 pre-pass
+        # + main)
+        if batch == 1:
+            kname, dtype, calls_per_group = "gemv_i8", "s8 x s8 -> s32, fp32 scales", lambda g: 1
+        elif batch <= 16:
+            kname, dtype, calls_per_group = "gemv_mma", "s8 x s8 -> s32 (mma.sync), fp32 scales", lambda g: 2 * len(g)
+        else:
+            kname, dtype, calls_per_group = "gemm_tc", "f16 x f16 -> f32 (tcgen05)", lambda g: 2 * len(g)
+        if batch > 16:
+            # tensor-bound: FLOPs of the dominant launch over its device time
+            dom_group = next(g for g in lgroups if "+".join(mats[i][0] for i in g) == dom_name)
+            flops = sum(2.0 * mats[i][2] * mats[i][3] * batch for i in dom_group)
+            tpk, tpk_src = tensor_peak()
+            tflops = flops / (per[dom_name]["us"] / 1e6) / 1e12
+            roof = {"bound": "tensor", "achieved": round(tflops, 1), "peak": tpk, "unit": "TFLOP/s",
+                    "frac": round(tflops / tpk, 4), "traffic": traffic, "peak_source": tpk_src,
+                    "flops_per_launch": flops}
+        else:
+            roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                    "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_src}
+        roof["kernel"] = f"{kname} <{mats[0][1]}> launch '{dom_name}' ({per[dom_name]['bytes'] / 1e6:.1f} MB per launch)"
+        roof["timing"] = ("K back-to-back launches of the dominant launch, one CUDA graph replay bracketed by CUDA "
+                          "events on the launching stream")
         out = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": wl["desc"], "global_batch": batch * world, "seq_len": 1,
+            "vs_baseline": None, "dtype": dtype, "data": "synthetic",
+            "config": {"workload": wl["desc"], "global_batch": (batch if batch <= 16 else 1) * world,
+                       "seq_len": 1 if batch <= 16 else batch,
                        "parallelism": f"row-shard x{world}" if world > 1 else "single GPU",
                        "weight_bytes_per_step": wbytes, "algorithmic_bytes_per_step": step_bytes,
                        "weight_copies_rotated": [p[2] for p in pools],
@@ -508,19 +564,13 @@ def main() -> None:
                              f"totalling >= 3x L2 ({sum(p[2] * mbytes[i] for i, p in enumerate(pools)) / 1e9:.2f} GB);"
                              f" L2 {l2 / 2**20:.0f} MiB"},
             "frac_of_8tbs": round(value / world / 8000.0, 4),
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": f"gemv_i8 <{mats[0][1]}> launch '{dom_name}' "
-                                   f"({per[dom_name]['bytes'] / 1e6:.1f} MB per launch)",
-                         "timing": "K back-to-back launches of the dominant launch, one CUDA graph replay bracketed "
-                                   "by CUDA events on the launching stream",
-                         "peak_source": peak_src},
+            "roofline": roof,
             "per_launch": per,
             "launches_per_step": len(lgroups),
             "cpu_baseline": cpu,
             "e2e": e2e,
             "clocks": clk,
-            "gpu_launches": K * len(lgroups),
+            "gpu_launches": K * sum(calls_per_group(g) for g in lgroups),
         }
         print(json.dumps(out), flush=True)
 

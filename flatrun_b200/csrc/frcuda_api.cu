@@ -516,7 +516,6 @@ int frc_gemv(int quant, const void* w_dev, size_t w_bytes, int64_t n, int64_t k,
              float* y_dev, void* stream) {
   int rc = check_matmul(quant, w_bytes, n, k, batch);
   if (rc) return rc;
-  if (batch > kMaxGemvBatch) return fail(FRC_ERR_INVALID, "frc_gemv: batch %lld > %d", (long long)batch, kMaxGemvBatch);
   if ((w_bytes && !w_dev) || (batch * k && !x_dev) || (batch * n && !y_dev)) return fail(FRC_ERR_INVALID, "null buffer");
   if (!aligned(w_dev, 16)) return fail(FRC_ERR_INVALID, "frc_gemv: weight must be 16-byte aligned");
   if (!aligned(x_dev, 16)) return fail(FRC_ERR_INVALID, "frc_gemv: x must be 16-byte aligned");
@@ -578,7 +577,7 @@ int frc_gemv_multi(int quant, int count, const void* const* w_dev, const size_t*
                    int64_t k, const float* x_dev, int64_t batch, float* const* y_dev, void* stream) {
   if (count < 1 || count > 4) return fail(FRC_ERR_INVALID, "frc_gemv_multi: count must be 1..4 (got %d)", count);
   if (!w_dev || !w_bytes || !n || !y_dev) return fail(FRC_ERR_INVALID, "null array");
-  if (batch < 1 || batch > kMaxGemvBatch) return fail(FRC_ERR_INVALID, "frc_gemv_multi: batch must be 1..%d", kMaxGemvBatch);
+  if (batch < 1) return fail(FRC_ERR_INVALID, "frc_gemv_multi: batch must be >= 1");
   for (int m = 0; m < count; ++m) {
     int rc = check_matmul(quant, w_bytes[m], n[m], k, batch);
     if (rc) return rc;

@@ -86,11 +86,14 @@ int frc_device_status(int device, uint32_t* flags);
  * No synchronisation: the work is enqueued on `stream` (a cudaStream_t;
  * NULL = legacy default stream) of the current device.  w_dev must be
  * 16-byte aligned.  frc_gemv computes y_dev (batch, n) from x_dev (batch, k),
- * 1 <= batch <= 16.  For 2 <= batch <= 16 the kernel first writes x as
- * 16-bit integer records into a per-device buffer the library owns; that
- * buffer is allocated on the first such call and grown (old buffers are kept
- * until exit) when a later call needs more.  Calls with batch >= 2 on one
- * device share it, so they must not overlap in time across streams. */
+ * batch >= 1: batch 1 on the dp4a kernel, 2..16 on the int8 tensor-core
+ * kernel, more (prefill) on the tcgen05 GEMM with fp16 operands and fp32
+ * accumulation (where the row length allows its tensor view; otherwise in
+ * chunks of at most 16 columns).  For batch >= 2 x is first staged (as
+ * 16-bit integer records, or as fp16) in a per-device buffer the library
+ * owns; it is allocated on the first such call and grown (old buffers are
+ * kept until exit) when a later call needs more.  Calls with batch >= 2 on
+ * one device share it, so they must not overlap in time across streams. */
 int frc_gemv(int quant, const void* w_dev, size_t w_bytes, int64_t n, int64_t k,
              const float* x_dev, int64_t batch, float* y_dev, void* stream);
 /* Batched GEMV that allocates no device memory (no counterpart in the

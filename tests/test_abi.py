@@ -74,10 +74,10 @@ def test_reference_error_paths_before_cuda(lib, fn, args, msg):
     assert msg in _lib.last_error(lib)
 
 
-def test_gemv_rejects_misaligned_and_oversized(lib):
+def test_gemv_rejects_misaligned_and_empty_batch(lib):
     assert lib.frc_gemv(12, 1, 144, 1, 256, 16, 1, 16, None) == _lib.FRC_ERR_INVALID
     assert "aligned" in _lib.last_error(lib)
-    assert lib.frc_gemv(12, 16, 144, 1, 256, 16, 17, 16, None) == _lib.FRC_ERR_INVALID
+    assert lib.frc_gemv(12, 16, 144, 1, 256, 16, 0, 16, None) == _lib.FRC_ERR_INVALID
     assert lib.frc_gemv(7, 16, 144, 1, 256, 16, 1, 16, None) == _lib.FRC_ERR_INVALID
 
 
