@@ -1,20 +1,22 @@
 // Batched prefill (more than 16 activation columns) on the 5th-generation
 // tensor cores: y (seq, n) = x (seq, k) . W^T with W in raw GGUF blocks.
 //
-// One CTA per output tile of kTcM = 256 weight rows x kTcN = 256 tokens,
-// accumulated in TMEM as two 128 x 256 fp32 accumulators (all 512 columns).
-// The k dimension advances in slices of kTcK = 32 elements:
-//   * warp 0 streams the raw weight bytes, kTcRawK elements of every row per
-//     raw chunk, as 2-D tensor boxes (the same G-row tensor view as the
+// One CTA per output tile of kTcM = 128 weight rows x kTcN = 512 tokens,
+// accumulated in TMEM as a 128 x 512 fp32 accumulator (all 512 columns), so
+// every weight of a 512-token prefill is dequantised once.  The k dimension
+// advances in slices of kTcK = 32 elements:
+//   * warp 0 streams the raw weight bytes, TcRaw<Q>::K elements of every row
+//     per raw chunk, as 2-D tensor boxes (the same G-row tensor view as the
 //     batched GEMV) into a 2-stage ring;
-//   * warp 1 streams the fp16 activation slice (256 tokens x 32 k, 64-byte
-//     swizzle) into a 3-stage ring;
-//   * warps 3..10 dequantise each slice of the raw rows to fp16, written in
-//     the 64-byte-swizzled K-major layout the MMA reads (2-stage ring), then
-//     run the epilogue;
+//   * warp 1 streams the fp16 activation slice (up to 512 tokens x 32 k as
+//     two 256-row boxes, 64-byte swizzle) into a 3-stage ring;
+//   * warps 3..10 dequantise each slice of the raw rows to fp16 (two threads
+//     per row), written in the 64-byte-swizzled K-major layout the MMA reads
+//     (4-stage ring), then run the epilogue;
 //   * one thread of warp 2 (which also owns the TMEM allocation) issues
-//     tcgen05.mma kind::f16 (M = 128, N = 256, K = 16: four per slice) and
-//     releases the stages with tcgen05.commit.
+//     tcgen05.mma kind::f16 (M = 128, N = 256, K = 16: up to four per
+//     slice, one per token half and k16 step) and releases the stages with
+//     tcgen05.commit.
 // Weights are rounded once to fp16 after the fp32 scale arithmetic and x is
 // rounded to fp16 by a pre-pass; products accumulate in fp32.  Every wait is
 // bounded; TMEM is freed on every path.
@@ -27,12 +29,13 @@
 
 namespace frc {
 
-constexpr int kTcM = 256, kTcN = 256, kTcK = 32;
+constexpr int kTcM = 128, kTcN = 512, kTcNH = 256, kTcK = 32;  // tile; kTcNH tokens per MMA
 constexpr int kTcWorkers = 8;              // dequant + epilogue warps (3 .. 10)
 constexpr int kTcThreads = (3 + kTcWorkers) * 32;
-constexpr int kTcAStages = 2, kTcBStages = 3, kTcRawStages = 2;
-constexpr int kTcTileBytes = kTcM * kTcK * 2;  // 16 KB: A stage; B stage is the same size
-static_assert(kTcM == kTcN, "A and B stages share one size");
+constexpr int kTcAStages = 4, kTcBStages = 3, kTcRawStages = 2;
+constexpr int kTcATile = kTcM * kTcK * 2;    // 8 KB
+constexpr int kTcBHalf = kTcNH * kTcK * 2;   // 16 KB: one 256-token box
+constexpr int kTcBTile = 2 * kTcBHalf;       // 32 KB
 
 template <int Q> struct TcRaw;  // elements of a row per raw chunk
 template <> struct TcRaw<kQ4_K> { static constexpr int K = 256; };
@@ -69,8 +72,8 @@ FRC_DEVICE_INLINE uint64_t umma_desc_sw64(uint32_t smem_addr) {
 }
 
 // Instruction descriptor: D f32, A/B f16, both K-major, M = 128, N = 256.
-constexpr uint32_t kTcIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(kTcN >> 3) << 17) |
-                              (static_cast<uint32_t>(128 >> 4) << 24);
+constexpr uint32_t kTcIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(kTcNH >> 3) << 17) |
+                              (static_cast<uint32_t>(kTcM >> 4) << 24);
 
 FRC_DEVICE_INLINE void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
   asm volatile(
@@ -100,10 +103,10 @@ FRC_DEVICE_INLINE void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// ---- dequantisation of one 32-element slice of a row ------------------------
-// Elements e0 .. e0+31 (e0 a multiple of 32, relative to the raw chunk) of a
-// row whose raw chunk starts at `row`, as 16 packed fp16 pairs of
-// w = scale * q - offset (fp32 arithmetic, one rounding to fp16).
+// ---- dequantisation of half a slice of a row --------------------------------
+// Elements e0 + 16 hf .. e0 + 16 hf + 15 (e0 a multiple of 32, relative to the
+// raw chunk) of a row whose raw chunk starts at `row`, as 8 packed fp16 pairs
+// of w = scale * q - offset (fp32 arithmetic, one rounding to fp16).
 FRC_DEVICE_INLINE uint32_t pack_h2(float a, float b) {
   const __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&h);
@@ -115,108 +118,100 @@ FRC_DEVICE_INLINE float byte_f(uint32_t t) {
   return __uint_as_float(__byte_perm(t, 0x4B000000u, 0x7650u + B));
 }
 
-// 32 unsigned byte values (8 words) -> fp16 pairs of s * (v - bias) - off,
+// 16 unsigned byte values (4 words) -> fp16 pairs of s * (v - bias) - off,
 // with v read as 2^23 + v and the 2^23 folded into the bias.
-FRC_DEVICE_INLINE void bytes_to_h2(const uint32_t (&v)[8], float s, float bias, float off, uint32_t (&h)[16]) {
+FRC_DEVICE_INLINE void bytes_to_h2(const uint32_t (&v)[4], float s, float bias, float off, uint32_t (&h)[8]) {
   const float b = 8388608.0f + bias;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < 4; ++i) {
     h[2 * i] = pack_h2(fmaf(s, byte_f<0>(v[i]) - b, -off), fmaf(s, byte_f<1>(v[i]) - b, -off));
     h[2 * i + 1] = pack_h2(fmaf(s, byte_f<2>(v[i]) - b, -off), fmaf(s, byte_f<3>(v[i]) - b, -off));
   }
+}
+
+FRC_DEVICE_INLINE void words4(const uint8_t* p, uint32_t (&w)[4]) {
+  const uint4 v = *reinterpret_cast<const uint4*>(p);
+  w[0] = v.x;
+  w[1] = v.y;
+  w[2] = v.z;
+  w[3] = v.w;
 }
 
 template <int Q> struct TcDeq;
 
 template <> struct TcDeq<kQ4_K> {
   // one sub-block: low (even) or high (odd) nibbles of 32 qs bytes
-  static FRC_DEVICE_INLINE void slice(const uint8_t* row, int e0, uint32_t (&h)[16]) {
+  static FRC_DEVICE_INLINE void half(const uint8_t* row, int e0, int hf, uint32_t (&h)[8]) {
     const int sb = e0 >> 5;
     const uint4 hdr = *reinterpret_cast<const uint4*>(row);
     float sc, m;
     scale_min_k4_words(sb, hdr.y, hdr.z, hdr.w, sc, m);
     const float ds = half_bits_to_float(hdr.x) * sc, dm = half_bits_to_float(hdr.x >> 16) * m;
-    const uint4* qs = reinterpret_cast<const uint4*>(row + 16 + 32 * (sb >> 1));
-    const uint4 q0 = qs[0], q1 = qs[1];
-    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    uint32_t w[4];
+    words4(row + 16 + 32 * (sb >> 1) + 16 * hf, w);
     const int sh = 4 * (sb & 1);
-    uint32_t v[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = (w[i] >> sh) & 0x0F0F0F0Fu;
-    bytes_to_h2(v, ds, 0.f, dm, h);
+    for (int i = 0; i < 4; ++i) w[i] = (w[i] >> sh) & 0x0F0F0F0Fu;
+    bytes_to_h2(w, ds, 0.f, dm, h);
   }
 };
 
 template <> struct TcDeq<kQ5_K> {
-  static FRC_DEVICE_INLINE void slice(const uint8_t* row, int e0, uint32_t (&h)[16]) {
+  static FRC_DEVICE_INLINE void half(const uint8_t* row, int e0, int hf, uint32_t (&h)[8]) {
     const int sb = e0 >> 5;
     const uint4 hdr = *reinterpret_cast<const uint4*>(row);
     float sc, m;
     scale_min_k4_words(sb, hdr.y, hdr.z, hdr.w, sc, m);
     const float ds = half_bits_to_float(hdr.x) * sc, dm = half_bits_to_float(hdr.x >> 16) * m;
-    const uint4* qs = reinterpret_cast<const uint4*>(row + 48 + 32 * (sb >> 1));
-    const uint4* qhp = reinterpret_cast<const uint4*>(row + 16);
-    const uint4 q0 = qs[0], q1 = qs[1], h0 = qhp[0], h1 = qhp[1];
-    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-    const uint32_t hb[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    uint32_t w[4], hb[4];
+    words4(row + 48 + 32 * (sb >> 1) + 16 * hf, w);
+    words4(row + 16 + 16 * hf, hb);
     const int sh = 4 * (sb & 1);
-    uint32_t v[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = ((w[i] >> sh) & 0x0F0F0F0Fu) | (((hb[i] >> sb) & 0x01010101u) << 4);
-    bytes_to_h2(v, ds, 0.f, dm, h);
+    for (int i = 0; i < 4; ++i) w[i] = ((w[i] >> sh) & 0x0F0F0F0Fu) | (((hb[i] >> sb) & 0x01010101u) << 4);
+    bytes_to_h2(w, ds, 0.f, dm, h);
   }
 };
 
 template <> struct TcDeq<kQ6_K> {
-  // one quarter (hh, r) of a block: two 16-element scale groups
-  static FRC_DEVICE_INLINE void slice(const uint8_t* row, int e0, uint32_t (&h)[16]) {
+  // quarter (hh, r) of a block; each 16-element half has its own scale
+  static FRC_DEVICE_INLINE void half(const uint8_t* row, int e0, int hf, uint32_t (&h)[8]) {
     const int hh = e0 >> 7, r = (e0 & 127) >> 5;
     const float d = half_bits_to_float(ld_u16(row + 208));
-    const uint8_t* scp = row + 192 + 8 * hh + 2 * r;
-    const float ds0 = d * static_cast<float>(static_cast<int8_t>(scp[0]));
-    const float ds1 = d * static_cast<float>(static_cast<int8_t>(scp[1]));
-    uint32_t ql[8], qh[8];
-    lds_words_a2<8>(row + 64 * hh + 32 * (r & 1), ql);
-    lds_words_a2<8>(row + 128 + 32 * hh, qh);
-    uint32_t v[8];
+    const float ds = d * static_cast<float>(static_cast<int8_t>(row[192 + 8 * hh + 2 * r + hf]));
+    uint32_t ql[4], qh[4];
+    lds_words_a2<4>(row + 64 * hh + 32 * (r & 1) + 16 * hf, ql);
+    lds_words_a2<4>(row + 128 + 32 * hh + 16 * hf, qh);
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      v[i] = ((ql[i] >> (r >= 2 ? 4 : 0)) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * r)) & 0x03030303u) << 4);
-    uint32_t lo[16], hi[16];
-    bytes_to_h2(v, ds0, 32.f, 0.f, lo);
-    bytes_to_h2(v, ds1, 32.f, 0.f, hi);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {  // elements 0..15 use scale 0, 16..31 scale 1
-      h[i] = lo[i];
-      h[8 + i] = hi[8 + i];
-    }
+    for (int i = 0; i < 4; ++i)
+      ql[i] = ((ql[i] >> (r >= 2 ? 4 : 0)) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * r)) & 0x03030303u) << 4);
+    bytes_to_h2(ql, ds, 32.f, 0.f, h);
   }
 };
 
 template <> struct TcDeq<kQ8_0> {
   // one block: int8 values read as unsigned after flipping the sign bit
-  static FRC_DEVICE_INLINE void slice(const uint8_t* row, int e0, uint32_t (&h)[16]) {
+  static FRC_DEVICE_INLINE void half(const uint8_t* row, int e0, int hf, uint32_t (&h)[8]) {
     const uint8_t* blk = row + 34 * (e0 >> 5);
     const float d = half_bits_to_float(ld_u16(blk));
-    uint32_t q[8];
-    lds_words_a2<8>(blk + 2, q);
+    uint32_t q[4];
+    lds_words_a2<4>(blk + 2 + 16 * hf, q);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] ^= 0x80808080u;
+    for (int i = 0; i < 4; ++i) q[i] ^= 0x80808080u;
     bytes_to_h2(q, d, 128.f, 0.f, h);
   }
 };
 
 template <> struct TcDeq<kQ1_0> {
-  static FRC_DEVICE_INLINE void slice(const uint8_t* row, int e0, uint32_t (&h)[16]) {
+  static FRC_DEVICE_INLINE void half(const uint8_t* row, int e0, int hf, uint32_t (&h)[8]) {
     const uint8_t* blk = row + 18 * (e0 >> 7);
     const float d = half_bits_to_float(ld_u16(blk));
-    const uint32_t bits = ld_u16(blk + 2 + ((e0 & 127) >> 3)) | (ld_u16(blk + 4 + ((e0 & 127) >> 3)) << 16);
+    const uint32_t bits = ld_u16(blk + 2 + ((e0 & 127) >> 3) + 2 * hf);
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
+    for (int i = 0; i < 8; ++i)
       h[i] = pack_h2((bits >> (2 * i)) & 1u ? d : -d, (bits >> (2 * i + 1)) & 1u ? d : -d);
   }
 };
-
 
 // Shared memory: barriers and the TMEM address (1 KB), then the A, B and raw
 // rings, every stage 1024-byte aligned.
@@ -232,7 +227,7 @@ constexpr int kTcHeader = 1024;
 static_assert(sizeof(TcSmem) <= kTcHeader, "header");
 
 __host__ __device__ constexpr int tc_smem_bytes(int raw_stride) {
-  return kTcHeader + kTcAStages * kTcTileBytes + kTcBStages * kTcTileBytes + kTcRawStages * raw_stride;
+  return kTcHeader + kTcAStages * kTcATile + kTcBStages * kTcBTile + kTcRawStages * raw_stride;
 }
 
 template <int Q>
@@ -244,8 +239,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint8_t* smem = tc_smem;
   TcSmem* sh = reinterpret_cast<TcSmem*>(smem);
   uint8_t* a_ring = smem + kTcHeader;
-  uint8_t* b_ring = a_ring + kTcAStages * kTcTileBytes;
-  uint8_t* raw_ring = b_ring + kTcBStages * kTcTileBytes;
+  uint8_t* b_ring = a_ring + kTcAStages * kTcATile;
+  uint8_t* raw_ring = b_ring + kTcBStages * kTcBTile;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (smem_u32(smem) & 1023u) {  // swizzled tiles need 1024-byte aligned stages
     if (threadIdx.x == 0) atomicOr(p.status, kStatusSmemMisaligned);
@@ -255,6 +250,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kTcM;
   const int tok0 = blockIdx.y * kTcN;
   const int nslice = p.k / kTcK;
+  const int nhalf = p.seq - tok0 > kTcNH ? 2 : 1;  // 256-token halves holding tokens
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcRawStages; ++s) {
@@ -323,8 +319,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           atomicOr(p.status, kStatusEmptyWaitTimeout);
           break;
         }
-        mbar_arrive_expect_tx(&sh->b_full[b], kTcTileBytes);
-        tma_load_2d(b_ring + b * kTcTileBytes, &xmap, s * kTcK, tok0, &sh->b_full[b]);
+        mbar_arrive_expect_tx(&sh->b_full[b], nhalf * kTcBHalf);
+        for (int nh = 0; nh < nhalf; ++nh)
+          tma_load_2d(b_ring + b * kTcBTile + nh * kTcBHalf, &xmap, s * kTcK, tok0 + nh * kTcNH, &sh->b_full[b]);
         ++issued;
       }
       for (int s = issued > kTcBStages ? issued - kTcBStages : 0; s < issued; ++s) {
@@ -345,13 +342,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(a_ring + a * kTcTileBytes), b_addr = smem_u32(b_ring + b * kTcTileBytes);
-#pragma unroll
-        for (int mi = 0; mi < 2; ++mi)
+        const uint32_t a_addr = smem_u32(a_ring + a * kTcATile), b_addr = smem_u32(b_ring + b * kTcBTile);
+        for (int nh = 0; nh < nhalf; ++nh)
 #pragma unroll
           for (int kk = 0; kk < kTcK / 16; ++kk)
-            umma_f16(tmem + mi * kTcN, umma_desc_sw64(a_addr + mi * 128 * 64 + kk * 32),
-                     umma_desc_sw64(b_addr + kk * 32), (s > 0 || kk > 0) ? 1u : 0u);
+            umma_f16(tmem + nh * kTcNH, umma_desc_sw64(a_addr + kk * 32), umma_desc_sw64(b_addr + nh * kTcBHalf + kk * 32),
+                     (s > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&sh->a_empty[a]);
         umma_commit(&sh->b_empty[b]);
       }
@@ -364,7 +360,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     // ---- dequantisation into the swizzled fp16 A stages ----------------------------
-    const int L = threadIdx.x - 3 * 32;  // this thread's tile row, 0 .. 255
+    const int L = (threadIdx.x - 3 * 32) >> 1;  // this thread's tile row, 0 .. 127
+    const int hf = threadIdx.x & 1;               // and its half of each slice
     const int64_t q = row0 + (static_cast<int64_t>(L & (p.R - 1)) << p.logG) + (L >> p.logR);
     const int slot = (L >> p.logR) * p.JS + (L & (p.R - 1)) * p.W;
     const uint32_t qmis = static_cast<uint32_t>((static_cast<uint64_t>(q) * p.row_bytes) & 15u);
@@ -383,14 +380,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       const uint8_t* raw = raw_ring + static_cast<size_t>(rs) * p.raw_stride;
       const uint32_t chmis = static_cast<uint32_t>((static_cast<uint64_t>(c) * p.chunk_bytes) & 15u);
-      uint32_t h[16];
-      TcDeq<Q>::slice(raw + slot + ((qmis + chmis) & 15u), (s % SPC) * kTcK, h);
+      uint32_t h[8];
+      TcDeq<Q>::half(raw + slot + ((qmis + chmis) & 15u), (s % SPC) * kTcK, hf, h);
       // 64-byte swizzle: 16-byte chunk index ^= (row / 2) % 4 within 512-byte atoms
-      uint8_t* line = a_ring + a * kTcTileBytes + L * 64;
+      uint8_t* line = a_ring + a * kTcATile + L * 64;
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch)
-        *reinterpret_cast<uint4*>(line + ((ch ^ swz) << 4)) =
-            make_uint4(h[4 * ch], h[4 * ch + 1], h[4 * ch + 2], h[4 * ch + 3]);
+      for (int j = 0; j < 2; ++j)
+        *reinterpret_cast<uint4*>(line + (((2 * hf + j) ^ swz) << 4)) =
+            make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -403,19 +400,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (ok) {
       tc_fence_after();
       const int quad = warp & 3;           // TMEM lanes 32*quad .. +31
-      const int half = (warp - 3) >> 2;    // tokens [128*half, 128*half + 128)
+      const int nh = (warp - 3) >> 2;      // tokens [256*nh, 256*nh + 256)
+      const int L = quad * 32 + lane;
+      const int64_t q = row0 + (static_cast<int64_t>(L & (p.R - 1)) << p.logG) + (L >> p.logR);
+      if (nh < nhalf) {
 #pragma unroll 1
-      for (int mi = 0; mi < 2; ++mi) {
-        const int L = mi * 128 + quad * 32 + lane;
-        const int64_t q = row0 + (static_cast<int64_t>(L & (p.R - 1)) << p.logG) + (L >> p.logR);
-#pragma unroll 1
-        for (int cb = 0; cb < 128; cb += 16) {
+        for (int cb = 0; cb < kTcNH; cb += 16) {
           float v[16];
-          tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + mi * kTcN + half * 128 + cb, v);
+          tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + nh * kTcNH + cb, v);
           if (q < p.n && !*abort) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              const int t = tok0 + half * 128 + cb + i;
+              const int t = tok0 + nh * kTcNH + cb + i;
               if (t < p.seq) p.y[static_cast<int64_t>(t) * p.n + q] = v[i];
             }
           }

@@ -407,7 +407,7 @@ inline cudaError_t launch_mma(const GemvRequest& r) {
 inline int64_t tc_scratch_bytes(int64_t k, int64_t seq) { return seq * k * 2; }
 
 // Tensor-core prefill (seq > 16): x -> fp16 pre-pass, then one CTA per
-// 256-row x 256-token tile.  cudaErrorNotSupported when the shape does not
+// 128-row x 512-token tile.  cudaErrorNotSupported when the shape does not
 // fit this kernel (the caller then runs 16-column chunks).
 template <int Q>
 inline cudaError_t launch_gemm_tc(const GemvRequest& r) {
@@ -456,7 +456,7 @@ inline cudaError_t launch_gemm_tc(const GemvRequest& r) {
   {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(r.k), static_cast<cuuint64_t>(r.batch)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(r.k) * 2};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTcK), static_cast<cuuint32_t>(kTcN)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTcK), static_cast<cuuint32_t>(kTcNH)};
     const cuuint32_t estr[2] = {1, 1};
     if (encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, r.xrec, dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
