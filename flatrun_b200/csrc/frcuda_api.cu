@@ -244,7 +244,8 @@ int gemv_device(DeviceState* ds, int quant, const uint8_t* w, int64_t n, int64_t
     r.stream = stream;
     r.device = ds->device;
     r.sms = ds->sms;
-    int rc = record_scratch(ds, static_cast<size_t>(frc::tc_scratch_bytes(k, seq)), &r.xrec);
+    r.tc_splits = frc::tc_split_count(quant, n, k, seq, ds->sms);
+    int rc = record_scratch(ds, static_cast<size_t>(frc::tc_scratch_bytes(k, n, seq, r.tc_splits)), &r.xrec);
     if (rc != FRC_OK) return rc;
     cudaError_t e;
     switch (quant) {

@@ -54,6 +54,7 @@ struct TcParams {
   int nchunk;         // raw chunks per row
   int G, W, R, logG, logR, JS;  // raw tile geometry (as in the batched GEMV)
   int raw_stride;     // bytes of one raw stage (G * JS rounded)
+  float* ws;          // split-k partials (gridDim.z, seq, n) when gridDim.z > 1
   uint32_t* status;
 };
 
@@ -250,6 +251,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kTcM;
   const int tok0 = blockIdx.y * kTcN;
   const int nslice = p.k / kTcK;
+  // split-k: this CTA's raw chunks [c_begin, c_begin + ncl) and slices
+  // [s_begin, s_begin + nsl); positions inside the rings count from there
+  const int c_begin = static_cast<int>(static_cast<int64_t>(blockIdx.z) * p.nchunk / gridDim.z);
+  const int ncl = static_cast<int>(static_cast<int64_t>(blockIdx.z + 1) * p.nchunk / gridDim.z) - c_begin;
+  const int s_begin = c_begin * SPC;
+  const int nsl = min((c_begin + ncl) * SPC, nslice) - s_begin;
   const int nhalf = p.seq - tok0 > kTcNH ? 2 : 1;  // 256-token halves holding tokens
 
   if (threadIdx.x == 0) {
@@ -285,9 +292,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       const uint32_t tx = static_cast<uint32_t>(p.G * p.R * p.W);
       const int ty = static_cast<int>(row0 >> p.logG);
-      uint64_t choff = 0;
+      uint64_t choff = static_cast<uint64_t>(c_begin) * p.chunk_bytes;
       int issued = 0;
-      for (int c = 0; c < p.nchunk; ++c, choff += p.chunk_bytes) {
+      for (int c = 0; c < ncl; ++c, choff += p.chunk_bytes) {
         const int s = c % kTcRawStages;
         if (c >= kTcRawStages &&
             !wait_phase(&sh->raw_empty[s], (static_cast<uint32_t>(c / kTcRawStages) & 1u) ^ 1u, abort)) {
@@ -312,7 +319,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---- fp16 activations -----------------------------------------------------
     if (lane == 0) {
       int issued = 0;
-      for (int s = 0; s < nslice; ++s) {
+      for (int s = 0; s < nsl; ++s) {
         const int b = s % kTcBStages;
         if (s >= kTcBStages &&
             !wait_phase(&sh->b_empty[b], (static_cast<uint32_t>(s / kTcBStages) & 1u) ^ 1u, abort)) {
@@ -321,7 +328,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         mbar_arrive_expect_tx(&sh->b_full[b], nhalf * kTcBHalf);
         for (int nh = 0; nh < nhalf; ++nh)
-          tma_load_2d(b_ring + b * kTcBTile + nh * kTcBHalf, &xmap, s * kTcK, tok0 + nh * kTcNH, &sh->b_full[b]);
+          tma_load_2d(b_ring + b * kTcBTile + nh * kTcBHalf, &xmap, (s_begin + s) * kTcK, tok0 + nh * kTcNH,
+                      &sh->b_full[b]);
         ++issued;
       }
       for (int s = issued > kTcBStages ? issued - kTcBStages : 0; s < issued; ++s) {
@@ -334,7 +342,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---- MMA issue (one thread) ------------------------------------------------
     if (lane == 0) {
       int s = 0;
-      for (; s < nslice; ++s) {
+      for (; s < nsl; ++s) {
         const int a = s % kTcAStages, b = s % kTcBStages;
         if (!wait_phase(&sh->a_full[a], static_cast<uint32_t>(s / kTcAStages) & 1u, abort) ||
             !wait_phase(&sh->b_full[b], static_cast<uint32_t>(s / kTcBStages) & 1u, abort)) {
@@ -353,7 +361,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       // accumulators complete (or, after an abort, every issued MMA retired);
       // this thread also waits, so no MMA is in flight at the teardown
-      uint64_t* done = s == nslice ? &sh->acc_full : &sh->drain;
+      uint64_t* done = s == nsl ? &sh->acc_full : &sh->drain;
       umma_commit(done);
       int zero = 0;
       if (!wait_phase(done, 0u, &zero)) atomicOr(p.status, kStatusDrainTimeout);
@@ -367,7 +375,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t qmis = static_cast<uint32_t>((static_cast<uint64_t>(q) * p.row_bytes) & 15u);
     const int swz = (L >> 1) & 3;
     bool ok = true;
-    for (int s = 0; s < nslice && ok; ++s) {
+    for (int s = 0; s < nsl && ok; ++s) {
       const int c = s / SPC, a = s % kTcAStages, rs = c % kTcRawStages;
       if (s % SPC == 0)
         ok = __all_sync(0xffffffffu, wait_phase(&sh->raw_full[rs], static_cast<uint32_t>(c / kTcRawStages) & 1u, abort));
@@ -379,7 +387,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       }
       const uint8_t* raw = raw_ring + static_cast<size_t>(rs) * p.raw_stride;
-      const uint32_t chmis = static_cast<uint32_t>((static_cast<uint64_t>(c) * p.chunk_bytes) & 15u);
+      const uint32_t chmis = static_cast<uint32_t>((static_cast<uint64_t>(c_begin + c) * p.chunk_bytes) & 15u);
       uint32_t h[8];
       TcDeq<Q>::half(raw + slot + ((qmis + chmis) & 15u), (s % SPC) * kTcK, hf, h);
       // 64-byte swizzle: 16-byte chunk index ^= (row / 2) % 4 within 512-byte atoms
@@ -392,7 +400,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&sh->a_full[a]);
-        if (s % SPC == SPC - 1 || s == nslice - 1) mbar_arrive(&sh->raw_empty[rs]);
+        if (s % SPC == SPC - 1 || s == nsl - 1) mbar_arrive(&sh->raw_empty[rs]);
       }
     }
     // ---- epilogue: TMEM -> y -------------------------------------------------------
@@ -403,6 +411,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int nh = (warp - 3) >> 2;      // tokens [256*nh, 256*nh + 256)
       const int L = quad * 32 + lane;
       const int64_t q = row0 + (static_cast<int64_t>(L & (p.R - 1)) << p.logG) + (L >> p.logR);
+      float* out = gridDim.z > 1 ? p.ws + static_cast<int64_t>(blockIdx.z) * p.seq * p.n : p.y;
       if (nh < nhalf) {
 #pragma unroll 1
         for (int cb = 0; cb < kTcNH; cb += 16) {
@@ -412,7 +421,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int t = tok0 + nh * kTcNH + cb + i;
-              if (t < p.seq) p.y[static_cast<int64_t>(t) * p.n + q] = v[i];
+              if (t < p.seq) out[static_cast<int64_t>(t) * p.n + q] = v[i];
             }
           }
         }
@@ -427,6 +436,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 2) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+  }
+}
+
+// y = sum of the split-k partials, in split order (deterministic).
+static __global__ void __launch_bounds__(256) tc_reduce(const float* __restrict__ ws, int splits, int64_t count,
+                                                      float* __restrict__ y) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count; i += stride) {
+    float v = ws[i];
+    for (int z = 1; z < splits; ++z) v += ws[z * count + i];
+    y[i] = v;
   }
 }
 

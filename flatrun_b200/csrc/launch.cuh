@@ -38,8 +38,10 @@ struct GemvRequest {
   int64_t mat_n[4];
   // batch 2..16: activation records of the tensor-core kernel (at least
   // mma_scratch_bytes(k, batch) bytes, 256-byte aligned); null selects the
-  // fp32 CUDA-core kernel
+  // fp32 CUDA-core kernel.  Prefill (batch > 16): fp16 x and split-k
+  // partials (tc_scratch_bytes(k, n, batch, tc_splits) bytes)
   uint8_t* xrec;
+  int tc_splits;  // prefill k-splits (>= 1)
 };
 
 struct DequantRequest {
@@ -403,8 +405,27 @@ inline cudaError_t launch_mma(const GemvRequest& r) {
   return launch_mma_ng<Q, 4>(p, r);
 }
 
-// Bytes of fp16 activations the tensor-core prefill stages.
-inline int64_t tc_scratch_bytes(int64_t k, int64_t seq) { return seq * k * 2; }
+// Raw-chunk elements of the prefill GEMM per format (TcRaw<Q>::K).
+inline int tc_raw_k(int quant) { return quant == kQ8_0 ? 128 : 256; }
+
+// k-splits of a prefill: enough CTAs to fill the SMs when the (row, token)
+// tiles alone do not (at most 16, at least one raw chunk per split);
+// FRC_TC_SPLIT overrides.
+inline int tc_split_count(int quant, int64_t n, int64_t k, int64_t seq, int sms) {
+  const int64_t tiles = ((n + kTcM - 1) / kTcM) * ((seq + kTcN - 1) / kTcN);
+  const int64_t nchunk = (k + tc_raw_k(quant) - 1) / tc_raw_k(quant);
+  int64_t s = env_int("FRC_TC_SPLIT", 0);
+  if (s <= 0) s = tiles >= sms ? 1 : sms / tiles;
+  if (s > 16) s = 16;
+  if (s > nchunk) s = nchunk;
+  return s < 1 ? 1 : static_cast<int>(s);
+}
+
+// Bytes of prefill scratch: fp16 x, then (split-k only) fp32 partials.
+inline int64_t tc_x16_bytes(int64_t k, int64_t seq) { return (seq * k * 2 + 255) / 256 * 256; }
+inline int64_t tc_scratch_bytes(int64_t k, int64_t n, int64_t seq, int splits) {
+  return tc_x16_bytes(k, seq) + (splits > 1 ? static_cast<int64_t>(splits) * seq * n * 4 : 0);
+}
 
 // Tensor-core prefill (seq > 16): x -> fp16 pre-pass, then one CTA per
 // 128-row x 512-token tile.  cudaErrorNotSupported when the shape does not
@@ -422,8 +443,10 @@ inline cudaError_t launch_gemm_tc(const GemvRequest& r) {
   p.chunk_bytes = RAWK / F::QK * F::TS;
   p.nchunk = (r.k + RAWK - 1) / RAWK;
   p.status = r.status;
+  const int splits = r.tc_splits < 1 ? 1 : r.tc_splits;
+  p.ws = splits > 1 ? reinterpret_cast<float*>(r.xrec + tc_x16_bytes(r.k, r.batch)) : nullptr;
   mma_geometry(p.row_bytes, p.chunk_bytes, &p.G, &p.W);
-  if (r.n % p.G != 0 || r.k % kTcK != 0 || !r.xrec) return cudaErrorNotSupported;
+  if (r.n % p.G != 0 || r.k % kTcK != 0 || !r.xrec || splits > p.nchunk) return cudaErrorNotSupported;
   p.R = kTcM / p.G;
   p.logG = 0;
   while ((1 << p.logG) < p.G) ++p.logG;
@@ -468,8 +491,15 @@ inline cudaError_t launch_gemm_tc(const GemvRequest& r) {
                                                                                        reinterpret_cast<__half*>(r.xrec));
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const dim3 grid(static_cast<unsigned>((r.n + kTcM - 1) / kTcM), static_cast<unsigned>((r.batch + kTcN - 1) / kTcN));
+  const dim3 grid(static_cast<unsigned>((r.n + kTcM - 1) / kTcM), static_cast<unsigned>((r.batch + kTcN - 1) / kTcN),
+                  static_cast<unsigned>(splits));
   gemm_tc<Q><<<grid, kTcThreads, smem, r.stream>>>(wmap, xmap, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || splits == 1) return e;
+  const int64_t ycount = static_cast<int64_t>(r.batch) * r.n;
+  int64_t blocks = (ycount + 255) / 256;
+  if (blocks > static_cast<int64_t>(r.sms) * 8) blocks = static_cast<int64_t>(r.sms) * 8;
+  tc_reduce<<<static_cast<unsigned>(blocks), 256, 0, r.stream>>>(p.ws, splits, ycount, r.y);
   return cudaGetLastError();
 }
 

@@ -209,6 +209,23 @@ def test_prefill_tensor_core_all_formats(cuda_backend, fmt, n, k, seq):
 
 
 @pytest.mark.parametrize("fmt", FMTS)
+@pytest.mark.parametrize("splits", ["1", "3"])
+def test_prefill_forced_k_splits(cuda_backend, fmt, splits, monkeypatch):
+    """The prefill GEMM with k split into a given number of ranges (partials
+    summed by the reduce kernel) and unsplit: both within the fp16 bounds."""
+    monkeypatch.setenv("FRC_TC_SPLIT", splits)
+    qk, _ = O.FORMATS[fmt]
+    n, k, seq = 300, 1024, 40
+    raw = synth.make_weight(fmt, n, k, seed=4200)
+    x = synth.make_x(k, batch=seq, seed=4201)
+    y = cuda_backend.weight(raw, n, k, fmt).matmul(x)
+    ref = O.matvec_fp64(fmt, raw, x, n, k)
+    assert O.rel_err(y, ref) < GATE
+    assert O.norm_err(y, ref, O.term_scale(fmt, raw, x, n, k)) < TOL_TC_NORM
+    cuda_backend.close()
+
+
+@pytest.mark.parametrize("fmt", FMTS)
 def test_batched_exact_fp32_kernel(cuda_backend, fmt, monkeypatch):
     """FRC_FORCE_XB=1 selects the batched kernel that keeps activations in
     fp32 (CUDA cores); held to the fp32 tolerance."""
