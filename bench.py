@@ -379,8 +379,14 @@ def main() -> None:
             order[-1][1].append(i)
         for gname, idx in order:
             local = sum(mats[i][2] for i in idx) * batch
-            groups.append((idx[-1], torch.empty(local, device="cuda"), torch.empty(local * world, device="cuda"),
-                           idx))
+            sendbuf = torch.empty(local, device="cuda")
+            # the projections write their y shards straight into the send buffer
+            off = 0
+            for j in idx:
+                sz = mats[j][2] * batch
+                ys_dev[j] = sendbuf[off:off + sz].view(batch, mats[j][2])
+                off += sz
+            groups.append((idx[-1], sendbuf, torch.empty(local * world, device="cuda"), idx))
 
     stream = torch.cuda.Stream()
 
@@ -414,11 +420,6 @@ def main() -> None:
             i = g[-1]
             for last, sendbuf, recvbuf, idx in groups:
                 if only is None and last == i:
-                    off = 0
-                    for j in idx:
-                        sz = mats[j][2] * batch
-                        sendbuf[off:off + sz].copy_(ys_dev[j].view(-1))
-                        off += sz
                     dist.all_gather_into_tensor(recvbuf, sendbuf)
 
     K = args.steps
