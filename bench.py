@@ -257,6 +257,8 @@ def main() -> None:
     ap.add_argument("--copies", type=int, default=0, help="distinct weight copies rotated (0 = auto, > 3x L2)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--nccl-gather", action="store_true",
+                    help="N > 1: assemble row shards with NCCL all-gathers instead of the gather fused into the GEMV")
     ap.add_argument("--unfused", action="store_true",
                     help="one launch per projection, each with its own x (no shared-x fusion)")
     args = ap.parse_args()
@@ -412,9 +414,38 @@ def main() -> None:
         if rc:
             _lib.check(rc, lib)
 
+    # N > 1, batch 1: the all-gather fused into the GEMV (each rank's GEMV
+    # stores its rows into every rank's gathered buffer over NVLink, then a
+    # bounded wait), where the launch group is exactly one gather group
+    fused = {}
+    if world > 1 and batch == 1 and not args.nccl_gather:
+        from flatrun_b200.shard import FusedGather
+        for last, sendbuf, recvbuf, idx in groups:
+            if idx in lgroups:
+                fused[tuple(idx)] = (FusedGather(lib, world, rank, sendbuf.numel()), sendbuf)
+
+    # each fused launch waits (before reading x) for the previous group's
+    # gather, as the forwarder's next projection consumes it; the chain runs
+    # across steps (q+k+v waits for the previous step's down)
+    chain = {"prev": None}
+
+    def fused_group(g: list, step: int) -> bool:
+        fg, sendbuf = fused[tuple(g)]
+        w = [pools[i][0].data_ptr() + (step % pools[i][2]) * pools[i][1] for i in g]
+        rc = fg.gemv(qid[g[0]], w, [mbytes[i] for i in g], [mats[i][2] for i in g], mats[g[0]][3],
+                     xs_dev[g[0]].data_ptr(), [ys_dev[i].data_ptr() for i in g], sendbuf.data_ptr(),
+                     stream.cuda_stream, wait_for=chain["prev"])
+        if rc == _lib.FRC_ERR_UNSUPPORTED:
+            return False
+        _lib.check(rc, lib)
+        chain["prev"] = fg
+        return True
+
     def launch(step: int, only=None) -> None:
         for g in lgroups:
             if only is not None and g[0] not in only:
+                continue
+            if only is None and tuple(g) in fused and fused_group(g, step):
                 continue
             gemv_group(g, step)
             i = g[-1]
@@ -453,9 +484,15 @@ def main() -> None:
             launch(s)
     torch.cuda.synchronize()
     graphs = capture()
-    # soak: replay untimed for ~1 s so clocks settle and the sampler sees load
-    t_soak = time.perf_counter()
-    while time.perf_counter() - t_soak < 1.0:
+    # soak: replay untimed for ~1 s so clocks settle and the sampler sees load;
+    # every rank replays the same number of times (the graphs hold collective
+    # steps), agreed on from the first replay
+    n_soak = max(1, int(np.ceil(1000.0 / max(replay_ms(graphs), 1e-3))))
+    if world > 1:
+        t = torch.tensor([n_soak], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        n_soak = int(t.item())
+    for _ in range(n_soak - 1):
         replay_ms(graphs)
 
     if world > 1:
@@ -559,6 +596,9 @@ def main() -> None:
             "config": {"workload": wl["desc"], "global_batch": (batch if batch <= 16 else 1) * world,
                        "seq_len": 1 if batch <= 16 else batch,
                        "parallelism": f"row-shard x{world}" if world > 1 else "single GPU",
+                       "gather": ("fused into the GEMV: stores to every rank over NVLink; the next GEMV waits for "
+                                  "every rank's flag before reading x" if fused else "NCCL all_gather_into_tensor")
+                                 if world > 1 else None,
                        "weight_bytes_per_step": wbytes, "algorithmic_bytes_per_step": step_bytes,
                        "weight_copies_rotated": [p[2] for p in pools],
                        "l2": f"inputs larger than L2: each projection rotates over distinct device copies "
@@ -578,6 +618,10 @@ def main() -> None:
     del graphs, pools
     if world > 1:
         import torch.distributed as dist
+        torch.cuda.synchronize()
+        dist.barrier()
+        for fg, _ in fused.values():
+            fg.close()
         dist.barrier()
         dist.destroy_process_group()
     be.close()

@@ -41,6 +41,15 @@ SIGNATURES: dict[str, list] = {
     "frc_device_status": [_i, ctypes.POINTER(ctypes.c_uint32)],
     "frc_gemv": [_i, _p, _sz, _i64, _i64, _p, _i64, _p, _p],
     "frc_gemv_noalloc": [_i, _p, _sz, _i64, _i64, _p, _i64, _p, _p],
+    "frc_ipc_alloc": [_sz, ctypes.POINTER(_p), _p],
+    "frc_ipc_open": [_p, ctypes.POINTER(_p)],
+    "frc_ipc_close": [_p],
+    "frc_ipc_free": [_p],
+    "frc_gather_create": [_i, _i, ctypes.POINTER(_p), ctypes.POINTER(_p), ctypes.POINTER(_p)],
+    "frc_gather_free": [_p],
+    "frc_gemv_gather": [_i, _i, ctypes.POINTER(_p), ctypes.POINTER(_sz), ctypes.POINTER(_i64), _i64, _p,
+                        ctypes.POINTER(_p), _p, _p, _p, _p],
+    "frc_gather_wait": [_p, _p],
     "frc_dequant_dev": [_i, _p, _sz, _i64, _p, _p],
     "frc_gemv_multi": [_i, _i, ctypes.POINTER(_p), ctypes.POINTER(_sz), ctypes.POINTER(_i64), _i64, _p, _i64,
                        ctypes.POINTER(_p), _p],

@@ -17,6 +17,7 @@ enum : uint32_t {
   kStatusEmptyWaitTimeout = 1u << 1,  // the producer gave up waiting for a free stage
   kStatusDrainTimeout     = 1u << 2,  // the producer gave up draining its copies
   kStatusSmemMisaligned   = 1u << 3,  // dynamic shared memory not 128-byte aligned (kernel skipped)
+  kStatusGatherTimeout    = 1u << 4,  // a fused all-gather wait gave up on a rank's flag
 };
 
 // Upper bound on polls of one mbarrier phase.  Each poll is a try_wait with

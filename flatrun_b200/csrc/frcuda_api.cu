@@ -37,6 +37,13 @@ extern template cudaError_t launch_gemm_tc<kQ6_K>(const GemvRequest&);
 extern template cudaError_t launch_gemm_tc<kQ1_0>(const GemvRequest&);
 }  // namespace frc
 
+struct frc_gather {
+  int world = 0, rank = 0, device = 0;
+  float* shard_dst[frc::kMaxGatherRanks] = {};   // rank r's gathered buffer at this rank's shard
+  uint32_t* flags[frc::kMaxGatherRanks] = {};    // rank r's flag array (one word per rank)
+  uint32_t* counters = nullptr;                  // [0] slots finished, [1] epoch (this device)
+};
+
 struct frc_weight {
   int device;
   int quant;
@@ -731,5 +738,146 @@ FRC_MIRROR(q8_0, FRC_Q8_0, true)
 FRC_MIRROR(q6_k, FRC_Q6_K, true)
 FRC_MIRROR(q5_k, FRC_Q5_K, false)
 FRC_MIRROR(q1_0, FRC_Q1_0, false)
+
+// ---- fused all-gather across GPUs --------------------------------------------
+
+int frc_ipc_alloc(size_t bytes, void** dev_ptr, void* handle) {
+  if (!dev_ptr || !handle || bytes == 0) return fail(FRC_ERR_INVALID, "frc_ipc_alloc: null argument or zero size");
+  *dev_ptr = nullptr;
+  void* p = nullptr;
+  FRC_CUDA(cudaMalloc(&p, bytes), "cudaMalloc(shared buffer)");
+  cudaError_t e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "cudaIpcGetMemHandle");
+  }
+  *dev_ptr = p;
+  return FRC_OK;
+}
+
+int frc_ipc_open(const void* handle, void** dev_ptr) {
+  if (!dev_ptr || !handle) return fail(FRC_ERR_INVALID, "frc_ipc_open: null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof h);
+  FRC_CUDA(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+  return FRC_OK;
+}
+
+int frc_ipc_close(void* dev_ptr) {
+  FRC_CUDA(cudaIpcCloseMemHandle(dev_ptr), "cudaIpcCloseMemHandle");
+  return FRC_OK;
+}
+
+int frc_ipc_free(void* dev_ptr) {
+  FRC_CUDA(cudaFree(dev_ptr), "cudaFree(shared buffer)");
+  return FRC_OK;
+}
+
+int frc_gather_create(int world, int rank, void* const* shard_dst, void* const* flags, frc_gather** out) {
+  if (!out || !shard_dst || !flags) return fail(FRC_ERR_INVALID, "frc_gather_create: null argument");
+  *out = nullptr;
+  if (world < 2 || world > frc::kMaxGatherRanks || rank < 0 || rank >= world)
+    return fail(FRC_ERR_INVALID, "frc_gather_create: world must be 2..%d and 0 <= rank < world", frc::kMaxGatherRanks);
+  for (int r = 0; r < world; ++r)
+    if (!shard_dst[r] || !flags[r] || !aligned(shard_dst[r], 4) || !aligned(flags[r], 4))
+      return fail(FRC_ERR_INVALID, "frc_gather_create: rank %d pointers null or misaligned", r);
+  DeviceState* ds;
+  int rc = current_device_state(&ds);
+  if (rc) return rc;
+  auto g = std::make_unique<frc_gather>();
+  g->world = world;
+  g->rank = rank;
+  g->device = ds->device;
+  for (int r = 0; r < world; ++r) {
+    g->shard_dst[r] = static_cast<float*>(shard_dst[r]);
+    g->flags[r] = static_cast<uint32_t*>(flags[r]);
+  }
+  FRC_CUDA(cudaMalloc(&g->counters, 2 * sizeof(uint32_t)), "cudaMalloc(gather counters)");
+  FRC_CUDA(cudaMemset(g->counters, 0, 2 * sizeof(uint32_t)), "cudaMemset(gather counters)");
+  *out = g.release();
+  return FRC_OK;
+}
+
+int frc_gather_free(frc_gather* g) {
+  if (!g) return FRC_OK;
+  DeviceGuard guard;
+  FRC_CUDA(guard.set(g->device), "cudaSetDevice");
+  if (g->counters) cudaFree(g->counters);
+  delete g;
+  return FRC_OK;
+}
+
+int frc_gemv_gather(int quant, int count, const void* const* w_dev, const size_t* w_bytes, const int64_t* n,
+                    int64_t k, const float* x_dev, float* const* y_dev, const float* y_base, frc_gather* g,
+                    const frc_gather* wait_for, void* stream) {
+  if (!g) return fail(FRC_ERR_INVALID, "frc_gemv_gather: null gather");
+  if (count < 1 || count > 4) return fail(FRC_ERR_INVALID, "frc_gemv_gather: count must be 1..4 (got %d)", count);
+  if (!w_dev || !w_bytes || !n || !y_dev || !y_base) return fail(FRC_ERR_INVALID, "null array");
+  int64_t total = 0;
+  for (int m = 0; m < count; ++m) {
+    int rc = check_matmul(quant, w_bytes[m], n[m], k, 1);
+    if (rc) return rc;
+    if ((w_bytes[m] && !w_dev[m]) || (n[m] && !y_dev[m])) return fail(FRC_ERR_INVALID, "null buffer");
+    if (!aligned(w_dev[m], 16)) return fail(FRC_ERR_INVALID, "frc_gemv_gather: weight %d must be 16-byte aligned", m);
+    if (!aligned(y_dev[m], 4) || y_dev[m] < y_base)
+      return fail(FRC_ERR_INVALID, "frc_gemv_gather: y %d must be 4-byte aligned and at or above y_base", m);
+    total += n[m];
+  }
+  if ((k && !x_dev) || !aligned(x_dev, 16)) return fail(FRC_ERR_INVALID, "frc_gemv_gather: x must be 16-byte aligned");
+  if (k == 0 || total == 0) return fail(FRC_ERR_UNSUPPORTED, "frc_gemv_gather: empty shapes are not gathered");
+  DeviceState* ds;
+  int rc = current_device_state(&ds);
+  if (rc) return rc;
+  if (ds->device != g->device) return fail(FRC_ERR_INVALID, "frc_gemv_gather: gather belongs to device %d", g->device);
+  frc::GemvRequest r{};
+  r.k = static_cast<int>(k);
+  r.x = x_dev;
+  r.batch = 1;
+  r.status = ds->status;
+  r.stream = static_cast<cudaStream_t>(stream);
+  r.device = ds->device;
+  r.sms = ds->sms;
+  r.nmat = count;
+  for (int m = 0; m < count; ++m) {
+    r.mat_w[m] = static_cast<const uint8_t*>(w_dev[m]);
+    r.mat_y[m] = y_dev[m];
+    r.mat_n[m] = n[m];
+  }
+  r.w = r.mat_w[0];
+  r.y = r.mat_y[0];
+  r.n = total;
+  r.g_world = g->world;
+  r.g_rank = g->rank;
+  r.g_ybase = y_base;
+  for (int i = 0; i < g->world; ++i) {
+    r.g_peer_y[i] = g->shard_dst[i];
+    r.g_flags[i] = g->flags[i];
+  }
+  r.g_done = g->counters;
+  r.g_epoch = g->counters + 1;
+  if (wait_for) {
+    if (wait_for->device != g->device || wait_for->world != g->world)
+      return fail(FRC_ERR_INVALID, "frc_gemv_gather: wait_for belongs to another device or world");
+    r.w_world = wait_for->world;
+    r.w_flags = wait_for->flags[wait_for->rank];
+    r.w_epoch = wait_for->counters + 1;
+  }
+  rc = launch_gemv_quant(quant, r);
+  if (rc == FRC_OK) return FRC_OK;
+  (void)cudaGetLastError();
+  return fail(FRC_ERR_UNSUPPORTED, "frc_gemv_gather: this shape has no fused all-gather path (%s)", g_err.c_str());
+}
+
+int frc_gather_wait(frc_gather* g, void* stream) {
+  if (!g) return fail(FRC_ERR_INVALID, "frc_gather_wait: null gather");
+  DeviceState* ds;
+  int rc = current_device_state(&ds);
+  if (rc) return rc;
+  cudaError_t e = frc::launch_gather_wait(g->flags[g->rank], g->world, g->counters + 1, ds->status,
+                                          static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gather wait launch");
+  return FRC_OK;
+}
 
 }  // extern "C"

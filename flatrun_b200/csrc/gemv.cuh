@@ -34,6 +34,7 @@ namespace frc {
 
 constexpr int kMaxConsumerWarps = 15;  // + 1 producer = 512 threads, 128 registers each
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s per wait
+constexpr int kMaxGatherRanks = 8;
 
 struct GemvParams {
   const uint8_t* w;   // raw blocks, 16-byte aligned
@@ -54,6 +55,22 @@ struct GemvParams {
   int64_t mat_end[4];
   const uint8_t* mat_w[4];  // each 16-byte aligned
   float* mat_y[4];
+  // gemv_i8 fused all-gather (g_world > 1): every y value is also stored at
+  // the same offset from g_peer_y[r] as from g_ybase, for each rank r (the
+  // rank's shard in r's gathered buffer, over NVLink for r != this rank);
+  // the last slot of the grid to finish publishes the group's next epoch in
+  // every rank's flag array (slot g_rank)
+  int g_world, g_rank;
+  const float* g_ybase;
+  float* g_peer_y[kMaxGatherRanks];
+  uint32_t* g_flags[kMaxGatherRanks];
+  uint32_t* g_done;   // slots finished in this launch (reset by the last)
+  uint32_t* g_epoch;  // gathers completed by this rank
+  // gemv_i8: before reading x, wait until every rank has published the
+  // epoch of an earlier fused gather (w_world > 1): x may be its output
+  int w_world;
+  const uint32_t* w_flags;
+  const uint32_t* w_epoch;
 };
 
 constexpr int kMaxMats = 4;
@@ -355,6 +372,40 @@ __host__ __device__ constexpr int i8_max_warps() {
 FRC_DEVICE_INLINE void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 FRC_DEVICE_INLINE void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
+// Stores one y value locally and, with a fused all-gather, into every rank's
+// gathered buffer.
+FRC_DEVICE_INLINE void put_y(const GemvParams& p, float* dst, float v) {
+  *dst = v;
+  if (p.g_world > 1) {
+    const int64_t off = dst - p.g_ybase;
+    for (int r = 0; r < p.g_world; ++r) p.g_peer_y[r][off] = v;
+  }
+}
+
+FRC_DEVICE_INLINE void st_release_sys(uint32_t* ptr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
+// Called by one thread per slot after the slot barrier that follows the
+// slot's y stores: the slot's stores are released at GPU scope before its
+// arrival; the last slot of the grid acquires them through the counter and
+// publishes the next epoch to every rank after one system-scope fence
+// (fences are cumulative, so it covers every slot's stores, remote ones
+// included).
+FRC_DEVICE_INLINE void gather_arrive(const GemvParams& p, int slots) {
+  if (p.g_world <= 1) return;
+  __threadfence();
+  const uint32_t total = gridDim.x * static_cast<uint32_t>(slots);
+  if (atomicAdd(p.g_done, 1u) + 1u == total) {
+    __threadfence();
+    __threadfence_system();
+    const uint32_t e = *reinterpret_cast<volatile uint32_t*>(p.g_epoch) + 1u;
+    for (int r = 0; r < p.g_world; ++r) st_release_sys(p.g_flags[r] + p.g_rank, e);
+    *p.g_epoch = e;
+    *p.g_done = 0u;
+  }
+}
+
 template <int Q, int UPT, int RPS>
 __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvParams p) {
   using F = Fmt<Q>;
@@ -411,6 +462,22 @@ __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvPa
   }
   griddep_wait();
   griddep_launch_dependents();
+  if (p.w_world > 1) {  // an earlier fused gather must be complete on every rank
+    if (threadIdx.x < static_cast<unsigned>(p.w_world)) {
+      const uint32_t e = *p.w_epoch;
+      const uint64_t t0 = global_ns();
+      while (true) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p.w_flags + threadIdx.x) : "memory");
+        if (static_cast<int32_t>(v - e) >= 0) break;
+        if (global_ns() - t0 > kWaitLimitNs) {
+          atomicOr(p.status, kStatusGatherTimeout);
+          break;
+        }
+      }
+    }
+    __syncthreads();
+  }
 
   {
     constexpr int NQ = I8<Q>::E / 16;
@@ -419,7 +486,10 @@ __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvPa
     quantise_units<Q, I8<Q>::UPB, F::QK>(p.x, p.units, records, P);
   }
   __syncthreads();
-  if (ntiles == 0) return;  // the whole slot leaves together
+  if (ntiles == 0) {  // the whole slot leaves together
+    if (st == leader) gather_arrive(p, slots);
+    return;
+  }
 
   UnitX<Q> xu[UPT];
   UnitCtx cx[UPT];
@@ -508,12 +578,22 @@ __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvPa
     }
     if (p.wps == 1) {
       if ((lane & (kLanesPerValue - 1)) == 0 && lane / kLanesPerValue < rows && !*abort) {
-        ym[lane / kLanesPerValue] = acc[0];
+        put_y(p, ym + lane / kLanesPerValue, acc[0]);
       }
     } else if (st < rows && !*abort) {
-      ym[st] = acc[0];
+      put_y(p, ym + st, acc[0]);
     }
     t0 = tile.t1;
+  }
+  if (p.g_world > 1) {  // publish this slot's gathered rows
+    // the leader's system fence after the slot barrier orders every thread's
+    // stores of the slot before the arrival (fences are cumulative)
+    if (p.wps == 1) {
+      __syncwarp();
+    } else {
+      named_barrier_sync(1 + slot, spt);
+    }
+    if (st == leader) gather_arrive(p, slots);
   }
 
   // on an abort, copies already issued must land before the CTA exits

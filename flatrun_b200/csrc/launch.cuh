@@ -42,6 +42,16 @@ struct GemvRequest {
   // partials (tc_scratch_bytes(k, n, batch, tc_splits) bytes)
   uint8_t* xrec;
   int tc_splits;  // prefill k-splits (>= 1)
+  // batch-1 fused all-gather (g_world > 1; see GemvParams)
+  int g_world, g_rank;
+  const float* g_ybase;
+  float* g_peer_y[kMaxGatherRanks];
+  uint32_t* g_flags[kMaxGatherRanks];
+  uint32_t* g_done;
+  uint32_t* g_epoch;
+  int w_world;  // batch-1: wait for an earlier fused gather before reading x
+  const uint32_t* w_flags;
+  const uint32_t* w_epoch;
 };
 
 struct DequantRequest {
@@ -503,6 +513,31 @@ inline cudaError_t launch_gemm_tc(const GemvRequest& r) {
   return cudaGetLastError();
 }
 
+// Bounded wait until every rank's flag in `flags` has reached this rank's
+// epoch for the group (the epoch its last fused GEMV published).
+static __global__ void __launch_bounds__(32) gather_wait_kernel(const uint32_t* flags, int world,
+                                                               const uint32_t* epoch, uint32_t* status) {
+  const int r = threadIdx.x;
+  if (r >= world) return;
+  const uint32_t e = *epoch;
+  const uint64_t t0 = global_ns();
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
+    if (static_cast<int32_t>(v - e) >= 0) break;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      atomicOr(status, kStatusGatherTimeout);
+      break;
+    }
+  }
+}
+
+inline cudaError_t launch_gather_wait(const uint32_t* flags, int world, const uint32_t* epoch, uint32_t* status,
+                                      cudaStream_t stream) {
+  gather_wait_kernel<<<1, 32, 0, stream>>>(flags, world, epoch, status);
+  return cudaGetLastError();
+}
+
 // Largest tile footprint must fit in shared memory with two stages.
 template <int Q>
 inline bool tiles_fit(int row_bytes) {
@@ -539,6 +574,22 @@ cudaError_t launch_gemv(const GemvRequest& r) {
     p.mat_y[0] = r.y;
   }
   if (!tiles_fit<Q>(p.row_bytes)) return cudaErrorInvalidValue;
+  if (r.g_world > 1) {
+    p.g_world = r.g_world;
+    p.g_rank = r.g_rank;
+    p.g_ybase = r.g_ybase;
+    for (int i = 0; i < r.g_world; ++i) {
+      p.g_peer_y[i] = r.g_peer_y[i];
+      p.g_flags[i] = r.g_flags[i];
+    }
+    p.g_done = r.g_done;
+    p.g_epoch = r.g_epoch;
+  }
+  if (r.w_world > 1) {
+    p.w_world = r.w_world;
+    p.w_flags = r.w_flags;
+    p.w_epoch = r.w_epoch;
+  }
   constexpr int E = 16 * F::NRUN;
   const bool force_xb = env_int("FRC_FORCE_XB", 0) != 0;
   if (r.batch == 1 && !force_xb && env_int("FRC_GEMV_FP32", 0) == 0) {
@@ -563,7 +614,9 @@ cudaError_t launch_gemv(const GemvRequest& r) {
     if (units <= 64 * i8_max_warps<Q, 2>()) return launch_i8<Q, 2>(p, r);
     p.units = (r.k / F::QK) * F::UPB;
   }
-  if (r.nmat > 1) return cudaErrorNotSupported;  // callers fall back to one launch per matrix
+  // the fused multi-matrix launch and the fused all-gather exist only in the
+  // batch-1 integer kernel: callers fall back (per matrix / NCCL)
+  if (r.nmat > 1 || r.g_world > 1 || r.w_world > 1) return cudaErrorNotSupported;
   if (r.batch > 1 && r.xrec && !force_xb && env_int("FRC_GEMV_FP32", 0) == 0) return launch_mma<Q>(r);
   if (r.batch == 1 && !force_xb) {
     const int cap1 = 32 * kMaxConsumerWarps;

@@ -127,6 +127,41 @@ int frc_gemv_noalloc(int quant, const void* w_dev, size_t w_bytes, int64_t n, in
  * reference dispatches one projection per call, flatrun/model/qwen2.py:1510-1519.) */
 int frc_gemv_multi(int quant, int count, const void* const* w_dev, const size_t* w_bytes, const int64_t* n,
                    int64_t k, const float* x_dev, int64_t batch, float* const* y_dev, void* stream);
+/* ---- row-sharded projections: all-gather fused into the GEMV ----------- *
+ * No reference counterpart: the reference runs on one CPU.  One process per
+ * GPU; rank r owns a contiguous row range of every projection and computes
+ * its y shard; the shards are assembled in every rank's gathered buffer by
+ * the GEMV itself, which stores each y value also into every rank's buffer
+ * (over NVLink peer mappings), so no separate collective runs.
+ * Set-up: each rank allocates its gathered buffer and a flag array of
+ * `world` 32-bit words with frc_ipc_alloc (zeroed), exchanges the handles
+ * (FRC_IPC_HANDLE_BYTES each, e.g. through torch.distributed) and maps its
+ * peers' buffers with frc_ipc_open.  frc_gather_create takes, for every rank
+ * r, the address of this rank's shard inside r's gathered buffer and r's
+ * flag array (peer mappings, or this rank's own pointers for r == rank).
+ * Per use: frc_gemv_gather (batch 1: the fused launch of up to four
+ * matrices sharing x, as frc_gemv_multi; y_dev[m] are this rank's outputs
+ * and y_base the address that offsets into the gathered buffers are taken
+ * from).  Its result is complete on every rank once a later kernel has
+ * waited for it: pass that gather as `wait_for` to the next frc_gemv_gather
+ * on the stream (the GEMV waits before reading x, which may be the gathered
+ * buffer), or call frc_gather_wait (a one-block kernel).  Waits are bounded
+ * at 1 s; a timeout sets a bit in the device status word.  Every rank must
+ * issue the same sequence of gathers.  frc_gemv_gather returns
+ * FRC_ERR_UNSUPPORTED for shapes without the fused path (callers then use a
+ * collective).  world <= 8. */
+#define FRC_IPC_HANDLE_BYTES 64
+int frc_ipc_alloc(size_t bytes, void** dev_ptr, void* handle);
+int frc_ipc_open(const void* handle, void** dev_ptr);
+int frc_ipc_close(void* dev_ptr);
+int frc_ipc_free(void* dev_ptr);
+typedef struct frc_gather frc_gather;
+int frc_gather_create(int world, int rank, void* const* shard_dst, void* const* flags, frc_gather** out);
+int frc_gather_free(frc_gather* g);
+int frc_gemv_gather(int quant, int count, const void* const* w_dev, const size_t* w_bytes, const int64_t* n,
+                    int64_t k, const float* x_dev, float* const* y_dev, const float* y_base, frc_gather* g,
+                    const frc_gather* wait_for, void* stream);
+int frc_gather_wait(frc_gather* g, void* stream);
 /* Bit-exact dequantisation of n_elems elements (ceil(n_elems/QK) blocks) into
  * out_dev (n_elems floats), matching the reference NumPy decoders
  * (dequant/gguf.py) bit for bit. */
