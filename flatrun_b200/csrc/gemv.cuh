@@ -382,8 +382,10 @@ FRC_DEVICE_INLINE void put_y(const GemvParams& p, float* dst, float v) {
   }
 }
 
-FRC_DEVICE_INLINE void st_release_sys(uint32_t* ptr, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+// A relaxed system-scope store; after one fence.sc.sys it completes a
+// release pattern (the fence orders every earlier write before it).
+FRC_DEVICE_INLINE void st_relaxed_sys(uint32_t* ptr, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
 }
 
 // Called by one thread per slot after the slot barrier that follows the
@@ -400,7 +402,7 @@ FRC_DEVICE_INLINE void gather_arrive(const GemvParams& p, int slots) {
     __threadfence();
     __threadfence_system();
     const uint32_t e = *reinterpret_cast<volatile uint32_t*>(p.g_epoch) + 1u;
-    for (int r = 0; r < p.g_world; ++r) st_release_sys(p.g_flags[r] + p.g_rank, e);
+    for (int r = 0; r < p.g_world; ++r) st_relaxed_sys(p.g_flags[r] + p.g_rank, e);
     *p.g_epoch = e;
     *p.g_done = 0u;
   }
