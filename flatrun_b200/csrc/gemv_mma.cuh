@@ -14,10 +14,10 @@
 // chunk), the block's chunk bytes as 2-D tensor boxes (the matrix viewed as
 // rows of G consecutive matrix rows, G * row_bytes a multiple of 16: one box
 // of R = 16*MT/G tensor rows per row residue) and the chunk's activation
-// records (one bulk copy) into a ring of shared-memory stages.  Eight consumer warps split each chunk's k-steps,
-// two 32-element steps (Q6_K: four 16-element steps) per warp chosen so the
-// warp's steps share their quant bytes; for every step and 16-row
-// tile they run mma.sync m16n8k32 (m16n8k16 for Q6_K's 16-element scale
+// records (one bulk copy) into a ring of shared-memory stages.  Eight
+// consumer warps split each chunk's k-steps, two 32-element steps (Q6_K: four
+// 16-element steps) per warp chosen so the warp's steps share their quant
+// bytes; for every step and 16-row tile they run mma.sync m16n8k32 (m16n8k16 for Q6_K's 16-element scale
 // groups) with the raw quant values as A (Q4_K: one mask per word) and the x
 // byte planes as B: columns 2c and 2c+1 of an 8-wide N tile are the h and l
 // planes of activation column c, so a thread's accumulator pair combines to
@@ -25,8 +25,9 @@
 // reads back as a float after one add).  Each (row, step, column) then adds
 // sx * (ds * T - dm * X) in fp32, with (ds, dm) from a per-warp shared table
 // (K-quants: d*sc and dmin*m; Q8_0: d and 0; Q1_0, whose bits enter as +1/-1
-// bytes: d and 0; Q6_K: d*sc, its -32 offset folded into the seeds).  At the end of a row block the warps' partial sums are reduced
-// through shared memory and written to y.
+// bytes: d and 0; Q6_K: d*sc, its -32 offset folded into the seeds).  At the
+// end of a row block the warps' partial sums are reduced through shared
+// memory and written to y.
 #pragma once
 
 #include <cuda.h>
@@ -113,7 +114,7 @@ static __global__ void __launch_bounds__(256) mma_quantise_x(const float* __rest
     uint32_t h = 0, l = 0;
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-      int q = __float2int_rn(v[4 * w + b] * inv);
+      int q = round_to_int(v[4 * w + b], inv);
       q = q > kXqMax ? kXqMax : (q < -kXqMax ? -kXqMax : q);
       const int qh = (q + 128) >> 8;
       const int ql = q - 256 * qh;

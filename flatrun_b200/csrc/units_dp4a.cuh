@@ -109,6 +109,13 @@ struct UnitX {
 // unit shorten the serial path when units are few, one thread per unit keeps
 // every load of a long row in flight at once.  Every thread of the block calls
 // this with the same arguments (it uses full-warp shuffles).
+// round(v * inv) to the nearest integer (ties to even) for |v * inv| < 2^22:
+// one FMA against 1.5 * 2^23 puts the integer in the low mantissa bits (full
+// rate; an int conversion instruction runs at a quarter of it).
+FRC_DEVICE_INLINE int round_to_int(float v, float inv) {
+  return __float_as_int(fmaf(v, inv, 12582912.0f)) - 0x4B400000;
+}
+
 template <int Q, int UPB, int QK>
 FRC_DEVICE_INLINE void quantise_units(const float* x, int units, uint32_t* records, int P) {
   constexpr int E = I8<Q>::E, NQ = E / 16, NW = E / 4, NG = I8<Q>::NG, RW = record_words<Q>();
@@ -168,7 +175,7 @@ FRC_DEVICE_INLINE void quantise_units(const float* x, int units, uint32_t* recor
         uint32_t h = 0, l = 0;
 #pragma unroll
         for (int bb = 0; bb < 4; ++bb) {
-          int q = __float2int_rn(v[qq][4 * w + bb] * inv);
+          int q = round_to_int(v[qq][4 * w + bb], inv);
           q = q > kXqMax ? kXqMax : (q < -kXqMax ? -kXqMax : q);
           psum += q;
           const int qh = (q + 128) >> 8;  // xq = 256 qh + ql, ql in [-128, 127]
