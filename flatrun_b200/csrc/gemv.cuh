@@ -48,6 +48,7 @@ struct GemvParams {
   int stage_stride;   // bytes per shared-memory stage
   int nstage;
   int wps;            // gemv_i8: warps per slot (one slot covers one row's units)
+  int pre_stages;     // gemv_i8: stages per slot filled before the grid dependency wait
   uint32_t* status;   // device status word
   // gemv_i8 row space: nmat matrices sharing x and k, rows concatenated;
   // matrix m covers rows [mat_end[m-1], mat_end[m]) of the n rows
@@ -455,7 +456,7 @@ __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvPa
   const int leader = p.wps == 1 ? 0 : spt - 32;  // lane 0 of the slot's last warp
   int64_t next_issue = r0;  // leader's cursor over the slot's tiles
   if (st == leader && ntiles > 0) {
-    for (int i = 0; i < nst && i < ntiles; ++i, ++issued) {
+    for (int i = 0; i < p.pre_stages && i < nst && i < ntiles; ++i, ++issued) {
       const Tile t = tile_at(p, next_issue, r1, RPS);
       issue_tile(p, p.mat_w[t.m], stages + static_cast<size_t>(i) * p.stage_stride, &full[i], t.local,
                  t.local + (t.t1 - next_issue));
@@ -481,11 +482,17 @@ __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvPa
     __syncthreads();
   }
 
-  {
-    constexpr int NQ = I8<Q>::E / 16;
-    int P = NQ;
-    while (P > 1 && p.units * P > static_cast<int>(blockDim.x)) P >>= 1;
-    quantise_units<Q, I8<Q>::UPB, F::QK>(p.x, p.units, records, P);
+  // the x loads of a row of up to 16 R blockDim.x elements in one round trip
+  quantise_words<Q, i8_max_warps<Q, UPT>() == 16 ? 3 : 4>(p.x, p.units, records);
+  // the rest of the ring: issued after x is read, so that the activation
+  // loads do not queue behind a full ring of weight copies
+  if (st == leader) {
+    for (int i = issued; i < nst && i < ntiles; ++i, ++issued) {
+      const Tile t = tile_at(p, next_issue, r1, RPS);
+      issue_tile(p, p.mat_w[t.m], stages + static_cast<size_t>(i) * p.stage_stride, &full[i], t.local,
+                 t.local + (t.t1 - next_issue));
+      next_issue = t.t1;
+    }
   }
   __syncthreads();
   if (ntiles == 0) {  // the whole slot leaves together

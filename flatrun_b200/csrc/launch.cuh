@@ -190,6 +190,7 @@ template <int Q, int UPT, int RPS>
 inline cudaError_t launch_i8_rps(GemvParams p, const GemvRequest& r, int slots, int nst) {
   p.stage_stride = round_up(RPS * p.row_bytes + 32, 128);
   p.nstage = nst;
+  p.pre_stages = env_int("FRC_PRE_STAGES", nst);
   const size_t smem =
       i8_smem_header<Q, RPS>(slots, nst, p.wps, p.units) + static_cast<size_t>(slots) * nst * p.stage_stride;
   const int threads = slots * p.wps * 32;

@@ -103,12 +103,6 @@ struct UnitX {
   }
 };
 
-// Quantise the activations of every unit of a row into shared records.  P
-// threads share a unit (P = 1, 2 or 4 for 64-element units; 1 or 2 for 32),
-// each taking E / P consecutive elements in x-word order: more threads per
-// unit shorten the serial path when units are few, one thread per unit keeps
-// every load of a long row in flight at once.  Every thread of the block calls
-// this with the same arguments (it uses full-warp shuffles).
 // round(v * inv) to the nearest integer (ties to even) for |v * inv| < 2^22:
 // one FMA against 1.5 * 2^23 puts the integer in the low mantissa bits (full
 // rate; an int conversion instruction runs at a quarter of it).
@@ -116,102 +110,104 @@ FRC_DEVICE_INLINE int round_to_int(float v, float inv) {
   return __float_as_int(fmaf(v, inv, 12582912.0f)) - 0x4B400000;
 }
 
-template <int Q, int UPB, int QK>
-FRC_DEVICE_INLINE void quantise_units(const float* x, int units, uint32_t* records, int P) {
-  constexpr int E = I8<Q>::E, NQ = E / 16, NW = E / 4, NG = I8<Q>::NG, RW = record_words<Q>();
-  const int per = NQ / P;  // 16-element quarters per thread
-  const int total = units * P;
-  for (int base = 0; base < total; base += blockDim.x) {
-    const int t = base + static_cast<int>(threadIdx.x);
-    const bool active = t < total;
-    const int u = active ? t / P : 0, part = t % P;
-    const int b = u / UPB, j = u % UPB;
-    float v[NQ][16];
+// Unit u and x-word w (four consecutive elements) that global x-word gw of a
+// row belongs to.  K-quants other than Q6_K, Q8_0 and Q1_0 number their unit
+// words in x order; a Q6_K block's 64 words interleave its four units: word e
+// (element 4e of the block) is in half e / 32, quarter (e / 8) % 4, 16-element
+// run (e / 4) % 2, so unit 2 half + run, word 4 quarter + e % 4.
+template <int Q> FRC_DEVICE_INLINE void x_word_home(int gw, int& u, int& w) {
+  if constexpr (Q == kQ6_K) {
+    const int e = gw & 63;
+    u = (gw >> 6) * 4 + 2 * (e >> 5) + ((e >> 2) & 1);
+    w = 4 * ((e >> 3) & 3) + (e & 3);
+  } else {
+    constexpr int NW = I8<Q>::E / 4;
+    u = gw / NW;
+    w = gw % NW;
+  }
+}
+
+// Lane-index bits that differ between the threads holding one unit
+// (kUnitLanes) and one scale group (kGroupLanes) when every thread takes four
+// consecutive x-words (16 elements) and a warp's lanes take consecutive
+// quads.  A 64-element unit is 4 neighbouring lanes (32-element: 2) and its
+// 32-element group 2 lanes.  A Q6_K block's 16 quads interleave its units:
+// lane bit 0 is the 16-element run (unit j % 2), bits 1-2 the quarter, bit 3
+// the half (unit j / 2), so a unit's lanes differ in bits 1-2 and every lane
+// holds one whole 16-element scale group.
+template <int Q> struct XQuads {
+  static constexpr int kUnitLanes = Q == kQ6_K ? 0x6 : I8<Q>::E / 16 - 1;
+  static constexpr int kGroupLanes = Q == kQ6_K ? 0x0 : I8<Q>::E / 16 / I8<Q>::NG - 1;
+};
+
+// Quantise the activations of every unit of a row into shared records: xq =
+// round(x * kXqMax / amax) per unit, stored as high bytes (xq + 128) >> 8 and
+// low bytes xq & 0xFF, plus the integer sum of xq over each scale group and the
+// unit's scale amax / kXqMax.  Every thread takes four x-words (16 consecutive
+// elements, four 16-byte loads) per round; the loads of R rounds (k <= 16 R
+// blockDim.x) are issued before any is used, since an L2 round trip under a
+// full weight stream costs about a microsecond.  The unit's amax and the group
+// sums are reduced across the lanes that share them with butterfly shuffles.
+// |x * inv| <= kXqMax (1 + 2^-24) rounds to at most kXqMax, so no clamp is
+// needed.  One FMA against 1.5 * 2^23 + 128 leaves xq + 128 in the low
+// mantissa bits: byte 0 is the low byte of xq with its top bit flipped, byte 1
+// the high byte.  Every thread of the block calls this with the same arguments
+// (it uses full-warp shuffles); blockDim.x is a multiple of 32.
+template <int Q, int R>
+FRC_DEVICE_INLINE void quantise_words(const float* x, int units, uint32_t* records) {
+  constexpr int NW = I8<Q>::E / 4, NG = I8<Q>::NG, RW = record_words<Q>();
+  constexpr int UL = XQuads<Q>::kUnitLanes, GL = XQuads<Q>::kGroupLanes;
+  const int ntask = units * NW / 4;
+  const int bd = static_cast<int>(blockDim.x), tid = static_cast<int>(threadIdx.x);
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  for (int base = 0; base < ntask; base += R * bd) {
+    float4 v[R][4];
 #pragma unroll
-    for (int qq = 0; qq < NQ; ++qq) {
-      const int quarter = part * per + qq;
-      if (active && qq < per) {
-        const float4* s4 = reinterpret_cast<const float4*>(x + static_cast<int64_t>(b) * QK + i8_pos<Q>(j, 16 * quarter));
+    for (int i = 0; i < R; ++i) {
+      const int t = base + i * bd + tid;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 tt = __ldg(s4 + q);
-          v[qq][4 * q] = tt.x; v[qq][4 * q + 1] = tt.y; v[qq][4 * q + 2] = tt.z; v[qq][4 * q + 3] = tt.w;
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[qq][i] = 0.f;
-      }
+      for (int q = 0; q < 4; ++q) v[i][q] = t < ntask ? __ldg(x4 + 4 * t + q) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    // tree-shaped max over the thread's quarters (short dependency chain)
-    float m16[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) m16[i] = fabsf(v[0][i]);
+    for (int i = 0; i < R; ++i) {
+      if (base + i * bd >= ntask) break;  // uniform over the block
+      const int t = base + i * bd + tid;
+      float m4[4];
 #pragma unroll
-    for (int qq = 1; qq < NQ; ++qq) {
-      if (qq < per) {
+      for (int q = 0; q < 4; ++q)
+        m4[q] = fmaxf(fmaxf(fabsf(v[i][q].x), fabsf(v[i][q].y)), fmaxf(fabsf(v[i][q].z), fabsf(v[i][q].w)));
+      float a = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
 #pragma unroll
-        for (int i = 0; i < 16; ++i) m16[i] = fmaxf(m16[i], fabsf(v[qq][i]));
-      }
-    }
-#pragma unroll
-    for (int w = 8; w >= 1; w >>= 1)
-#pragma unroll
-      for (int i = 0; i < w; ++i) m16[i] = fmaxf(m16[i], m16[i + w]);
-    float amax = m16[0];
-    if (P >= 2) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    if (P >= 4) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    const float inv = amax > 0.f ? static_cast<float>(kXqMax) / amax : 0.0f;
-    uint32_t* rec = records + u * RW;
-    int qsum[NQ];
-#pragma unroll
-    for (int qq = 0; qq < NQ; ++qq) {
-      qsum[qq] = 0;
-      if (qq >= per) continue;  // uniform: every thread has the same `per`
-      const int quarter = part * per + qq;
+      for (int m = 1; m < 32; m <<= 1)
+        if (UL & m) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, m));
+      const float inv = a > 0.f ? static_cast<float>(kXqMax) / a : 0.0f;
       uint32_t hw[4], lw[4];
-      int psum = 0;
+      uint32_t sum = 0;  // the xq plus 0x4B400080 each, in 32-bit wrapping arithmetic
 #pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        uint32_t h = 0, l = 0;
-#pragma unroll
-        for (int bb = 0; bb < 4; ++bb) {
-          int q = round_to_int(v[qq][4 * w + bb], inv);
-          q = q > kXqMax ? kXqMax : (q < -kXqMax ? -kXqMax : q);
-          psum += q;
-          const int qh = (q + 128) >> 8;  // xq = 256 qh + ql, ql in [-128, 127]
-          const int ql = q - 256 * qh;
-          h |= (static_cast<uint32_t>(qh) & 0xFFu) << (8 * bb);
-          l |= (static_cast<uint32_t>(ql) & 0xFFu) << (8 * bb);
-        }
-        hw[w] = h;
-        lw[w] = l;
+      for (int q = 0; q < 4; ++q) {
+        const int r0 = __float_as_int(fmaf(v[i][q].x, inv, 12583040.0f));
+        const int r1 = __float_as_int(fmaf(v[i][q].y, inv, 12583040.0f));
+        const int r2 = __float_as_int(fmaf(v[i][q].z, inv, 12583040.0f));
+        const int r3 = __float_as_int(fmaf(v[i][q].w, inv, 12583040.0f));
+        hw[q] = __byte_perm(__byte_perm(r0, r1, 0x0051), __byte_perm(r2, r3, 0x0051), 0x5410);
+        lw[q] = __byte_perm(__byte_perm(r0, r1, 0x0040), __byte_perm(r2, r3, 0x0040), 0x5410) ^ 0x80808080u;
+        sum += static_cast<uint32_t>(r0) + static_cast<uint32_t>(r1) + static_cast<uint32_t>(r2) +
+               static_cast<uint32_t>(r3);
       }
-      qsum[qq] = psum;
-      if (active) {
-        *reinterpret_cast<uint4*>(rec + 4 * quarter) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        *reinterpret_cast<uint4*>(rec + NW + 4 * quarter) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      int gs = static_cast<int>(sum - 16u * 0x4B400080u);
+#pragma unroll
+      for (int m = 1; m < 32; m <<= 1)
+        if (GL & m) gs += __shfl_xor_sync(0xffffffffu, gs, m);
+      if (t < ntask) {
+        int u, w;
+        x_word_home<Q>(4 * t, u, w);
+        uint32_t* rec = records + u * RW;
+        *reinterpret_cast<uint4*>(rec + w) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(rec + NW + w) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        if (w % (NW / NG) == 0) rec[2 * NW + w / (NW / NG)] = static_cast<uint32_t>(gs);
+        if (w == 0) rec[2 * NW + NG] = __float_as_uint(a > 0.f ? a / static_cast<float>(kXqMax) : 1.0f);
       }
     }
-    // scale-group sums: a group spans QPG quarters; a thread holds `per`
-    // consecutive quarters, so it owns whole groups (per >= QPG) or a group is
-    // split over QPG / per neighbouring lanes (summed by shuffles)
-    constexpr int QPG = NQ / NG;
-    if (per >= QPG) {
-#pragma unroll
-      for (int qq = 0; qq < NQ; qq += QPG) {
-        if (active && qq < per) {
-          int g = 0;
-#pragma unroll
-          for (int i = 0; i < QPG; ++i) g += qsum[qq + i];
-          rec[2 * NW + (part * per + qq) / QPG] = static_cast<uint32_t>(g);
-        }
-      }
-    } else {
-      int g = qsum[0];
-      for (int o = 1; o < QPG / per; o <<= 1) g += __shfl_xor_sync(0xffffffffu, g, o);
-      if (active && (part * per) % QPG == 0) rec[2 * NW + (part * per) / QPG] = static_cast<uint32_t>(g);
-    }
-    if (active && part == 0) rec[2 * NW + NG] = __float_as_uint(amax > 0.f ? amax / static_cast<float>(kXqMax) : 1.0f);
   }
 }
 
