@@ -115,6 +115,50 @@ FRC_DEVICE_INLINE void lds_words_a2(const uint8_t* p, uint32_t (&out)[N]) {
   for (int i = 0; i < N; ++i) out[i] = __funnelshift_r(w[i], w[i + 1], sh);
 }
 
+// Shared-memory loads at a 32-bit shared address plus an immediate byte
+// offset (one LDS each, no generic-address arithmetic).  Volatile keeps them
+// after the mbarrier waits that publish the stage they read.
+template <int OFF>
+FRC_DEVICE_INLINE uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4+%5];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(a), "n"(OFF));
+  return v;
+}
+template <int OFF>
+FRC_DEVICE_INLINE uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(a), "n"(OFF));
+  return v;
+}
+template <int OFF>
+FRC_DEVICE_INLINE uint32_t lds16(uint32_t a) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1+%2];" : "=h"(v) : "r"(a), "n"(OFF));
+  return v;
+}
+
+// N little-endian words starting OFF bytes past the 4-byte aligned shared
+// address a, shifted right by sh bits (0 or 16) across word boundaries: the N
+// words at byte a + OFF + sh / 8.  Reads the words [a + OFF, a + OFF + 4N + 4).
+template <int N, int OFF>
+FRC_DEVICE_INLINE void lds_words_sh(uint32_t a, uint32_t sh, uint32_t (&out)[N]) {
+  uint32_t w[N + 1];
+  if constexpr (N >= 1) w[0] = lds32<OFF>(a);
+  if constexpr (N >= 1) w[1] = lds32<OFF + 4>(a);
+  if constexpr (N >= 2) w[2] = lds32<OFF + 8>(a);
+  if constexpr (N >= 3) w[3] = lds32<OFF + 12>(a);
+  if constexpr (N >= 4) w[4] = lds32<OFF + 16>(a);
+  if constexpr (N >= 5) w[5] = lds32<OFF + 20>(a);
+  if constexpr (N >= 6) w[6] = lds32<OFF + 24>(a);
+  if constexpr (N >= 7) w[7] = lds32<OFF + 28>(a);
+  if constexpr (N >= 8) w[8] = lds32<OFF + 32>(a);
+  static_assert(N <= 8, "at most 8 words");
+#pragma unroll
+  for (int i = 0; i < N; ++i) out[i] = __funnelshift_r(w[i], w[i + 1], sh);
+}
+
 // Byte b (0..3) of word w placed as the mantissa byte of 1.0f:
 // returns 1 + ((w >> 8b) & 0xFF) / 128 for bytes already ORed with 0x80,
 // i.e. the float 0x3F80_0000 | (low 7 bits << 16).

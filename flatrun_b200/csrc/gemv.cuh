@@ -502,7 +502,6 @@ __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvPa
 
   UnitX<Q> xu[UPT];
   UnitCtx cx[UPT];
-  int uoff[UPT];
   bool uval[UPT];
 #pragma unroll
   for (int i = 0; i < UPT; ++i) {
@@ -510,8 +509,7 @@ __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvPa
     uval[i] = u < p.units;
     const int b = uval[i] ? u / I8<Q>::UPB : 0;
     const int j = uval[i] ? u % I8<Q>::UPB : 0;
-    cx[i] = make_ctx<Q>(j);
-    uoff[i] = b * F::TS;
+    cx[i] = make_ctx<Q>(j, b);
     if (uval[i]) {
       xu[i].from_record(records + u * RW);
     } else {
@@ -520,6 +518,7 @@ __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvPa
   }
 
   const int wis = warp - slot * p.wps;  // warp index inside the slot
+  const uint32_t stages_s = smem_u32(stages);
   int64_t t0 = r0;  // consumers' cursor
   for (int it = 0; it < ntiles; ++it) {
     const int s = it % nst;
@@ -531,8 +530,10 @@ __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvPa
 #pragma unroll
     for (int r = 0; r < RPS; ++r) acc[r] = 0.f;
     if (wait_phase(&full[s], ph, abort)) {
-      const uint8_t* base = stages + static_cast<size_t>(s) * p.stage_stride +
-                            ((static_cast<uint64_t>(tile.local) * p.row_bytes) & 15u);
+      // shared address of the tile's first row: the copy keeps the source's
+      // offset modulo 16 (only the low bits of the product matter)
+      const uint32_t base = stages_s + static_cast<uint32_t>(s) * static_cast<uint32_t>(p.stage_stride) +
+                            ((static_cast<uint32_t>(tile.local) * static_cast<uint32_t>(p.row_bytes)) & 15u);
       if (rows == RPS) {
         // full tile: no per-row guard, so the rows' independent instruction
         // streams can be interleaved
@@ -541,17 +542,17 @@ __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvPa
           if (uval[i]) {
 #pragma unroll
             for (int r = 0; r < RPS; ++r)
-              acc[r] += UnitDotI8<Q>::dot(base + r * p.row_bytes + uoff[i], cx[i], xu[i]);
+              acc[r] += UnitDotI8<Q>::dot(base + static_cast<uint32_t>(r * p.row_bytes), cx[i], xu[i]);
           }
         }
       } else {
 #pragma unroll
         for (int r = 0; r < RPS; ++r) {
           if (r < rows) {
-            const uint8_t* row = base + r * p.row_bytes;
+            const uint32_t row = base + static_cast<uint32_t>(r * p.row_bytes);
 #pragma unroll
             for (int i = 0; i < UPT; ++i) {
-              if (uval[i]) acc[r] += UnitDotI8<Q>::dot(row + uoff[i], cx[i], xu[i]);
+              if (uval[i]) acc[r] += UnitDotI8<Q>::dot(row, cx[i], xu[i]);
             }
           }
         }

@@ -211,9 +211,13 @@ FRC_DEVICE_INLINE void quantise_words(const float* x, int units, uint32_t* recor
   }
 }
 
-// Per-thread constants derived from the unit index j.
+// Per-thread constants derived from the unit index j and block index b.
 struct UnitCtx {
   int j;
+  uint32_t blk;     // byte offset of the unit's block in its row
+  uint32_t f0;      // Q4_K/Q5_K: offset of the unit's quants in the row; Q6_K: of ql (within the block)
+  uint32_t f1;      // Q6_K: offset of the unit's qh bytes in the block; Q1_0: of its bit word in the row
+  uint32_t f2;      // Q6_K: offset of the unit's half of the scales in the block
   uint32_t sh;      // Q5_K: high-bit shift 2g; Q6_K: scale byte shift 8 lh
   uint32_t sel_a;   // K-quants: PRMT selector of the low scale/min bits
   uint32_t sel_h;   // K-quants: PRMT selector of the top two bits
@@ -221,9 +225,19 @@ struct UnitCtx {
   uint32_t mhi;     // K-quants: mask of the moved top bits (0 for groups 0, 1)
 };
 
-template <int Q> FRC_DEVICE_INLINE UnitCtx make_ctx(int j) {
+template <int Q> FRC_DEVICE_INLINE UnitCtx make_ctx(int j, int b) {
   UnitCtx c{};
   c.j = j;
+  c.blk = static_cast<uint32_t>(b * Fmt<Q>::TS);
+  if constexpr (Q == kQ4_K) c.f0 = c.blk + 16u + 32u * j;
+  if constexpr (Q == kQ5_K) c.f0 = c.blk + 48u + 32u * j;
+  if constexpr (Q == kQ6_K) {
+    const uint32_t half = static_cast<uint32_t>(j >> 1), lh = static_cast<uint32_t>(j & 1);
+    c.f0 = 64u * half + 16u * lh;
+    c.f1 = 128u + 32u * half + 16u * lh;
+    c.f2 = 192u + 8u * half;
+  }
+  if constexpr (Q == kQ1_0) c.f1 = c.blk + 2u + 4u * j;
   if constexpr (Q == kQ4_K || Q == kQ5_K) {
     // Sub-blocks s0 = 2j, s1 = 2j + 1 use byte t0 = (2j) & 3 and t0 + 1 of
     // the scale words.  Groups 0, 1: sc = q[s] & 63 (word 0), m = q[s+4] & 63
@@ -261,10 +275,11 @@ template <int Q> struct UnitDotI8;
 // Bounds: |xq| <= 32639.  Q4_K: |T| <= 32*15*32767 = 15.7e6 per sub-block,
 // sc*T <= 991e6, two sub-blocks <= 1.98e9 < 2^31.
 template <> struct UnitDotI8<kQ4_K> {
-  static FRC_DEVICE_INLINE float dot(const uint8_t* blk, const UnitCtx& c, const UnitX<kQ4_K>& x) {
-    const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-    const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * c.j);
-    const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * c.j);
+  // row: shared address of the row (16-byte aligned: 144-byte blocks)
+  static FRC_DEVICE_INLINE float dot(uint32_t row, const UnitCtx& c, const UnitX<kQ4_K>& x) {
+    const uint4 hdr = lds128<0>(row + c.blk);
+    const uint4 qa = lds128<0>(row + c.f0);
+    const uint4 qb = lds128<16>(row + c.f0);
     const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
     // two accumulator chains per sum for instruction-level parallelism; the
     // high nibbles stay in place (16 * nibble, unsigned) and the factor 16 is
@@ -296,12 +311,14 @@ template <> struct UnitDotI8<kQ4_K> {
 // sc*T <= 2.05e9 is too close to 2^31 for two sub-blocks, so each sub-block
 // is converted to fp32 separately.
 template <> struct UnitDotI8<kQ5_K> {
-  static FRC_DEVICE_INLINE float dot(const uint8_t* blk, const UnitCtx& c, const UnitX<kQ5_K>& x) {
-    const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-    const uint4 ha = *reinterpret_cast<const uint4*>(blk + 16);
-    const uint4 hb = *reinterpret_cast<const uint4*>(blk + 32);
-    const uint4 qa = *reinterpret_cast<const uint4*>(blk + 48 + 32 * c.j);
-    const uint4 qb = *reinterpret_cast<const uint4*>(blk + 64 + 32 * c.j);
+  // row: shared address of the row (16-byte aligned: 176-byte blocks)
+  static FRC_DEVICE_INLINE float dot(uint32_t row, const UnitCtx& c, const UnitX<kQ5_K>& x) {
+    const uint32_t blk = row + c.blk;
+    const uint4 hdr = lds128<0>(blk);
+    const uint4 ha = lds128<16>(blk);
+    const uint4 hb = lds128<32>(blk);
+    const uint4 qa = lds128<0>(row + c.f0);
+    const uint4 qb = lds128<16>(row + c.f0);
     const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
     const uint32_t h[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
     int lh = 0, ll = 0, hh = 0, hl = 0;
@@ -330,13 +347,17 @@ template <> struct UnitDotI8<kQ5_K> {
 // Q6_K: u = nibble | 2 bits << 4 in [0, 63], weight (u - 32) * sc.
 // Per quarter |T| <= 16*63*32767 = 33e6; T - 32 X fits int32; fp32 per quarter.
 template <> struct UnitDotI8<kQ6_K> {
-  static FRC_DEVICE_INLINE float dot(const uint8_t* blk, const UnitCtx& c, const UnitX<kQ6_K>& x) {
-    const int half = c.j >> 1, lh = c.j & 1;
+  // row: shared address of the row; 210-byte blocks are 2-byte aligned, so the
+  // fields (at multiples of 4 inside the block) are read as aligned words
+  // and funnel-shifted by the block's misalignment
+  static FRC_DEVICE_INLINE float dot(uint32_t row, const UnitCtx& c, const UnitX<kQ6_K>& x) {
+    const uint32_t blk = row + c.blk;
+    const uint32_t al = blk & ~3u, fs = (blk & 3u) * 8u;
     uint32_t qa[4], qb[4], qh[4], sw[2];
-    lds_words_a2<4>(blk + 64 * half + 16 * lh, qa);
-    lds_words_a2<4>(blk + 64 * half + 32 + 16 * lh, qb);
-    lds_words_a2<4>(blk + 128 + 32 * half + 16 * lh, qh);
-    lds_words_a2<2>(blk + 192 + 8 * half, sw);
+    lds_words_sh<4, 0>(al + c.f0, fs, qa);
+    lds_words_sh<4, 32>(al + c.f0, fs, qb);
+    lds_words_sh<4, 0>(al + c.f1, fs, qh);
+    lds_words_sh<2, 0>(al + c.f2, fs, sw);
     int sh[4] = {0, 0, 0, 0}, sl[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -363,23 +384,25 @@ template <> struct UnitDotI8<kQ6_K> {
     const float w1 = static_cast<float>(sh[1] * 256 + sl[1] - 32 * x.xsum[1]);
     const float w2 = static_cast<float>(sh[2] * 256 + sl[2] - 32 * x.xsum[2]);
     const float w3 = static_cast<float>(sh[3] * 256 + sl[3] - 32 * x.xsum[3]);
-    const float d = half_bits_to_float(ld_u16(blk + 208));
+    const float d = half_bits_to_float(lds16<208>(blk));
     return x.sx * d * ((s0 * w0 + s1 * w1) + (s2 * w2 + s3 * w3));
   }
 };
 
 // Q8_0: signed quants; |T| <= 32*127*32767 = 133e6.
 template <> struct UnitDotI8<kQ8_0> {
-  static FRC_DEVICE_INLINE float dot(const uint8_t* blk, const UnitCtx&, const UnitX<kQ8_0>& x) {
+  // row: shared address of the row; 34-byte blocks are 2-byte aligned
+  static FRC_DEVICE_INLINE float dot(uint32_t row, const UnitCtx& c, const UnitX<kQ8_0>& x) {
+    const uint32_t blk = row + c.blk, qs = blk + 2u;
     uint32_t q[8];
-    lds_words_a2<8>(blk + 2, q);
+    lds_words_sh<8, 0>(qs & ~3u, (qs & 3u) * 8u, q);
     int sh = 0, sl = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       sh = dp4a_ss(q[i], x.xh[i], sh);
       sl = dp4a_ss(q[i], x.xl[i], sl);
     }
-    const float d = half_bits_to_float(ld_u16(blk));
+    const float d = half_bits_to_float(lds16<0>(blk));
     return x.sx * d * static_cast<float>(sh * 256 + sl);
   }
 };
@@ -388,8 +411,12 @@ template <> struct UnitDotI8<kQ8_0> {
 // bytes four at a time: (nibble * 0x00204081) & 0x01010101 puts bit b of the
 // nibble in byte b.
 template <> struct UnitDotI8<kQ1_0> {
-  static FRC_DEVICE_INLINE float dot(const uint8_t* blk, const UnitCtx& c, const UnitX<kQ1_0>& x) {
-    const uint32_t bits = ld_u32_a2(blk + 2 + 4 * c.j);
+  // row: shared address of the row; 18-byte blocks are 2-byte aligned
+  static FRC_DEVICE_INLINE float dot(uint32_t row, const UnitCtx& c, const UnitX<kQ1_0>& x) {
+    const uint32_t bw = row + c.f1;
+    uint32_t bits1[1];
+    lds_words_sh<1, 0>(bw & ~3u, (bw & 3u) * 8u, bits1);
+    const uint32_t bits = bits1[0];
     int sh = 0, sl = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -397,7 +424,7 @@ template <> struct UnitDotI8<kQ1_0> {
       sh = dp4a_ss(b, x.xh[i], sh);
       sl = dp4a_ss(b, x.xl[i], sl);
     }
-    const float d = half_bits_to_float(ld_u16(blk));
+    const float d = half_bits_to_float(lds16<0>(row + c.blk));
     return x.sx * d * static_cast<float>(2 * (sh * 256 + sl) - x.xsum[0]);
   }
 };
