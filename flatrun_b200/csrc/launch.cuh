@@ -190,7 +190,10 @@ template <int Q, int UPT, int RPS>
 inline cudaError_t launch_i8_rps(GemvParams p, const GemvRequest& r, int slots, int nst) {
   p.stage_stride = round_up(RPS * p.row_bytes + 32, 128);
   p.nstage = nst;
-  p.pre_stages = env_int("FRC_PRE_STAGES", nst);
+  // one stage per slot before the grid dependency wait: a full ring of
+  // weight copies in flight delays the activation loads behind it (measured
+  // on B200: the Qwen2-7B layer step 43.8 -> 41.8 us)
+  p.pre_stages = env_int("FRC_PRE_STAGES", 1);
   const size_t smem =
       i8_smem_header<Q, RPS>(slots, nst, p.wps, p.units) + static_cast<size_t>(slots) * nst * p.stage_stride;
   const int threads = slots * p.wps * 32;
@@ -230,9 +233,11 @@ inline cudaError_t launch_i8(GemvParams p, const GemvRequest& r) {
   int slots = warps / p.wps;
   if (slots < 1) slots = 1;
   if (slots * p.wps > kMaxW) slots = kMaxW / p.wps;
-  // ~8 KB tiles for short rows; long rows (k > ~14K for Q4_K) do better
-  // with two-row tiles up to 32 KB
-  const int tile_target = env_int("FRC_TILE_BYTES", p.row_bytes > 8192 ? 32 * 1024 : 8 * 1024);
+  // ~8 KB tiles for short rows (12 KB for Q6_K: four 2940-byte rows of the
+  // k = 3584 lm_head, 4.3 -> 4.9 TB/s); long rows (k > ~14K for Q4_K) do
+  // better with two-row tiles up to 32 KB
+  const int tile_target =
+      env_int("FRC_TILE_BYTES", p.row_bytes > 8192 ? 32 * 1024 : (Q == kQ6_K ? 12 * 1024 : 8 * 1024));
   int rps = 1;
   while (rps < 8 && 2 * rps * p.row_bytes <= tile_target) rps *= 2;
   const int forced = env_int("FRC_RPS", 0);
@@ -597,15 +602,13 @@ cudaError_t launch_gemv(const GemvRequest& r) {
     const int units = (r.k / F::QK) * I8<Q>::UPB;
     p.units = units;
     // Units per thread (measured on B200, batch 1): 32-element units (Q8_0,
-    // Q1_0) use one warp per row with up to 4 units per thread; Q6_K rows of
-    // up to 64 units use one warp per row with 2; Q4_K/Q5_K rows of up to 64
-    // units use 1 unit per thread in two-warp slots; longer rows use 2 units
-    // per thread in multi-warp slots.
+    // Q1_0) use one warp per row with up to 4 units per thread; K-quant rows
+    // of up to 64 units use 1 unit per thread in two-warp slots; longer rows
+    // use 2 units per thread in multi-warp slots.
     int upt = env_int("FRC_UPT", 0);
     if (upt == 0) {
       if (I8<Q>::E == 32) upt = units <= 128 ? 4 : 2;
-      else if (units <= 64) upt = Q == kQ6_K ? 2 : 1;
-      else upt = 2;
+      else upt = units <= 64 ? 1 : 2;
     }
     if constexpr (I8<Q>::E == 32) {
       if (upt == 4 && units <= 128) return launch_i8<Q, 4>(p, r);
