@@ -520,9 +520,9 @@ __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvPa
   const int wis = warp - slot * p.wps;  // warp index inside the slot
   const uint32_t stages_s = smem_u32(stages);
   int64_t t0 = r0;  // consumers' cursor
+  int s = 0;          // stage of tile it (it % nst, kept incrementally)
+  uint32_t ph = 0u;   // its mbarrier phase parity ((it / nst) & 1)
   for (int it = 0; it < ntiles; ++it) {
-    const int s = it % nst;
-    const uint32_t ph = static_cast<uint32_t>(it / nst) & 1u;
     const Tile tile = tile_at(p, t0, r1, RPS);
     const int rows = static_cast<int>(tile.t1 - t0);
     float* ym = p.mat_y[tile.m] + tile.local;
@@ -594,6 +594,10 @@ __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvPa
       put_y(p, ym + st, acc[0]);
     }
     t0 = tile.t1;
+    if (++s == nst) {
+      s = 0;
+      ph ^= 1u;
+    }
   }
   if (p.g_world > 1) {  // publish this slot's gathered rows
     // the leader's system fence after the slot barrier orders every thread's
