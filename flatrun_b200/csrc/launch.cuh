@@ -221,6 +221,20 @@ inline cudaError_t launch_i8_rps(GemvParams p, const GemvRequest& r, int slots, 
 // Shared memory available to one block (B200: 227 KB opt-in).
 constexpr int kSmemBudget = 227 * 1024;
 
+// Bytes of weights per tile the batch-1 kernel aims for (rows per tile = the
+// largest power of two <= 8 whose tile fits), swept on B200: ~8 KB for short
+// K-quant rows, 12 KB (four 2940-byte rows) for the k = 3584 Q6_K lm_head
+// (4.3 -> 5.1 TB/s), 18 KB (four rows) for k = 4096 Q8_0, 4 KB (four rows) for
+// Q1_0; long rows (k > ~14K for Q4_K) two-row tiles up to 32 KB.
+template <int Q>
+inline int i8_tile_target(int row_bytes) {
+  if (row_bytes > 8192) return 32 * 1024;
+  if constexpr (Q == kQ6_K) return 12 * 1024;
+  if constexpr (Q == kQ8_0) return 18 * 1024;
+  if constexpr (Q == kQ1_0) return 4 * 1024;
+  return 8 * 1024;
+}
+
 // Choose slots (independent pipelines of wps warps), rows per tile and stages
 // so the block fits in shared memory: prefer the requested tile size and as
 // many warps as the register budget allows, then shrink tiles, then warps.
@@ -233,11 +247,7 @@ inline cudaError_t launch_i8(GemvParams p, const GemvRequest& r) {
   int slots = warps / p.wps;
   if (slots < 1) slots = 1;
   if (slots * p.wps > kMaxW) slots = kMaxW / p.wps;
-  // ~8 KB tiles for short rows (12 KB for Q6_K: four 2940-byte rows of the
-  // k = 3584 lm_head, 4.3 -> 4.9 TB/s); long rows (k > ~14K for Q4_K) do
-  // better with two-row tiles up to 32 KB
-  const int tile_target =
-      env_int("FRC_TILE_BYTES", p.row_bytes > 8192 ? 32 * 1024 : (Q == kQ6_K ? 12 * 1024 : 8 * 1024));
+  const int tile_target = env_int("FRC_TILE_BYTES", i8_tile_target<Q>(p.row_bytes));
   int rps = 1;
   while (rps < 8 && 2 * rps * p.row_bytes <= tile_target) rps *= 2;
   const int forced = env_int("FRC_RPS", 0);
@@ -601,13 +611,15 @@ cudaError_t launch_gemv(const GemvRequest& r) {
   if (r.batch == 1 && !force_xb && env_int("FRC_GEMV_FP32", 0) == 0) {
     const int units = (r.k / F::QK) * I8<Q>::UPB;
     p.units = units;
-    // Units per thread (measured on B200, batch 1): 32-element units (Q8_0,
-    // Q1_0) use one warp per row with up to 4 units per thread; K-quant rows
-    // of up to 64 units use 1 unit per thread in two-warp slots; longer rows
-    // use 2 units per thread in multi-warp slots.
+    // Units per thread (swept on B200, batch 1): K-quant rows of up to 64
+    // units use 1 unit per thread in two-warp slots, longer rows 2 units per
+    // thread in multi-warp slots; Q8_0 rows of up to 128 units 1 unit per
+    // thread in four-warp slots (4096x4096: 6.5 -> 6.1 us), Q1_0 2 units per
+    // thread (4096x4096: 6.0 -> 5.4 us).
     int upt = env_int("FRC_UPT", 0);
     if (upt == 0) {
-      if (I8<Q>::E == 32) upt = units <= 128 ? 4 : 2;
+      if constexpr (Q == kQ8_0) upt = units <= 128 ? 1 : 2;
+      else if constexpr (Q == kQ1_0) upt = 2;
       else upt = units <= 64 ? 1 : 2;
     }
     if constexpr (I8<Q>::E == 32) {
