@@ -25,9 +25,11 @@ cpu_baseline: the reference's own native kernels (flatrun_native._C, built
 
 Multi-GPU (--gpus N under torchrun): each rank owns an n-row shard (the
 config's shapes) of every projection of an N-times taller layer, whole quant
-blocks per row, and the outputs are assembled by NCCL all-gathers in the
+blocks per row, and the outputs are assembled by all-gathers in the
 forwarder's dependency groups (qkv, o, gate+up, down).  Per-GPU work is fixed
-("weak" scaling); value = bytes of all ranks / max-over-ranks time.
+("weak" scaling); value = bytes of all ranks / max-over-ranks time.  The
+`layer_llama70b` workload (config 5) instead splits one whole Llama-3-70B
+layer's rows over the ranks ("strong" scaling).
 """
 
 from __future__ import annotations
@@ -58,6 +60,17 @@ QWEN2_7B = [  # (name, quant, n, k, gather group)
     ("gate", "Q4_K", 18944, 3584, "gateup"),
     ("up", "Q4_K", 18944, 3584, "gateup"),
     ("down", "Q4_K", 3584, 18944, "down"),
+]
+
+
+LLAMA3_70B = [  # one Llama-3-70B layer: hidden 8192, 64 / 8 heads of 128, FFN 28672
+    ("q", "Q4_K", 8192, 8192, "qkv"),
+    ("k", "Q4_K", 1024, 8192, "qkv"),
+    ("v", "Q4_K", 1024, 8192, "qkv"),
+    ("o", "Q4_K", 8192, 8192, "o"),
+    ("gate", "Q4_K", 28672, 8192, "gateup"),
+    ("up", "Q4_K", 28672, 8192, "gateup"),
+    ("down", "Q4_K", 8192, 28672, "down"),
 ]
 
 
@@ -96,6 +109,10 @@ WORKLOADS = {
                      desc="Q6_K down 3584x18944, batch 1"),
     "q1_0": dict(mats=[("w", "Q1_0", 4096, 4096, "w")], batch=1, desc="Q1_0 4096x4096, batch 1"),
     "gate_q4k": dict(mats=[("gate", "Q4_K", 18944, 3584, "w")], batch=1, desc="Q4_K gate 18944x3584, batch 1"),
+    "layer_llama70b": dict(mats=LLAMA3_70B, batch=1, strong=True,
+                           desc="config 5: one Llama-3-70B layer's projections (q,k,v,o,gate,up,down) in Q4_K, "
+                                "batch 1; under --gpus N every projection's rows are split over the N ranks "
+                                "(strong scaling)"),
     "decode_qwen2_7b": dict(mats=qwen2_7b_decode_token(), batch=1,
                             desc="config 4 projections: one Qwen2-7B decode token (28 layers, Q4_K_M mix, Q6_K "
                                  "lm_head), batch 1"),
@@ -305,7 +322,8 @@ def main() -> None:
         print(json.dumps({
             "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
             "steps": steps, "warmup": warm, "ms_per_step": round(med * 1e3, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "higher_is_better": True, "scaling": "strong" if wl.get("strong") else "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
             "config": {"workload": wl["desc"], "global_batch": batch},
             "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": 1, "kind": kind,
                              "sample": f"{steps} timed steps of the full workload (median), reference "
@@ -322,6 +340,15 @@ def main() -> None:
     import torch
 
     from flatrun_b200 import CudaBackend, _lib
+
+    # strong scaling: the workload is one whole layer, each rank owns n / N
+    # rows of every projection (whole quant blocks per row)
+    if wl.get("strong") and world > 1:
+        if any(n % world for _, _, n, _, _ in mats):
+            raise SystemExit(f"{args.workload}: row counts must divide by {world}")
+        mats = [(nm, q, n // world, k, g) for nm, q, n, k, g in mats]
+        step_bytes = algorithmic_bytes(mats, batch, fused=not getattr(args, "unfused", False))
+    scaling = "strong" if wl.get("strong") else "weak"
 
     if world > 1:
         import datetime
@@ -628,7 +655,7 @@ def main() -> None:
                           "events on the launching stream")
         out = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
-            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": dtype, "data": "synthetic",
             "config": {"workload": wl["desc"], "global_batch": (batch if batch <= 16 else 1) * world,
                        "seq_len": 1 if batch <= 16 else batch,
