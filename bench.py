@@ -74,6 +74,14 @@ LLAMA3_70B = [  # one Llama-3-70B layer: hidden 8192, 64 / 8 heads of 128, FFN 2
 ]
 
 
+def shard_rows(mats, world: int):
+    """Strong scaling: rank-local shapes when every projection's n rows are
+    split evenly over `world` ranks (whole quant blocks per row)."""
+    if any(n % world for _, _, n, _, _ in mats):
+        raise ValueError(f"row counts must divide by {world}")
+    return [(nm, q, n // world, k, g) for nm, q, n, k, g in mats]
+
+
 def qwen2_7b_decode_token():
     """Every projection of one Qwen2-7B decode token in the Q4_K_M mix: 28
     layers, Q4_K everywhere except v and down in half of the layers (Q6_K),
@@ -344,9 +352,7 @@ def main() -> None:
     # strong scaling: the workload is one whole layer, each rank owns n / N
     # rows of every projection (whole quant blocks per row)
     if wl.get("strong") and world > 1:
-        if any(n % world for _, _, n, _, _ in mats):
-            raise SystemExit(f"{args.workload}: row counts must divide by {world}")
-        mats = [(nm, q, n // world, k, g) for nm, q, n, k, g in mats]
+        mats = shard_rows(mats, world)
         step_bytes = algorithmic_bytes(mats, batch, fused=not getattr(args, "unfused", False))
     scaling = "strong" if wl.get("strong") else "weak"
 

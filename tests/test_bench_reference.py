@@ -10,6 +10,8 @@ import os
 import subprocess
 import sys
 
+import pytest
+
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
@@ -26,3 +28,22 @@ def test_reference_arm_prints_one_contract_line():
     assert d["config"]["workload"].startswith("config 1: Q8_0 4096x4096")
     assert d["cpu_baseline"]["kind"] in ("reference", "port") and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"] == {"value": d["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_strong_scaling_shards_whole_layer():
+    """The config-5 workload splits each projection's rows over the ranks;
+    the shards of all ranks add back to the whole layer's bytes."""
+    sys.path.insert(0, REPO)
+    import bench
+
+    mats = bench.WORKLOADS["layer_llama70b"]["mats"]
+    assert bench.WORKLOADS["layer_llama70b"]["strong"]
+    full = bench.algorithmic_bytes(mats, 1)
+    for world in (1, 2, 4, 8):
+        local = bench.shard_rows(mats, world)
+        assert [m[2] * world for m in local] == [m[2] for m in mats]
+        weights = sum(bench.synth.weight_bytes(q, n, k) for _, q, n, k, _ in local) * world
+        assert weights == sum(bench.synth.weight_bytes(q, n, k) for _, q, n, k, _ in mats)
+    assert full > 480e6
+    with pytest.raises(ValueError):
+        bench.shard_rows(mats, 3)
