@@ -305,6 +305,8 @@ def main() -> None:
                     help="N > 1: assemble row shards with NCCL all-gathers instead of the gather fused into the GEMV")
     ap.add_argument("--unfused", action="store_true",
                     help="one launch per projection, each with its own x (no shared-x fusion)")
+    ap.add_argument("--batch1-int16", action="store_true",
+                    help="batch 1 on the 16-bit activation grid kernel (dp4a) instead of fp32 activations")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -367,6 +369,8 @@ def main() -> None:
         torch.cuda.set_device(0)
     dev = torch.cuda.current_device()
     lib = _lib.load()
+    if args.batch1_int16:
+        _lib.set_option("batch1_int16", 1)
     be = CudaBackend(dev)
     if not be.available:
         raise RuntimeError(f"CUDA backend unavailable: {be._load_error}")
@@ -639,7 +643,7 @@ def main() -> None:
         # tensor-core GEMV (pre-pass + main), more: tcgen05 GEMM (fp16 pre-pass
         # + main)
         if batch == 1:
-            kname, dtype, calls_per_group = "gemv_i8", "s8 x s8 -> s32, fp32 scales", lambda g: 1
+            kname, dtype, calls_per_group = "gemv_b1 (fp32 activations)", "f32", lambda g: 1
         elif batch <= 16:
             kname, dtype, calls_per_group = "gemv_mma", "s8 x s8 -> s32 (mma.sync), fp32 scales", lambda g: 2 * len(g)
         else:

@@ -22,6 +22,9 @@ FRC_ERR_UNSUPPORTED = 5
 QUANT_IDS = {"Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "Q1_0": 41}
 QUANT_NAMES = {v: k for k, v in QUANT_IDS.items()}
 
+# frc_set_option ids (include/frcuda.h FRC_OPT_*)
+OPTIONS = {"batch1_int16": 1, "batched_fp32": 2, "prefill_tc": 3, "prefill_splits": 4, "inject_oom": 5}
+
 _i = ctypes.c_int
 _i64 = ctypes.c_int64
 _sz = ctypes.c_size_t
@@ -39,6 +42,9 @@ SIGNATURES: dict[str, list] = {
     "frc_block_geometry": [_i, ctypes.POINTER(_i), ctypes.POINTER(_i)],
     "frc_weight_nbytes": [_i, _i64, _i64, ctypes.POINTER(_sz)],
     "frc_device_status": [_i, ctypes.POINTER(ctypes.c_uint32)],
+    "frc_set_option": [_i, _i],
+    "frc_get_option": [_i, ctypes.POINTER(_i)],
+    "frc_noalloc_status": [_i, ctypes.POINTER(ctypes.c_uint32)],
     "frc_gemv": [_i, _p, _sz, _i64, _i64, _p, _i64, _p, _p],
     "frc_gemv_noalloc": [_i, _p, _sz, _i64, _i64, _p, _i64, _p, _p],
     "frc_ipc_alloc": [_sz, ctypes.POINTER(_p), _p],
@@ -130,3 +136,35 @@ def device_count() -> int:
     if rc != FRC_OK:
         return 0
     return int(n.value)
+
+
+def set_option(name: str, value: int) -> int:
+    """Set a library option (frc_set_option); returns the previous value."""
+    lib = load()
+    old = ctypes.c_int(0)
+    check(lib.frc_get_option(OPTIONS[name], ctypes.byref(old)), lib)
+    check(lib.frc_set_option(OPTIONS[name], int(value)), lib)
+    return int(old.value)
+
+
+def get_option(name: str) -> int:
+    lib = load()
+    v = ctypes.c_int(0)
+    check(lib.frc_get_option(OPTIONS[name], ctypes.byref(v)), lib)
+    return int(v.value)
+
+
+class option:
+    """Context manager: `with option("batch1_int16", 1): ...` sets a library
+    option for the block and restores the previous value after it."""
+
+    def __init__(self, name: str, value: int):
+        self.name, self.value, self.old = name, value, None
+
+    def __enter__(self):
+        self.old = set_option(self.name, self.value)
+        return self
+
+    def __exit__(self, *exc):
+        set_option(self.name, self.old)
+        return False

@@ -1,21 +1,14 @@
 // GGUF block formats on the device: geometry, bit-exact dequantisation and the
-// fused dequant-dot of one "unit" used by the GEMV kernels.
+// exact decode of one "unit" used by the batched fp32 GEMV.
 //
 // Block layouts and element order follow the reference decoders in
 // src/flatrun/dequant/gguf.py (Q8_0 :112-127, Q4_K :166-220, Q5_K :223-263,
 // Q1_0 :266-299, Q6_K :365-420; scale/min unpack :135-163).
 //
-// A GEMV "unit" is the slice of one block that one thread turns into a partial
-// dot product.  Every unit covers NRUN runs of 16 consecutive elements of the
-// row, so its activations load as float4s and its per-run activation sums
-// (needed by the offset terms below) are computed once per thread.
-//
-// Fast decode.  A quant value u in [0, 127] is turned into a float with one
-// byte permute: 0x3F80_0000 | (u << 16) == 1 + u/128 exactly.  With
-// A = sum(f * x) and X = sum(x) over a run, sum(u * x) = 128 * (A - X); the
-// scale (and any offset such as Q6_K's -32, or K-quant mins) is applied once
-// per run.  Q8_0 quants are signed 8-bit, so they go through 2^23 + (q ^ 0x80)
-// and an exact subtraction instead.
+// A "unit" here is the slice of one block that one thread of the batched
+// fp32 kernel (gemv_xb) decodes into registers: NRUN runs of 16 consecutive
+// elements of the row, so its activations load as float4s.  The batch-1
+// kernel's units (64 or 32 elements) are defined in units_dp4a.cuh.
 #pragma once
 
 #include "frc_common.cuh"
@@ -141,151 +134,6 @@ template <> FRC_DEVICE_INLINE int run_start<kQ5_K>(int j, int r) { return 64 * (
 template <> FRC_DEVICE_INLINE int run_start<kQ6_K>(int j, int r) { return 128 * (j >> 1) + 32 * r + 16 * (j & 1); }
 // Q1_0 unit j: sign bytes 4j..4j+3, elements 32j + [0,32).
 template <> FRC_DEVICE_INLINE int run_start<kQ1_0>(int j, int r) { return 32 * j + 16 * r; }
-
-// ---------------------------------------------------------------------------
-// Fused dot of one unit.  xv: the unit's NRUN*16 activations in run order;
-// xs: their per-run sums.  `blk` points into shared memory.
-// ---------------------------------------------------------------------------
-
-// sum over 4 bytes (already ORed with 0x80) of (1 + u/128) * x, as two lanes.
-FRC_DEVICE_INLINE float2 acc4_unit(uint32_t w, const float* x, float2 acc) {
-  const float2 f01 = make_float2(byte_as_unit_float<0>(w), byte_as_unit_float<1>(w));
-  const float2 f23 = make_float2(byte_as_unit_float<2>(w), byte_as_unit_float<3>(w));
-  acc = __ffma2_rn(f01, make_float2(x[0], x[1]), acc);
-  acc = __ffma2_rn(f23, make_float2(x[2], x[3]), acc);
-  return acc;
-}
-
-FRC_DEVICE_INLINE float run_sum16(const uint32_t (&w)[4], const float* x) {
-  float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
-  a = acc4_unit(w[0], x + 0, a);
-  b = acc4_unit(w[1], x + 4, b);
-  a = acc4_unit(w[2], x + 8, a);
-  b = acc4_unit(w[3], x + 12, b);
-  return (a.x + b.x) + (a.y + b.y);
-}
-
-template <int Q> struct UnitDot;
-
-template <> struct UnitDot<kQ4_K> {
-  static FRC_DEVICE_INLINE float dot(const uint8_t* blk, int j, const float* xv, const float* xs) {
-    const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-    const uint4 qs = *reinterpret_cast<const uint4*>(blk + 16 + 32 * (j >> 1) + 16 * (j & 1));
-    const float d = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
-    float sc0, m0, sc1, m1;
-    scale_min_k4_words(2 * (j >> 1), hdr.y, hdr.z, hdr.w, sc0, m0);
-    scale_min_k4_words(2 * (j >> 1) + 1, hdr.y, hdr.z, hdr.w, sc1, m1);
-    const uint32_t q[4] = {qs.x, qs.y, qs.z, qs.w};
-    uint32_t lo[4], hi[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      lo[i] = (q[i] & 0x0F0F0F0Fu) | 0x80808080u;
-      hi[i] = ((q[i] >> 4) & 0x0F0F0F0Fu) | 0x80808080u;
-    }
-    const float a0 = run_sum16(lo, xv), a1 = run_sum16(hi, xv + 16);
-    const float ds = d * 128.0f;
-    return ds * (sc0 * (a0 - xs[0]) + sc1 * (a1 - xs[1])) - dmin * (m0 * xs[0] + m1 * xs[1]);
-  }
-};
-
-template <> struct UnitDot<kQ5_K> {
-  static FRC_DEVICE_INLINE float dot(const uint8_t* blk, int j, const float* xv, const float* xs) {
-    const int g = j >> 1, h = j & 1;
-    const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-    const uint4 qh = *reinterpret_cast<const uint4*>(blk + 16 + 16 * h);
-    const uint4 qs = *reinterpret_cast<const uint4*>(blk + 48 + 32 * g + 16 * h);
-    const float d = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
-    float sc0, m0, sc1, m1;
-    scale_min_k4_words(2 * g, hdr.y, hdr.z, hdr.w, sc0, m0);
-    scale_min_k4_words(2 * g + 1, hdr.y, hdr.z, hdr.w, sc1, m1);
-    const uint32_t q[4] = {qs.x, qs.y, qs.z, qs.w};
-    const uint32_t b[4] = {qh.x, qh.y, qh.z, qh.w};
-    uint32_t lo[4], hi[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t b0 = ((b[i] >> (2 * g)) & 0x01010101u) << 4;
-      const uint32_t b1 = ((b[i] >> (2 * g + 1)) & 0x01010101u) << 4;
-      lo[i] = (q[i] & 0x0F0F0F0Fu) | b0 | 0x80808080u;
-      hi[i] = ((q[i] >> 4) & 0x0F0F0F0Fu) | b1 | 0x80808080u;
-    }
-    const float a0 = run_sum16(lo, xv), a1 = run_sum16(hi, xv + 16);
-    const float ds = d * 128.0f;
-    return ds * (sc0 * (a0 - xs[0]) + sc1 * (a1 - xs[1])) - dmin * (m0 * xs[0] + m1 * xs[1]);
-  }
-};
-
-template <> struct UnitDot<kQ6_K> {
-  static FRC_DEVICE_INLINE float dot(const uint8_t* blk, int j, const float* xv, const float* xs) {
-    const int half = j >> 1, lh = j & 1;
-    uint32_t qa[4], qb[4], qh[4], sw[2];
-    lds_words_a2<4>(blk + 64 * half + 16 * lh, qa);        // ql[l]
-    lds_words_a2<4>(blk + 64 * half + 32 + 16 * lh, qb);   // ql[l+32]
-    lds_words_a2<4>(blk + 128 + 32 * half + 16 * lh, qh);  // qh[l]
-    lds_words_a2<2>(blk + 192 + 8 * half, sw);             // this half's 8 scales
-    const float d = half_bits_to_float(ld_u16(blk + 208));
-    uint32_t u0[4], u1[4], u2[4], u3[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      u0[i] = (qa[i] & 0x0F0F0F0Fu) | ((qh[i] << 4) & 0x30303030u) | 0x80808080u;
-      u1[i] = (qb[i] & 0x0F0F0F0Fu) | ((qh[i] << 2) & 0x30303030u) | 0x80808080u;
-      u2[i] = ((qa[i] >> 4) & 0x0F0F0F0Fu) | (qh[i] & 0x30303030u) | 0x80808080u;
-      u3[i] = ((qb[i] >> 4) & 0x0F0F0F0Fu) | ((qh[i] >> 2) & 0x30303030u) | 0x80808080u;
-    }
-    // scale of quarter r for this l-range: scales[8*half + 2r + lh]
-    const uint32_t sA = sw[0] >> (8 * lh), sB = sw[1] >> (8 * lh);
-    const float s0 = static_cast<float>(static_cast<int8_t>(sA & 0xFF));
-    const float s1 = static_cast<float>(static_cast<int8_t>((sA >> 16) & 0xFF));
-    const float s2 = static_cast<float>(static_cast<int8_t>(sB & 0xFF));
-    const float s3 = static_cast<float>(static_cast<int8_t>((sB >> 16) & 0xFF));
-    const float a0 = run_sum16(u0, xv), a1 = run_sum16(u1, xv + 16);
-    const float a2 = run_sum16(u2, xv + 32), a3 = run_sum16(u3, xv + 48);
-    // sum((u - 32) x) = 128 (A - X) - 32 X
-    const float t0 = 128.0f * (a0 - xs[0]) - 32.0f * xs[0];
-    const float t1 = 128.0f * (a1 - xs[1]) - 32.0f * xs[1];
-    const float t2 = 128.0f * (a2 - xs[2]) - 32.0f * xs[2];
-    const float t3 = 128.0f * (a3 - xs[3]) - 32.0f * xs[3];
-    return d * ((s0 * t0 + s1 * t1) + (s2 * t2 + s3 * t3));
-  }
-};
-
-template <> struct UnitDot<kQ8_0> {
-  static FRC_DEVICE_INLINE float dot(const uint8_t* blk, int, const float* xv, const float*) {
-    uint32_t q[8];
-    lds_words_a2<8>(blk + 2, q);
-    const float d = half_bits_to_float(ld_u16(blk));
-    const float2 bias = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
-    float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t u = q[i] ^ 0x80808080u;  // q + 128 as unsigned bytes
-      const float2 f01 = __fadd2_rn(make_float2(byte_as_magic_float<0>(u), byte_as_magic_float<1>(u)), bias);
-      const float2 f23 = __fadd2_rn(make_float2(byte_as_magic_float<2>(u), byte_as_magic_float<3>(u)), bias);
-      a = __ffma2_rn(f01, make_float2(xv[4 * i], xv[4 * i + 1]), a);
-      b = __ffma2_rn(f23, make_float2(xv[4 * i + 2], xv[4 * i + 3]), b);
-    }
-    return d * ((a.x + b.x) + (a.y + b.y));
-  }
-};
-
-template <> struct UnitDot<kQ1_0> {
-  static FRC_DEVICE_INLINE float dot(const uint8_t* blk, int j, const float* xv, const float* xs) {
-    // sum(s_i x_i) with s = +-1 equals 2 * sum(x_i over set bits) - sum(x_i)
-    const uint32_t bits = ld_u32_a2(blk + 2 + 4 * j);
-    const float d = half_bits_to_float(ld_u16(blk));
-    float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-      const float f0 = __uint_as_float((0u - ((bits >> i) & 1u)) & 0x3F800000u);
-      const float f1 = __uint_as_float((0u - ((bits >> (i + 1)) & 1u)) & 0x3F800000u);
-      const float f2 = __uint_as_float((0u - ((bits >> (i + 2)) & 1u)) & 0x3F800000u);
-      const float f3 = __uint_as_float((0u - ((bits >> (i + 3)) & 1u)) & 0x3F800000u);
-      a = __ffma2_rn(make_float2(f0, f1), make_float2(xv[i], xv[i + 1]), a);
-      b = __ffma2_rn(make_float2(f2, f3), make_float2(xv[i + 2], xv[i + 3]), b);
-    }
-    const float set = (a.x + b.x) + (a.y + b.y);
-    return d * (2.0f * set - (xs[0] + xs[1]));
-  }
-};
 
 // ---------------------------------------------------------------------------
 // Exact decode of a unit's elements (used by the batched kernel, which shares

@@ -1,5 +1,6 @@
-// Shared device helpers: mbarriers, bulk async copies, bounded waits, byte
-// extraction.  Everything here targets sm_100a only.
+// Shared device helpers: mbarriers, bulk async copies, byte extraction.  The
+// kernels bound every wait by wall-clock time (%globaltimer, gemv.cuh
+// wait_phase), not by a poll count.  Everything here targets sm_100a only.
 #pragma once
 
 #include <cstdint>
@@ -19,12 +20,6 @@ enum : uint32_t {
   kStatusSmemMisaligned   = 1u << 3,  // dynamic shared memory not 128-byte aligned (kernel skipped)
   kStatusGatherTimeout    = 1u << 4,  // a fused all-gather wait gave up on a rank's flag
 };
-
-// Upper bound on polls of one mbarrier phase.  Each poll is a try_wait with
-// a hardware suspend hint, so this bounds a wait to well under a second
-// while never triggering on a healthy pipeline (a stage completes in
-// microseconds).
-constexpr uint32_t kMaxPolls = 1u << 22;
 
 FRC_DEVICE_INLINE uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -57,15 +52,6 @@ FRC_DEVICE_INLINE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
       : "memory");
   return ok != 0;
-}
-
-// Wait until the phase with the given parity has completed; false if the
-// poll budget ran out (the caller records it and stops).
-FRC_DEVICE_INLINE bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kMaxPolls; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-  }
-  return false;
 }
 
 // 1-D bulk copy global -> shared, completion signalled on `bar` as tx bytes.

@@ -239,7 +239,7 @@ int gemv_device(DeviceState* ds, int quant, const uint8_t* w, int64_t n, int64_t
   }
   // more than kMaxGemvBatch columns: the tensor-core prefill GEMM, if the
   // shape suits it (FRC_TC=0 turns it off)
-  if (seq > kMaxGemvBatch && frc::env_int("FRC_TC", 1)) {
+  if (seq > kMaxGemvBatch && frc::opt(frc::options().prefill_tc)) {
     frc::GemvRequest r{};
     r.w = w;
     r.x = x;
@@ -425,7 +425,8 @@ int stateless_dequant(int quant, const uint8_t* w, size_t w_bytes, int64_t out_d
 constexpr size_t kNoAllocRecordBytes = FRC_NOALLOC_SCRATCH_BYTES;
 static __device__ __align__(256) uint8_t g_noalloc_records[kNoAllocRecordBytes];
 // Bounded-wait status of the kernels this entry point launches; zero when the
-// module loads (kernels only OR bits into it).
+// module loads (kernels only OR bits into it), read and cleared by
+// frc_noalloc_status.
 static __device__ uint32_t g_noalloc_status;
 
 struct NoAllocDevice {
@@ -520,6 +521,34 @@ int frc_device_status(int device, uint32_t* flags) {
   return FRC_OK;
 }
 
+int frc_set_option(int option, int value) {
+  frc::Options& o = frc::options();
+  switch (option) {
+    case FRC_OPT_BATCH1_INT16: o.batch1_int16.store(value ? 1 : 0); return FRC_OK;
+    case FRC_OPT_BATCHED_FP32: o.batched_fp32.store(value ? 1 : 0); return FRC_OK;
+    case FRC_OPT_PREFILL_TC: o.prefill_tc.store(value ? 1 : 0); return FRC_OK;
+    case FRC_OPT_PREFILL_SPLITS:
+      if (value < 0) return fail(FRC_ERR_INVALID, "frc_set_option: prefill splits must be >= 0 (got %d)", value);
+      o.prefill_splits.store(value);
+      return FRC_OK;
+    case FRC_OPT_INJECT_OOM: o.inject_oom.store(value ? 1 : 0); return FRC_OK;
+    default: return fail(FRC_ERR_INVALID, "frc_set_option: unknown option %d", option);
+  }
+}
+
+int frc_get_option(int option, int* value) {
+  if (!value) return fail(FRC_ERR_INVALID, "null pointer");
+  const frc::Options& o = frc::options();
+  switch (option) {
+    case FRC_OPT_BATCH1_INT16: *value = frc::opt(o.batch1_int16); return FRC_OK;
+    case FRC_OPT_BATCHED_FP32: *value = frc::opt(o.batched_fp32); return FRC_OK;
+    case FRC_OPT_PREFILL_TC: *value = frc::opt(o.prefill_tc); return FRC_OK;
+    case FRC_OPT_PREFILL_SPLITS: *value = frc::opt(o.prefill_splits); return FRC_OK;
+    case FRC_OPT_INJECT_OOM: *value = frc::opt(o.inject_oom); return FRC_OK;
+    default: return fail(FRC_ERR_INVALID, "frc_get_option: unknown option %d", option);
+  }
+}
+
 int frc_gemv(int quant, const void* w_dev, size_t w_bytes, int64_t n, int64_t k, const float* x_dev, int64_t batch,
              float* y_dev, void* stream) {
   int rc = check_matmul(quant, w_bytes, n, k, batch);
@@ -579,6 +608,23 @@ int frc_gemv_noalloc(int quant, const void* w_dev, size_t w_bytes, int64_t n, in
   r.sms = d->sms;
   r.xrec = d->records;
   return launch_gemv_quant(quant, r);
+}
+
+int frc_noalloc_status(int device, uint32_t* flags) {
+  if (!flags) return fail(FRC_ERR_INVALID, "null pointer");
+  int count = 0;
+  FRC_CUDA(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+  if (device < 0 || device >= count) return fail(FRC_ERR_INVALID, "device %d out of range (%d devices)", device, count);
+  DeviceGuard g;
+  FRC_CUDA(g.set(device), "cudaSetDevice");
+  int dev = 0;
+  NoAllocDevice* d = nullptr;
+  int rc = noalloc_device(&dev, &d);
+  if (rc) return rc;
+  FRC_CUDA(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  FRC_CUDA(cudaMemcpy(flags, d->status, sizeof(uint32_t), cudaMemcpyDeviceToHost), "status read");
+  FRC_CUDA(cudaMemset(d->status, 0, sizeof(uint32_t)), "status clear");
+  return FRC_OK;
 }
 
 int frc_gemv_multi(int quant, int count, const void* const* w_dev, const size_t* w_bytes, const int64_t* n,
@@ -646,7 +692,7 @@ int frc_weight_create(int device, int quant, const void* host, size_t nbytes, in
   int rc = check_matmul(quant, nbytes, n, k, 1);
   if (rc) return rc;
   if (nbytes && !host) return fail(FRC_ERR_INVALID, "null host buffer");
-  if (frc::env_int("FRC_FAULT_INJECT_OOM", 0)) return fail(FRC_ERR_NOMEM, "weight upload: injected allocation failure");
+  if (frc::opt(frc::options().inject_oom)) return fail(FRC_ERR_NOMEM, "weight upload: injected allocation failure");
   DeviceState* ds;
   rc = device_state(device, &ds);
   if (rc) return rc;

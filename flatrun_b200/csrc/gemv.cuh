@@ -1,34 +1,35 @@
 // Fused dequantise + GEMV kernels for GGUF row-major weights.
 //
-// Both kernels are persistent and warp-specialised:
-//  * the last warp is the producer: one lane streams tiles of `RT` consecutive
-//    rows (a contiguous byte range of the weight) into a ring of shared-memory
-//    stages with cp.async.bulk, signalling each stage's mbarrier;
-//  * the other warps are consumers.  Consumer thread t owns the units
-//    t, t + NCT, t + 2*NCT, ... of every row (a unit is a fixed slice of one
-//    block, see formats.cuh), so it decodes the same columns of each row of
-//    every tile.
+// gemv_b1 (batch 1, the decode path) streams weight rows through shared
+// memory in independent per-slot pipelines (described above the kernel).  Its
+// activation arithmetic is a template parameter: exact fp32 activations and
+// fp32 products (units_f32.cuh, the reference's arithmetic and the default),
+// or activations on a 16-bit integer grid with dp4a products
+// (units_dp4a.cuh, opt-in).
+//
+// gemv_xb (batch 2..16, exact fp32 activations) is persistent and
+// warp-specialised: the last warp is the producer (one lane streams tiles of
+// RT consecutive rows into a ring of shared-memory stages with cp.async.bulk,
+// signalling each stage's mbarrier), the others are consumers; consumer
+// thread t owns the units t, t + NCT, ... of every row, decodes each unit once
+// per row and reuses it for every activation column (read through L1).
+//
 // Each CTA owns the contiguous rows [c*n/G, (c+1)*n/G), which balances work
 // to within one row; a tile's global start is rounded down to 16 bytes for
 // the bulk copy (its offset is kept in shared memory), and the <16-byte tail
-// of the last tile is copied by the producer lane.
-//
-// gemv_x1: batch 1.  A consumer keeps its units' activations (and their
-//   16-element sums) in registers for the whole launch, so x is read from
-//   global memory once per CTA and the inner loop touches only the weight
-//   stream in shared memory.
-// gemv_xb: batch 2..16.  Each unit is decoded once per row into registers and
-//   reused for every activation column, which are read through L1.
-//
-// Per-row partial sums are reduced with a register-transpose butterfly
-// (V-1 shuffles for V rows), across warps through shared memory, and written
-// by warp 0.  Every mbarrier wait is bounded by wall-clock time; on a timeout
-// the CTA raises a shared abort flag, records a status bit, stops computing
-// and still passes every barrier, so it always exits.
+// of the last tile is copied by the issuing thread.  Per-row partial sums are
+// reduced with a register-transpose butterfly (V-1 shuffles for V rows), then
+// across warps through shared memory.  Every mbarrier wait is bounded by
+// wall-clock time (kWaitLimitNs, read from %globaltimer); on a timeout the CTA
+// raises a shared abort flag, records a status bit, stops computing and still
+// passes every barrier, so it always exits.
 #pragma once
+
+#include <type_traits>
 
 #include "formats.cuh"
 #include "units_dp4a.cuh"
+#include "units_f32.cuh"
 
 namespace frc {
 
@@ -47,16 +48,16 @@ struct GemvParams {
   int units;          // units per row
   int stage_stride;   // bytes per shared-memory stage
   int nstage;
-  int wps;            // gemv_i8: warps per slot (one slot covers one row's units)
-  int pre_stages;     // gemv_i8: stages per slot filled before the grid dependency wait
+  int wps;            // gemv_b1: warps per slot (one slot covers one row's units)
+  int pre_stages;     // gemv_b1: stages per slot filled before the grid dependency wait
   uint32_t* status;   // device status word
-  // gemv_i8 row space: nmat matrices sharing x and k, rows concatenated;
+  // gemv_b1 row space: nmat matrices sharing x and k, rows concatenated;
   // matrix m covers rows [mat_end[m-1], mat_end[m]) of the n rows
   int nmat;
   int64_t mat_end[4];
   const uint8_t* mat_w[4];  // each 16-byte aligned
   float* mat_y[4];
-  // gemv_i8 fused all-gather (g_world > 1): every y value is also stored at
+  // gemv_b1 fused all-gather (g_world > 1): every y value is also stored at
   // the same offset from g_peer_y[r] as from g_ybase, for each rank r (the
   // rank's shard in r's gathered buffer, over NVLink for r != this rank);
   // the last slot of the grid to finish publishes the group's next epoch in
@@ -67,7 +68,7 @@ struct GemvParams {
   uint32_t* g_flags[kMaxGatherRanks];
   uint32_t* g_done;   // slots finished in this launch (reset by the last)
   uint32_t* g_epoch;  // gathers completed by this rank
-  // gemv_i8: before reading x, wait until every rank has published the
+  // gemv_b1: before reading x, wait until every rank has published the
   // epoch of an earlier fused gather (w_world > 1): x may be its output
   int w_world;
   const uint32_t* w_flags;
@@ -202,107 +203,13 @@ FRC_DEVICE_INLINE void load_run16(const float* src, float* dst) {
 }
 
 // ---------------------------------------------------------------------------
-// batch 1, activations in registers
-// ---------------------------------------------------------------------------
-template <int Q, int UPT, int RT>
-__global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1) gemv_x1(GemvParams p) {
-  using F = Fmt<Q>;
-  constexpr int E = 16 * F::NRUN;
-  extern __shared__ __align__(128) uint8_t smem[];
-  const SmemLayout L = carve<RT>(smem, p.nstage);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ncw = static_cast<int>(blockDim.x >> 5) - 1;
-  const int nct = ncw * 32;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < p.nstage; ++s) {
-      mbar_init(&L.full[s], 1);
-      mbar_init(&L.empty[s], ncw);
-    }
-    *L.abort = 0;
-    fence_barrier_init();
-  }
-  __syncthreads();
-
-  int64_t r0, r1;
-  cta_rows(p.n, r0, r1);
-
-  if (warp == ncw) {
-    if (lane == 0) produce(p, L, r0, r1, RT);
-    return;
-  }
-
-  // --- consumer: activations of the owned units, kept in registers --------
-  const int ct = threadIdx.x;
-  float xv[UPT][E];
-  float xs[UPT][F::NRUN];
-  int uoff[UPT], uj[UPT];
-  bool uval[UPT];
-#pragma unroll
-  for (int i = 0; i < UPT; ++i) {
-    const int u = ct + i * nct;
-    uval[i] = u < p.units;
-    const int b = uval[i] ? u / F::UPB : 0;
-    uj[i] = uval[i] ? u % F::UPB : 0;
-    uoff[i] = b * F::TS;
-#pragma unroll
-    for (int r = 0; r < F::NRUN; ++r) {
-      if (uval[i]) {
-        load_run16(p.x + static_cast<int64_t>(b) * F::QK + run_start<Q>(uj[i], r), &xv[i][16 * r]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 16; ++e) xv[i][16 * r + e] = 0.f;
-      }
-      float s = 0.f;
-#pragma unroll
-      for (int e = 0; e < 16; ++e) s += xv[i][16 * r + e];
-      xs[i][r] = s;
-    }
-  }
-
-  volatile int* abort = L.abort;
-  int it = 0;
-  for (int64_t t0 = r0; t0 < r1; t0 += RT, ++it) {
-    const int s = it % p.nstage;
-    const uint32_t ph = static_cast<uint32_t>(it / p.nstage) & 1u;
-    const int rows = static_cast<int>((t0 + RT < r1 ? t0 + RT : r1) - t0);
-    float acc[RT];
-#pragma unroll
-    for (int r = 0; r < RT; ++r) acc[r] = 0.f;
-    if (wait_phase(&L.full[s], ph, abort)) {
-      const uint8_t* base = L.stages + static_cast<size_t>(s) * p.stage_stride +
-                            ((static_cast<uint64_t>(t0) * p.row_bytes) & 15u);
-#pragma unroll
-      for (int r = 0; r < RT; ++r) {
-        if (r < rows) {
-          const uint8_t* row = base + r * p.row_bytes;
-#pragma unroll
-          for (int i = 0; i < UPT; ++i) {
-            if (uval[i]) acc[r] += UnitDot<Q>::dot(row + uoff[i], uj[i], xv[i], xs[i]);
-          }
-        }
-      }
-    } else {
-      atomicOr(p.status, kStatusFullWaitTimeout);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&L.empty[s]);
-
-    butterfly<RT>(acc, lane);
-    float* red = L.red + (it & 1) * kMaxConsumerWarps * RT;
-    constexpr int kLanesPerValue = 32 / RT;
-    if ((lane & (kLanesPerValue - 1)) == 0) red[warp * RT + lane / kLanesPerValue] = acc[0];
-    named_barrier_sync(1, nct);
-    if (warp == 0 && lane < rows) {
-      float v = 0.f;
-      for (int w = 0; w < ncw; ++w) v += red[w * RT + lane];
-      if (!*abort) p.y[t0 + lane] = v;
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
-// batch 1, activations quantised to a 16-bit integer split, dp4a dot products
+// batch 1: gemv_b1<Q, UPT, RPS, F32>
+//
+// F32 = true: every thread keeps its units' fp32 activations in registers
+// (UnitXF, loaded straight from global memory) and UnitDotF32 multiplies them
+// with the decoded quants in fp32.  F32 = false: each CTA quantises x once into
+// shared-memory records on a 16-bit integer grid (quantise_words), each thread
+// copies its units' records into registers (UnitX) and UnitDotI8 runs dp4a.
 //
 // Every warp of the CTA computes; there is no producer warp.  The warps form
 // slots of p.wps warps, and each slot is an independent pipeline: it owns a
@@ -363,11 +270,14 @@ FRC_DEVICE_INLINE int count_tiles(const GemvParams& p, int64_t r0, int64_t r1, i
 }
 
 // Warps per CTA at most, from the activation registers a thread holds (UPT
-// records of 2 E/4 + NG + 1 words): 16 warps (128 registers each) up to 72
-// activation registers, 12 warps (168 registers) beyond.
-template <int Q, int UPT>
-__host__ __device__ constexpr int i8_max_warps() {
-  return UPT * (2 * I8<Q>::E / 4 + I8<Q>::NG + 1) <= 72 ? 16 : 12;
+// units of 2 E/4 + NG + 1 words on the integer grid, E + NG in fp32): 16 warps
+// (128 registers each) up to 72 activation registers, 12 warps (168
+// registers) beyond.  One fp32 K-quant unit (66 registers) fits the 128
+// (ptxas: no spills for Q4_K, Q6_K, Q8_0, Q1_0; a few bytes for Q5_K at
+// four- and eight-row tiles).
+template <int Q, int UPT, bool F32>
+__host__ __device__ constexpr int b1_max_warps() {
+  return UPT * (F32 ? I8<Q>::E + I8<Q>::NG : 2 * I8<Q>::E / 4 + I8<Q>::NG + 1) <= 72 ? 16 : 12;
 }
 
 FRC_DEVICE_INLINE void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -409,10 +319,18 @@ FRC_DEVICE_INLINE void gather_arrive(const GemvParams& p, int slots) {
   }
 }
 
-template <int Q, int UPT, int RPS>
-__global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvParams p) {
-  using F = Fmt<Q>;
-  constexpr int RW = record_words<Q>();
+template <int Q, bool F32, typename XU>
+FRC_DEVICE_INLINE float unit_dot(uint32_t row, const UnitCtx& c, const XU& x) {
+  if constexpr (F32) {
+    return UnitDotF32<Q>::dot(row, c, x);
+  } else {
+    return UnitDotI8<Q>::dot(row, c, x);
+  }
+}
+
+template <int Q, int UPT, int RPS, bool F32>
+__global__ void __launch_bounds__(b1_max_warps<Q, UPT, F32>() * 32, 1) gemv_b1(GemvParams p) {
+  constexpr int RW = F32 ? 0 : record_words<Q>();
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = static_cast<int>(blockDim.x >> 5);
@@ -482,8 +400,32 @@ __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvPa
     __syncthreads();
   }
 
-  // the x loads of a row of up to 16 R blockDim.x elements in one round trip
-  quantise_words<Q, i8_max_warps<Q, UPT>() == 16 ? 3 : 4>(p.x, p.units, records);
+  UnitCtx cx[UPT];
+  bool uval[UPT];
+#pragma unroll
+  for (int i = 0; i < UPT; ++i) {
+    const int u = st + i * spt;
+    uval[i] = u < p.units;
+    cx[i] = make_ctx<Q>(uval[i] ? u % I8<Q>::UPB : 0, uval[i] ? u / I8<Q>::UPB : 0);
+  }
+  using XU = std::conditional_t<F32, UnitXF<Q>, UnitX<Q>>;
+  XU xu[UPT];
+  if constexpr (F32) {
+    // every thread loads its own units' activations (all loads issued here,
+    // consumed after the ring is filled)
+#pragma unroll
+    for (int i = 0; i < UPT; ++i) {
+      const int u = st + i * spt;
+      if (uval[i]) {
+        xu[i].load(p.x, u / I8<Q>::UPB, u % I8<Q>::UPB);
+      } else {
+        xu[i].zero();
+      }
+    }
+  } else {
+    // the x loads of a row of up to 16 R blockDim.x elements in one round trip
+    quantise_words<Q, b1_max_warps<Q, UPT, F32>() == 16 ? 3 : 4>(p.x, p.units, records);
+  }
   // the rest of the ring: issued after x is read, so that the activation
   // loads do not queue behind a full ring of weight copies
   if (st == leader) {
@@ -494,26 +436,22 @@ __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvPa
       next_issue = t.t1;
     }
   }
-  __syncthreads();
+  if constexpr (!F32) __syncthreads();  // the records are complete
   if (ntiles == 0) {  // the whole slot leaves together
     if (st == leader) gather_arrive(p, slots);
     return;
   }
-
-  UnitX<Q> xu[UPT];
-  UnitCtx cx[UPT];
-  bool uval[UPT];
+  if constexpr (F32) {
 #pragma unroll
-  for (int i = 0; i < UPT; ++i) {
-    const int u = st + i * spt;
-    uval[i] = u < p.units;
-    const int b = uval[i] ? u / I8<Q>::UPB : 0;
-    const int j = uval[i] ? u % I8<Q>::UPB : 0;
-    cx[i] = make_ctx<Q>(j, b);
-    if (uval[i]) {
-      xu[i].from_record(records + u * RW);
-    } else {
-      xu[i].zero();
+    for (int i = 0; i < UPT; ++i) xu[i].finish();
+  } else {
+#pragma unroll
+    for (int i = 0; i < UPT; ++i) {
+      if (uval[i]) {
+        xu[i].from_record(records + (st + i * spt) * RW);
+      } else {
+        xu[i].zero();
+      }
     }
   }
 
@@ -542,7 +480,7 @@ __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvPa
           if (uval[i]) {
 #pragma unroll
             for (int r = 0; r < RPS; ++r)
-              acc[r] += UnitDotI8<Q>::dot(base + static_cast<uint32_t>(r * p.row_bytes), cx[i], xu[i]);
+              acc[r] += unit_dot<Q, F32>(base + static_cast<uint32_t>(r * p.row_bytes), cx[i], xu[i]);
           }
         }
       } else {
@@ -552,7 +490,7 @@ __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvPa
             const uint32_t row = base + static_cast<uint32_t>(r * p.row_bytes);
 #pragma unroll
             for (int i = 0; i < UPT; ++i) {
-              if (uval[i]) acc[r] += UnitDotI8<Q>::dot(row, cx[i], xu[i]);
+              if (uval[i]) acc[r] += unit_dot<Q, F32>(row, cx[i], xu[i]);
             }
           }
         }
@@ -622,11 +560,12 @@ __global__ void __launch_bounds__(i8_max_warps<Q, UPT>() * 32, 1) gemv_i8(GemvPa
   }
 }
 
-// Bytes before the stages: barriers, reduction buffers, activation records.
-template <int Q, int RPS>
-__host__ __device__ constexpr int i8_smem_header(int slots, int nst, int wps, int units) {
+// Bytes before the stages: barriers, reduction buffers, activation records
+// (integer grid only).
+template <int Q, int RPS, bool F32>
+__host__ __device__ constexpr int b1_smem_header(int slots, int nst, int wps, int units) {
   return (((slots * nst * 8 + 4 + 15) / 16) * 16 + ((slots * 2 * wps * RPS * 4 + 15) / 16) * 16 +
-          units * record_words<Q>() * 4 + 127) / 128 * 128;
+          units * (F32 ? 0 : record_words<Q>()) * 4 + 127) / 128 * 128;
 }
 
 // ---------------------------------------------------------------------------

@@ -8,6 +8,7 @@
 
 #include <cstdint>
 #include <cstdlib>
+#include <atomic>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -62,12 +63,56 @@ struct DequantRequest {
   int sms;
 };
 
-// Integer knob from the environment (used for tuning sweeps), or `def`.
-inline int env_int(const char* name, int def) {
-  const char* s = std::getenv(name);
-  if (!s || !*s) return def;
-  return std::atoi(s);
+// Library options, set through frc_set_option (include/frcuda.h); read on
+// every launch with relaxed atomics, never from the environment.
+struct Options {
+  std::atomic<int> batch1_int16{0};    // FRC_OPT_BATCH1_INT16
+  std::atomic<int> batched_fp32{0};    // FRC_OPT_BATCHED_FP32
+  std::atomic<int> prefill_tc{1};      // FRC_OPT_PREFILL_TC
+  std::atomic<int> prefill_splits{0};  // FRC_OPT_PREFILL_SPLITS
+  std::atomic<int> inject_oom{0};      // FRC_OPT_INJECT_OOM
+};
+inline Options& options() {
+  static Options o;
+  return o;
 }
+inline int opt(const std::atomic<int>& v) { return v.load(std::memory_order_relaxed); }
+
+// Launch-configuration overrides for tuning sweeps.  They are read from the
+// environment once, at the first launch, and only when FRC_TUNE=1; otherwise
+// every kernel runs its measured default configuration.  -1 = not set.
+struct Tuning {
+  int upt = -1, rps = -1, tile_bytes = -1, nwarps = -1, nstage = -1, smem_bytes = -1, rt = -1, stage_bytes = -1,
+      ctas_per_sm = -1, mma_grid = -1, mma_mt = -1, pre_stages = -1, pdl = -1;
+};
+inline const Tuning& tuning() {
+  static const Tuning t = [] {
+    Tuning v;
+    const char* on = std::getenv("FRC_TUNE");
+    if (!on || std::strcmp(on, "1") != 0) return v;
+    auto get = [](const char* name) {
+      const char* s = std::getenv(name);
+      return (s && *s) ? std::atoi(s) : -1;
+    };
+    v.upt = get("FRC_UPT");
+    v.rps = get("FRC_RPS");
+    v.tile_bytes = get("FRC_TILE_BYTES");
+    v.nwarps = get("FRC_NWARPS");
+    v.nstage = get("FRC_NSTAGE");
+    v.smem_bytes = get("FRC_SMEM_BYTES");
+    v.rt = get("FRC_RT");
+    v.stage_bytes = get("FRC_STAGE_BYTES");
+    v.ctas_per_sm = get("FRC_CTAS_PER_SM");
+    v.mma_grid = get("FRC_MMA_GRID");
+    v.mma_mt = get("FRC_MMA_MT");
+    v.pre_stages = get("FRC_PRE_STAGES");
+    v.pdl = get("FRC_PDL");
+    return v;
+  }();
+  return t;
+}
+// A tuning override if set, else the default.
+inline int tuned(int v, int def) { return v >= 0 ? v : def; }
 
 // Blocks of `kernel` resident per SM with `threads` threads and `smem` bytes,
 // after opting the kernel into `smem` bytes of dynamic shared memory.
@@ -105,10 +150,10 @@ inline int round_up(int v, int m) { return (v + m - 1) / m * m; }
 // Shared-memory stage geometry for tiles of `rt` rows.
 inline void stage_geometry(int row_bytes, int rt, int* stride, int* nstage) {
   *stride = round_up(rt * row_bytes + 32, 128);
-  const int target = env_int("FRC_STAGE_BYTES", 64 * 1024);
+  const int target = tuned(tuning().stage_bytes, 64 * 1024);
   int ns = target / *stride;
   ns = ns < 2 ? 2 : (ns > 8 ? 8 : ns);
-  const int forced = env_int("FRC_NSTAGE", 0);
+  const int forced = tuning().nstage;
   *nstage = forced > 0 ? forced : ns;
 }
 
@@ -118,7 +163,7 @@ inline cudaError_t launch_persistent(K kernel, GemvParams p, int ncw, size_t sme
   int per_sm = 0;
   cudaError_t e = kernel_occupancy(reinterpret_cast<const void*>(kernel), r.device, threads, smem, &per_sm);
   if (e != cudaSuccess) return e;
-  const int cap = env_int("FRC_CTAS_PER_SM", 0);
+  const int cap = tuning().ctas_per_sm;
   if (cap > 0 && cap < per_sm) per_sm = cap;
   int64_t grid = static_cast<int64_t>(per_sm) * r.sms;
   if (grid > p.n) grid = p.n;
@@ -128,26 +173,6 @@ inline cudaError_t launch_persistent(K kernel, GemvParams p, int ncw, size_t sme
 }
 
 inline int rows_per_tile(int row_bytes);
-
-template <int Q, int UPT>
-inline cudaError_t launch_x1(GemvParams p, const GemvRequest& r, int ncw) {
-  const int rt = rows_per_tile(p.row_bytes);
-  stage_geometry(p.row_bytes, rt, &p.stage_stride, &p.nstage);
-  switch (rt) {
-    case 2: {
-      const size_t smem = smem_header_bytes<2>() + static_cast<size_t>(p.nstage) * p.stage_stride;
-      return launch_persistent(gemv_x1<Q, UPT, 2>, p, ncw, smem, r);
-    }
-    case 4: {
-      const size_t smem = smem_header_bytes<4>() + static_cast<size_t>(p.nstage) * p.stage_stride;
-      return launch_persistent(gemv_x1<Q, UPT, 4>, p, ncw, smem, r);
-    }
-    default: {
-      const size_t smem = smem_header_bytes<8>() + static_cast<size_t>(p.nstage) * p.stage_stride;
-      return launch_persistent(gemv_x1<Q, UPT, 8>, p, ncw, smem, r);
-    }
-  }
-}
 
 template <int Q, int RT, int BMAX>
 inline cudaError_t launch_xb_rt(GemvParams p, const GemvRequest& r) {
@@ -163,7 +188,7 @@ inline int rows_per_tile(int row_bytes) {
   int rt = 8;
   if (row_bytes > 4096) rt = 4;
   if (row_bytes > 16384) rt = 2;
-  const int forced = env_int("FRC_RT", 0);
+  const int forced = tuning().rt;
   if (forced == 2 || forced == 4 || forced == 8) rt = forced;
   return rt;
 }
@@ -184,20 +209,21 @@ inline cudaError_t launch_xb(GemvParams p, const GemvRequest& r) {
   }
 }
 
-// Batch-1 integer-dot kernel: slots of `wps` warps each cover one row's units
-// and run independent pipelines; up to 16 warps per CTA.
-template <int Q, int UPT, int RPS>
-inline cudaError_t launch_i8_rps(GemvParams p, const GemvRequest& r, int slots, int nst) {
+// Batch-1 kernel (gemv_b1): slots of `wps` warps each cover one row's units
+// and run independent pipelines; up to 16 warps per CTA.  F32 selects the
+// fp32-activation arithmetic, otherwise the 16-bit integer grid.
+template <int Q, int UPT, int RPS, bool F32>
+inline cudaError_t launch_b1_rps(GemvParams p, const GemvRequest& r, int slots, int nst) {
   p.stage_stride = round_up(RPS * p.row_bytes + 32, 128);
   p.nstage = nst;
   // one stage per slot before the grid dependency wait: a full ring of
   // weight copies in flight delays the activation loads behind it (measured
   // on B200: the Qwen2-7B layer step 43.8 -> 41.8 us)
-  p.pre_stages = env_int("FRC_PRE_STAGES", 1);
+  p.pre_stages = tuned(tuning().pre_stages, 1);
   const size_t smem =
-      i8_smem_header<Q, RPS>(slots, nst, p.wps, p.units) + static_cast<size_t>(slots) * nst * p.stage_stride;
+      b1_smem_header<Q, RPS, F32>(slots, nst, p.wps, p.units) + static_cast<size_t>(slots) * nst * p.stage_stride;
   const int threads = slots * p.wps * 32;
-  const void* fn = reinterpret_cast<const void*>(gemv_i8<Q, UPT, RPS>);
+  const void* fn = reinterpret_cast<const void*>(gemv_b1<Q, UPT, RPS, F32>);
   int per_sm = 0;
   cudaError_t e = kernel_occupancy(fn, r.device, threads, smem, &per_sm);
   if (e != cudaSuccess) return e;
@@ -212,22 +238,23 @@ inline cudaError_t launch_i8_rps(GemvParams p, const GemvRequest& r, int slots, 
   cfg.stream = r.stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = env_int("FRC_PDL", 1) ? 1 : 0;
+  attr[0].val.programmaticStreamSerializationAllowed = tuned(tuning().pdl, 1) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemv_i8<Q, UPT, RPS>, p);
+  return cudaLaunchKernelEx(&cfg, gemv_b1<Q, UPT, RPS, F32>, p);
 }
 
 // Shared memory available to one block (B200: 227 KB opt-in).
 constexpr int kSmemBudget = 227 * 1024;
 
 // Bytes of weights per tile the batch-1 kernel aims for (rows per tile = the
-// largest power of two <= 8 whose tile fits), swept on B200: ~8 KB for short
-// K-quant rows, 12 KB (four 2940-byte rows) for the k = 3584 Q6_K lm_head
-// (4.3 -> 5.1 TB/s), 18 KB (four rows) for k = 4096 Q8_0, 4 KB (four rows) for
-// Q1_0; long rows (k > ~14K for Q4_K) two-row tiles up to 32 KB.
+// largest power of two <= 8 whose tile fits), swept on B200 with the integer
+// kernel: ~8 KB for short K-quant rows, 12 KB (four 2940-byte rows) for the
+// k = 3584 Q6_K lm_head (4.3 -> 5.1 TB/s), 18 KB (four rows) for k = 4096
+// Q8_0, 4 KB (four rows) for Q1_0; long rows (k > ~14K for Q4_K) two-row
+// tiles up to 32 KB.
 template <int Q>
-inline int i8_tile_target(int row_bytes) {
+inline int b1_tile_target(int row_bytes) {
   if (row_bytes > 8192) return 32 * 1024;
   if constexpr (Q == kQ6_K) return 12 * 1024;
   if constexpr (Q == kQ8_0) return 18 * 1024;
@@ -238,44 +265,70 @@ inline int i8_tile_target(int row_bytes) {
 // Choose slots (independent pipelines of wps warps), rows per tile and stages
 // so the block fits in shared memory: prefer the requested tile size and as
 // many warps as the register budget allows, then shrink tiles, then warps.
-template <int Q, int UPT>
-inline cudaError_t launch_i8(GemvParams p, const GemvRequest& r) {
+template <int Q, int UPT, bool F32>
+inline cudaError_t launch_b1(GemvParams p, const GemvRequest& r) {
   const int spt = 32 * UPT;
   p.wps = (p.units + spt - 1) / spt;
-  constexpr int kMaxW = i8_max_warps<Q, UPT>();
-  const int warps = env_int("FRC_NWARPS", kMaxW);
+  constexpr int kMaxW = b1_max_warps<Q, UPT, F32>();
+  const int warps = tuned(tuning().nwarps, kMaxW);
   int slots = warps / p.wps;
   if (slots < 1) slots = 1;
   if (slots * p.wps > kMaxW) slots = kMaxW / p.wps;
-  const int tile_target = env_int("FRC_TILE_BYTES", i8_tile_target<Q>(p.row_bytes));
+  if (slots < 1) return cudaErrorInvalidValue;
+  const int tile_target = tuned(tuning().tile_bytes, b1_tile_target<Q>(p.row_bytes));
   int rps = 1;
   while (rps < 8 && 2 * rps * p.row_bytes <= tile_target) rps *= 2;
-  const int forced = env_int("FRC_RPS", 0);
+  const int forced = tuning().rps;
   if (forced == 1 || forced == 2 || forced == 4 || forced == 8) rps = forced;
-  const int budget = env_int("FRC_SMEM_BYTES", kSmemBudget);
-  const int want_nst = env_int("FRC_NSTAGE", 0);
+  const int budget = tuned(tuning().smem_bytes, kSmemBudget);
+  const int want_nst = tuning().nstage;
   for (; slots >= 1; --slots) {
     for (int rr = rps; rr >= 1; rr /= 2) {
       const int stride = round_up(rr * p.row_bytes + 32, 128);
       int header = 0;
       switch (rr) {
-        case 1: header = i8_smem_header<Q, 1>(slots, 8, p.wps, p.units); break;
-        case 2: header = i8_smem_header<Q, 2>(slots, 8, p.wps, p.units); break;
-        case 4: header = i8_smem_header<Q, 4>(slots, 8, p.wps, p.units); break;
-        default: header = i8_smem_header<Q, 8>(slots, 8, p.wps, p.units); break;
+        case 1: header = b1_smem_header<Q, 1, F32>(slots, 8, p.wps, p.units); break;
+        case 2: header = b1_smem_header<Q, 2, F32>(slots, 8, p.wps, p.units); break;
+        case 4: header = b1_smem_header<Q, 4, F32>(slots, 8, p.wps, p.units); break;
+        default: header = b1_smem_header<Q, 8, F32>(slots, 8, p.wps, p.units); break;
       }
       int nst = (budget - header) / (slots * stride);
       if (nst > 8) nst = 8;
       if (want_nst > 0 && want_nst < nst) nst = want_nst;
       if (nst < 2) continue;
       switch (rr) {
-        case 1: return launch_i8_rps<Q, UPT, 1>(p, r, slots, nst);
-        case 2: return launch_i8_rps<Q, UPT, 2>(p, r, slots, nst);
-        case 4: return launch_i8_rps<Q, UPT, 4>(p, r, slots, nst);
-        default: return launch_i8_rps<Q, UPT, 8>(p, r, slots, nst);
+        case 1: return launch_b1_rps<Q, UPT, 1, F32>(p, r, slots, nst);
+        case 2: return launch_b1_rps<Q, UPT, 2, F32>(p, r, slots, nst);
+        case 4: return launch_b1_rps<Q, UPT, 4, F32>(p, r, slots, nst);
+        default: return launch_b1_rps<Q, UPT, 8, F32>(p, r, slots, nst);
       }
     }
   }
+  return cudaErrorInvalidValue;
+}
+
+// Units per thread of the batch-1 kernel: the fewest that cover a row with
+// the warps the register budget allows.  The integer kernel's choice was swept
+// on B200: K-quant rows of up to 64 units use 1 unit per thread in two-warp
+// slots, longer rows 2; Q8_0 rows of up to 128 units 1 (4096x4096: 6.5 -> 6.1
+// us); Q1_0 2 (4096x4096: 6.0 -> 5.4 us).  fp32 units hold 4x the activation
+// registers, so they take 1 unit per thread while a row fits 16 warps.
+template <int Q, bool F32>
+inline cudaError_t launch_b1_any(GemvParams p, const GemvRequest& r) {
+  const int units = p.units;
+  int upt = tuning().upt;
+  if (upt <= 0) {
+    if constexpr (F32) upt = units <= 32 * b1_max_warps<Q, 1, F32>() ? 1 : 2;
+    else if constexpr (Q == kQ8_0) upt = units <= 128 ? 1 : 2;
+    else if constexpr (Q == kQ1_0) upt = 2;
+    else upt = units <= 64 ? 1 : 2;
+  }
+  if constexpr (!F32 && I8<Q>::E == 32) {
+    if (upt == 4 && units <= 128) return launch_b1<Q, 4, F32>(p, r);
+  }
+  if (upt >= 2 && units <= 64 * b1_max_warps<Q, 2, F32>()) return launch_b1<Q, 2, F32>(p, r);
+  if (units <= 32 * b1_max_warps<Q, 1, F32>()) return launch_b1<Q, 1, F32>(p, r);
+  if (units <= 64 * b1_max_warps<Q, 2, F32>()) return launch_b1<Q, 2, F32>(p, r);
   return cudaErrorInvalidValue;
 }
 
@@ -296,7 +349,7 @@ inline cudaError_t launch_pdl(void (*kernel)(P...), unsigned grid, unsigned thre
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = env_int("FRC_PDL", 1) ? 1 : 0;
+  attr[0].val.programmaticStreamSerializationAllowed = tuned(tuning().pdl, 1) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
@@ -353,10 +406,10 @@ inline cudaError_t launch_mma_cfg(MmaParams p, const GemvRequest& r, int grid) {
   const int xbytes = 4 * NG * kMmaColBytes;
   p.stage_stride = round_up(p.x_off + xbytes, 128);
   constexpr int header = mma_header_bytes<Q, NG, MT>();
-  const int budget = env_int("FRC_SMEM_BYTES", kSmemBudget);
+  const int budget = tuned(tuning().smem_bytes, kSmemBudget);
   int nst = (budget - header) / p.stage_stride;
   if (nst > 6) nst = 6;
-  const int want = env_int("FRC_NSTAGE", 0);
+  const int want = tuning().nstage;
   if (want > 0 && want < nst) nst = want;
   if (nst < 2) return cudaErrorInvalidValue;
   p.nstage = nst;
@@ -393,12 +446,12 @@ inline cudaError_t launch_mma_ng(MmaParams p, const GemvRequest& r) {
   mma_geometry(p.row_bytes, p.chunk_bytes, &p.G, &p.W);
   // smallest row block whose boxes hold whole 8-row half tiles
   const int mt_min = p.G >= 8 ? 4 : (p.G == 4 ? 2 : 1);
-  int64_t grid = env_int("FRC_MMA_GRID", r.sms);
+  int64_t grid = tuned(tuning().mma_grid, r.sms);
   const int64_t useful = (p.n + 16 * mt_min - 1) / (16 * mt_min);
   if (grid > useful) grid = useful;
   if (grid < 1) grid = 1;
   const int64_t per_cta = (p.n + grid - 1) / grid;
-  int mt = env_int("FRC_MMA_MT", per_cta <= 16 ? 1 : (per_cta <= 32 ? 2 : 4));
+  int mt = tuned(tuning().mma_mt, per_cta <= 16 ? 1 : (per_cta <= 32 ? 2 : 4));
   if (mt < mt_min) mt = mt_min;
   if (mt == 1) return launch_mma_cfg<Q, NG, 1>(p, r, static_cast<int>(grid));
   if (mt == 2) return launch_mma_cfg<Q, NG, 2>(p, r, static_cast<int>(grid));
@@ -440,7 +493,7 @@ inline int tc_raw_k(int quant) { return quant == kQ8_0 ? 128 : 256; }
 inline int tc_split_count(int quant, int64_t n, int64_t k, int64_t seq, int sms) {
   const int64_t tiles = ((n + kTcM - 1) / kTcM) * ((seq + kTcN - 1) / kTcN);
   const int64_t nchunk = (k + tc_raw_k(quant) - 1) / tc_raw_k(quant);
-  int64_t s = env_int("FRC_TC_SPLIT", 0);
+  int64_t s = opt(options().prefill_splits);
   if (s <= 0) s = tiles >= sms ? 1 : sms / tiles;
   if (s > 16) s = 16;
   if (s > nchunk) s = nchunk;
@@ -606,41 +659,23 @@ cudaError_t launch_gemv(const GemvRequest& r) {
     p.w_flags = r.w_flags;
     p.w_epoch = r.w_epoch;
   }
-  constexpr int E = 16 * F::NRUN;
-  const bool force_xb = env_int("FRC_FORCE_XB", 0) != 0;
-  if (r.batch == 1 && !force_xb && env_int("FRC_GEMV_FP32", 0) == 0) {
-    const int units = (r.k / F::QK) * I8<Q>::UPB;
-    p.units = units;
-    // Units per thread (swept on B200, batch 1): K-quant rows of up to 64
-    // units use 1 unit per thread in two-warp slots, longer rows 2 units per
-    // thread in multi-warp slots; Q8_0 rows of up to 128 units 1 unit per
-    // thread in four-warp slots (4096x4096: 6.5 -> 6.1 us), Q1_0 2 units per
-    // thread (4096x4096: 6.0 -> 5.4 us).
-    int upt = env_int("FRC_UPT", 0);
-    if (upt == 0) {
-      if constexpr (Q == kQ8_0) upt = units <= 128 ? 1 : 2;
-      else if constexpr (Q == kQ1_0) upt = 2;
-      else upt = units <= 64 ? 1 : 2;
-    }
-    if constexpr (I8<Q>::E == 32) {
-      if (upt == 4 && units <= 128) return launch_i8<Q, 4>(p, r);
-    }
-    if (upt >= 2 && units <= 64 * i8_max_warps<Q, 2>()) return launch_i8<Q, 2>(p, r);
-    if (units <= 32 * i8_max_warps<Q, 1>()) return launch_i8<Q, 1>(p, r);
-    if (units <= 64 * i8_max_warps<Q, 2>()) return launch_i8<Q, 2>(p, r);
-    p.units = (r.k / F::QK) * F::UPB;
+  const bool exact_batched = opt(options().batched_fp32) != 0;
+  if (r.batch == 1) {
+    GemvParams b1 = p;
+    b1.units = (r.k / F::QK) * I8<Q>::UPB;
+    const cudaError_t e =
+        opt(options().batch1_int16) ? launch_b1_any<Q, false>(b1, r) : launch_b1_any<Q, true>(b1, r);
+    if (e != cudaErrorInvalidValue) return e;
+    (void)cudaGetLastError();
+    // a row longer than one CTA's threads cover: the column-reusing kernel
+    // (fp32 activations), without the fused multi-matrix or gather forms
+    if (r.nmat > 1 || r.g_world > 1 || r.w_world > 1) return cudaErrorNotSupported;
+    return launch_xb<Q, 4>(p, r);
   }
   // the fused multi-matrix launch and the fused all-gather exist only in the
-  // batch-1 integer kernel: callers fall back (per matrix / NCCL)
+  // batch-1 kernel: callers fall back (per matrix / NCCL)
   if (r.nmat > 1 || r.g_world > 1 || r.w_world > 1) return cudaErrorNotSupported;
-  if (r.batch > 1 && r.xrec && !force_xb && env_int("FRC_GEMV_FP32", 0) == 0) return launch_mma<Q>(r);
-  if (r.batch == 1 && !force_xb) {
-    const int cap1 = 32 * kMaxConsumerWarps;
-    if (p.units <= cap1) return launch_x1<Q, 1>(p, r, (p.units + 31) / 32);
-    if constexpr (E == 32) {
-      if (p.units <= 2 * cap1) return launch_x1<Q, 2>(p, r, (p.units + 63) / 64);
-    }
-  }
+  if (r.xrec && !exact_batched) return launch_mma<Q>(r);
   if (r.batch <= 4) return launch_xb<Q, 4>(p, r);
   if (r.batch <= 8) return launch_xb<Q, 8>(p, r);
   return launch_xb<Q, 16>(p, r);

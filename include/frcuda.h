@@ -82,12 +82,35 @@ int frc_weight_nbytes(int quant, int64_t n, int64_t k, size_t* nbytes);
  * bounded waits ran out); *flags == 0 means no fault was recorded. */
 int frc_device_status(int device, uint32_t* flags);
 
+/* Library options (no reference counterpart).  Process-wide, read by every
+ * later launch; the defaults are the production configuration.
+ *  FRC_OPT_BATCH1_INT16   0 (default): batch 1 keeps x in fp32 and forms every
+ *                         product in fp32, the reference's arithmetic
+ *                         (kernels/q4_k.h:153-184); 1: x is quantised per
+ *                         64-element unit to a 16-bit integer grid and the
+ *                         products run on dp4a (~3e-5 relative error).
+ *  FRC_OPT_BATCHED_FP32   0 (default): batch 2..16 on the int8 tensor-core
+ *                         kernel; 1: on the fp32 CUDA-core kernel.
+ *  FRC_OPT_PREFILL_TC     1 (default): batches above 16 on the tcgen05 GEMM;
+ *                         0: in chunks of at most 16 columns.
+ *  FRC_OPT_PREFILL_SPLITS 0 (default): k-splits of the prefill GEMM chosen from
+ *                         the shape; n > 0: n splits (clamped to 1..16).
+ *  FRC_OPT_INJECT_OOM     1: frc_weight_create fails with FRC_ERR_NOMEM before
+ *                         any CUDA call (a test of the error path); default 0. */
+#define FRC_OPT_BATCH1_INT16   1
+#define FRC_OPT_BATCHED_FP32   2
+#define FRC_OPT_PREFILL_TC     3
+#define FRC_OPT_PREFILL_SPLITS 4
+#define FRC_OPT_INJECT_OOM     5
+int frc_set_option(int option, int value);
+int frc_get_option(int option, int* value);
+
 /* ---- stream-ordered device-pointer kernels ------------------------------ *
  * No synchronisation: the work is enqueued on `stream` (a cudaStream_t;
  * NULL = legacy default stream) of the current device.  w_dev must be
  * 16-byte aligned.  frc_gemv computes y_dev (batch, n) from x_dev (batch, k),
- * batch >= 1: batch 1 on the dp4a kernel, 2..16 on the int8 tensor-core
- * kernel, more (prefill) on the tcgen05 GEMM with fp16 operands and fp32
+ * batch >= 1: batch 1 on the fp32-activation kernel (FRC_OPT_BATCH1_INT16
+ * selects the dp4a one), 2..16 on the int8 tensor-core kernel, more (prefill) on the tcgen05 GEMM with fp16 operands and fp32
  * accumulation (where the row length allows its tensor view; otherwise in
  * chunks of at most 16 columns).  For batch >= 2 x is first staged (as
  * 16-bit integer records, or as fp16) in a per-device buffer the library
@@ -114,11 +137,15 @@ int frc_gemv(int quant, const void* w_dev, size_t w_bytes, int64_t n, int64_t k,
  * rewrites the records it reads.  All calls on one device share the region,
  * so two calls that can overlap in time (streams without ordering between
  * them) race and give wrong results.  A bounded wait that runs out sets a bit
- * in a status word of this entry point that frc_device_status does not read;
- * y is then incomplete. */
+ * in this entry point's own status word (also static device memory) and y is
+ * then incomplete: frc_noalloc_status reads and clears that word. */
 #define FRC_NOALLOC_SCRATCH_BYTES 2097152
 int frc_gemv_noalloc(int quant, const void* w_dev, size_t w_bytes, int64_t n, int64_t k,
                      const float* x_dev, int64_t batch, float* y_dev, void* stream);
+/* Reads and clears the status word of frc_gemv_noalloc on `device`, after
+ * waiting for the device's queued work; *flags == 0 means every call so far
+ * completed.  Allocates nothing.  (No reference counterpart.) */
+int frc_noalloc_status(int device, uint32_t* flags);
 /* One launch for up to 4 weights of the same quant and k that share x
  * (q/k/v, or gate/up, of a layer): y_dev[m] (batch, n[m]) = x . W_m^T.  At
  * batch 1 the rows of all matrices form one row space of a single kernel

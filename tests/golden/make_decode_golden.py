@@ -32,7 +32,7 @@ PROMPT_LEN, STEPS, PROMPT_SEED = 8, 12, 11
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("FLATRUN_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("FLATRUN_REFERENCE") or os.path.join(os.path.dirname(REPO), "reference"))
     a = ap.parse_args()
     sys.path.insert(0, os.path.join(a.ref, "src"))
     from flatrun.core.tensor import BufferTensorHandle

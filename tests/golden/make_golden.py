@@ -57,7 +57,7 @@ def _load_native(path: str):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("FLATRUN_REFERENCE") or os.path.join(os.path.dirname(REPO), "reference"))
     args = ap.parse_args()
     sys.path.insert(0, os.path.join(args.ref, "src"))
     from flatrun.dequant import gguf

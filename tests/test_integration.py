@@ -14,7 +14,9 @@ import sys
 import numpy as np
 import pytest
 
-REF = os.environ.get("FLATRUN_REFERENCE", "/root/reference")
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+# the reference checkout: FLATRUN_REFERENCE, else "reference" beside this repository
+REF = os.environ.get("FLATRUN_REFERENCE") or os.path.join(os.path.dirname(REPO), "reference")
 REF_SRC = os.path.join(REF, "src")
 
 
