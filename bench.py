@@ -1,35 +1,40 @@
 """Benchmark of the fused GGUF dequant + matvec path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload layer_q4k|q8_0|head_q6k|down_q5k|...]
+                    [--workload layer_llama70b|layer_q4k|q8_0|head_q6k|...]
 
-Default workload (the configuration the headline metric is quoted on): one
-Qwen2-7B layer's projections at batch 1 in Q4_K -- q/o 3584x3584, k/v
-512x3584, gate/up 18944x3584, down 3584x18944 (131,088,384 weight bytes).  A
-step is one pass over the seven matvecs.  Eight distinct copies of the layer
-(1.05 GB, well above the 126 MB L2) are rotated step by step, so every step
-streams its weights from HBM.
+Default workload, at every N (config 5): one Llama-3-70B layer's projections
+at batch 1 in Q4_K -- q/o 8192x8192, k/v 1024x8192, gate/up 28672x8192,
+down 8192x28672 (481.8 MB of weights).  A step is one pass over the seven
+matvecs in the forwarder's dataflow: q/k/v and gate/up each run as one fused
+launch over matrices sharing x, so four launches.  Under torchrun (--gpus N)
+every projection's rows are split over the N ranks (whole quant blocks per
+row) and each launch assembles its outputs on every rank with the all-gather
+fused into the GEMV (peer stores over NVLink): strong scaling, value = bytes
+of the whole layer / max-over-ranks step time.  Per matrix, distinct device
+copies totalling >= 3x L2 are rotated step by step, so every launch streams
+its weights from HBM.  Other workloads: config 2 (`layer_q4k`, one Qwen2-7B
+layer, weak scaling under N ranks), config 1 (`q8_0`), config 3 (`head_q6k*`,
+`down_q5k*`, `prefill_gate_q4k`), config 4's projections (`decode_qwen2_7b`).
 
 value  = algorithmic bytes (weights + x + y) per step / device time per step,
-         weights and activations resident in HBM; the K steps are one CUDA
-         graph replay timed with CUDA events on the launching stream.
+         weights and activations resident in HBM; the K steps are CUDA graph
+         replays timed with CUDA events on the launching stream.
 e2e    = the same metric through the public call a user makes,
          CudaBackend.matmul_q4k(x, weight, n, k) with x in pinned host memory:
-         x host->device, kernel, y device->host and a synchronise per call.
-roofline: achieved GB/s of the dominant kernel (the gemv_x1 launches of the
-         3584-column projections: 6 of 7 launches, 71% of the bytes) from
-         per-launch CUDA events inside the timed graph, against the measured
-         copy bandwidth in MEASURED_PEAKS.json.
-cpu_baseline: the reference's own native kernels (flatrun_native._C, built
-         from its sources into oracle/_ref) on the same layer.
-
-Multi-GPU (--gpus N under torchrun): each rank owns an n-row shard (the
-config's shapes) of every projection of an N-times taller layer, whole quant
-blocks per row, and the outputs are assembled by all-gathers in the
-forwarder's dependency groups (qkv, o, gate+up, down).  Per-GPU work is fixed
-("weak" scaling); value = bytes of all ranks / max-over-ranks time.  The
-`layer_llama70b` workload (config 5) instead splits one whole Llama-3-70B
-layer's rows over the ranks ("strong" scaling).
+         x host->device, kernel, y device->host and a synchronise per call
+         (N = 1).
+roofline: achieved GB/s of the dominant launch (the one carrying the most
+         bytes: gate+up for the layer workloads) from K back-to-back launches
+         timed with CUDA events, against the measured copy bandwidth in
+         MEASURED_PEAKS.json.
+cpu_baseline / cpu_baseline_numpy: the reference's native C++ kernels
+         (flatrun_native._C built from its sources into oracle/_ref, one core)
+         and its NumPy + BLAS path (restated in oracle/), each on a bounded
+         row sample of the same workload (N = 1, rank 0).
+assembly_share / gather_check (N > 1): the share of the step the output
+         assembly adds to the GEMVs alone, and an in-run bit-exact check of
+         the assembled outputs on every rank.
 """
 
 from __future__ import annotations
@@ -124,6 +129,11 @@ WORKLOADS = {
     "decode_qwen2_7b": dict(mats=qwen2_7b_decode_token(), batch=1,
                             desc="config 4 projections: one Qwen2-7B decode token (28 layers, Q4_K_M mix, Q6_K "
                                  "lm_head), batch 1"),
+    "decode_qwen2_7b_device": dict(mats=qwen2_7b_decode_token(), batch=1, device_decode=True,
+                                   desc="config 4: one Qwen2-7B decode token entirely on the GPU (28 layers, Q4_K_M "
+                                        "mix, Q6_K lm_head, KV cache pre-filled with 4096 positions; embedding, "
+                                        "norms, RoPE, attention, SwiGLU, head and argmax on the device, one CUDA "
+                                        "graph per token), greedy, batch 1"),
     "prefill_gate_q4k": dict(mats=[("gate", "Q4_K", 18944, 3584, "w")], batch=512,
                              desc="config 3: batched prefill, 512 tokens x 3584 through gate 18944x3584 Q4_K"),
 }
@@ -243,15 +253,33 @@ def _load_ref_native():
 _REF_FN = {"Q4_K": "matmul_q4_k", "Q6_K": "matmul_q6_k", "Q8_0": "matmul_q8_0"}
 
 
-def cpu_reference_step_fn(mats, batch, host_w, xs):
-    """One step of the reference's CPU path: the native C++ kernels where the
-    reference has one (scalar, single-threaded on x86: q4_k.h:38-41), else its
-    NumPy decoders + BLAS (restated in oracle/)."""
-    nat = _load_ref_native()
+def sample_rows(mats, host_w, frac: float):
+    """The first ceil(frac * n) rows of every projection (whole rows, hence
+    whole quant blocks): a bounded sample of the workload for the CPU legs."""
+    out_m, out_w = [], []
+    for (name, q, n, k, g), w in zip(mats, host_w):
+        ns = max(1, min(n, int(np.ceil(frac * n))))
+        out_m.append((name, q, ns, k, g))
+        out_w.append(w[: ns * synth.row_bytes(q, k)])
+    return out_m, out_w
+
+
+def cpu_step_fn(mats, batch, host_w, xs, path: str):
+    """One pass of a reference CPU path over the projections.
+
+    path "native": the reference's own C++ kernels (flatrun_native._C, built
+    from its sources into oracle/_ref; scalar and single-threaded on x86,
+    kernels/q4_k.h:38-41, _C.cpp:190-194), and for the formats it has no
+    kernel for (Q5_K, Q1_0) its NumPy decoders + BLAS, restated in oracle/.
+    path "numpy": the reference's NumPy path for every format
+    (PythonBackend.matmul_*, runtime/backend.py:164-213: dequantise to fp32,
+    then a BLAS product), restated in oracle/.
+    Returns (step, kind): kind "reference" when every call ran the
+    reference's own compiled code, else "port"."""
     from oracle import gguf_oracle as O
 
-    calls = []
-    kinds = set()
+    nat = _load_ref_native() if path == "native" else None
+    calls, kinds = [], set()
     for (name, q, n, k, _), w, x in zip(mats, host_w, xs):
         if nat is not None and q in _REF_FN:
             fn = getattr(nat, _REF_FN[q] + ("_batched" if batch > 1 else ""))
@@ -263,29 +291,208 @@ def cpu_reference_step_fn(mats, batch, host_w, xs):
     return (lambda: [c() for c in calls]), ("reference" if kinds == {"reference"} else "port")
 
 
-def run_cpu(mats, batch, steps, warmup, host_w, xs):
-    """Median seconds of one reference step at `batch`; above
-    CPU_SAMPLE_TOKENS tokens the step runs on the first CPU_SAMPLE_TOKENS rows
-    of x and is scaled by batch / CPU_SAMPLE_TOKENS."""
-    scale = 1.0
+def blas_threads() -> int:
+    """Threads the BLAS library under NumPy runs with."""
+    try:
+        from threadpoolctl import threadpool_info
+        n = [int(i.get("num_threads") or 0) for i in threadpool_info() if i.get("user_api") == "blas"]
+        if n:
+            return max(n)
+    except Exception:  # pragma: no cover - threadpoolctl absent
+        pass
+    return os.cpu_count() or 1
+
+
+def cpu_leg(mats, batch, host_w, xs, path: str, steps: int, warmup: int, budget_s: float):
+    """Time a reference CPU path on a bounded sample of the workload.
+
+    Above CPU_SAMPLE_TOKENS tokens the passes use the first CPU_SAMPLE_TOKENS
+    rows of x (the reference's batched kernels re-read the weight per token,
+    so time scales linearly).  A 1 % row sample is timed once to size the
+    sample: the largest row fraction whose warmup + steps passes fit in
+    budget_s.  Returns (seconds per full-workload pass, as the median of
+    `steps` sampled passes scaled by bytes and tokens; kind; description)."""
+    tok_scale = 1.0
     if batch > CPU_SAMPLE_TOKENS:
         xs = [np.ascontiguousarray(x[:CPU_SAMPLE_TOKENS]) for x in xs]
-        scale = batch / CPU_SAMPLE_TOKENS
+        tok_scale = batch / CPU_SAMPLE_TOKENS
         batch = CPU_SAMPLE_TOKENS
-    step, kind = cpu_reference_step_fn(mats, batch, host_w, xs)
+    full_w = sum(synth.weight_bytes(q, n, k) for _, q, n, k, _ in mats)
+    pm, pw = sample_rows(mats, host_w, 0.01)
+    probe, _ = cpu_step_fn(pm, batch, pw, xs, path)
+    t0 = time.perf_counter()
+    probe()
+    t_probe = max(time.perf_counter() - t0, 1e-6)
+    probe_w = sum(synth.weight_bytes(q, n, k) for _, q, n, k, _ in pm)
+    per_byte = t_probe / probe_w
+    frac = min(1.0, budget_s / max(1, steps + warmup) / (per_byte * full_w))
+    sm, sw = sample_rows(mats, host_w, frac)
+    step, kind = cpu_step_fn(sm, batch, sw, xs, path)
     for _ in range(warmup):
         step()
     times = []
     for _ in range(steps):
         t0 = time.perf_counter()
         step()
-        times.append((time.perf_counter() - t0) * scale)
-    return statistics.median(times), sum(times), kind
+        times.append(time.perf_counter() - t0)
+    sample_w = sum(synth.weight_bytes(q, n, k) for _, q, n, k, _ in sm)
+    t_full = statistics.median(times) * (full_w / sample_w) * tok_scale
+    desc = (f"{steps} timed passes (median) after {warmup} warm-up over the first "
+            f"{100.0 * sample_w / full_w:.3g} % of every projection's rows ({sample_w / 1e6:.1f} MB of weights), "
+            f"scaled to the full workload by bytes")
+    if tok_scale != 1.0:
+        desc += f"; {CPU_SAMPLE_TOKENS} of the {int(batch * tok_scale)} tokens per pass, time scaled by {tok_scale:g}"
+    return t_full, kind, desc
+
+
+def cpu_baselines(mats, batch, host_w, xs, step_bytes: int, budget_s: float = 12.0) -> tuple[dict, dict]:
+    """The reference's two CPU paths on the host cores: native C++ (1 core)
+    and NumPy + BLAS (the BLAS library's threads), each on a bounded sample."""
+    t_nat, kind, desc = cpu_leg(mats, batch, host_w, xs, "native", 3, 1, budget_s)
+    native = {"value": round(step_bytes / t_nat / 1e9, 4), "unit": UNIT, "cores": 1, "kind": kind,
+              "sample": desc + "; reference flatrun_native._C built from its sources (scalar, single-threaded "
+                               "on x86: the x86 build has no threaded path)"}
+    t_np, kind_np, desc_np = cpu_leg(mats, batch, host_w, xs, "numpy", 3, 1, budget_s)
+    numpy_leg = {"value": round(step_bytes / t_np / 1e9, 4), "unit": UNIT, "cores": blas_threads(),
+                 "kind": kind_np,
+                 "sample": desc_np + "; the reference NumPy path (dequantise to fp32, then BLAS) restated in "
+                                     "oracle/: NumPy decoding on one core, the BLAS product on the cores stated"}
+    return native, numpy_leg
+
+
+def config_of(wl: dict, mats, batch: int, world: int, scaling: str) -> dict:
+    """The workload description both arms print (same keys and values)."""
+    total = mats if scaling == "strong" or world == 1 else mats * world
+    return {"workload": wl["desc"], "global_batch": (batch if batch <= 16 else 1),
+            "seq_len": 1 if batch <= 16 else batch,
+            "parallelism": f"row-shard x{world}" if world > 1 else "single GPU",
+            "weight_bytes_per_step": sum(synth.weight_bytes(q, n, k) for _, q, n, k, _ in total),
+            "algorithmic_bytes_per_step": algorithmic_bytes(mats, batch) * (world if scaling == "weak" else 1)}
 
 
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+
+def run_device_decode(args, wl: dict, config: dict, step_bytes: int) -> None:
+    """The decode_qwen2_7b_device workload: K greedy tokens through
+    flatrun_b200.decode.DecodeEngine (one CUDA graph replay per token) on a
+    random-init Qwen2-7B in the Q4_K_M mix (centred Q4_K blocks, synthetic
+    Q6_K blocks, fp32 embedding, norms 0.1, q/k/v biases) with a KV cache
+    pre-filled with 4096 positions."""
+    import ctypes
+
+    import torch
+
+    from flatrun_b200 import _lib
+    from flatrun_b200.decode import DecodeEngine, DecoderConfig
+
+    torch.cuda.set_device(0)
+    H, F, V, L, NH, NKV, HD, PRE = 3584, 18944, 152064, 28, 28, 4, 128, 4096
+    rng = np.random.default_rng(0)
+    quant, w = {}, {}
+    for i in range(L):
+        p = f"model.layers.{i}"
+        hi = "Q6_K" if i % 2 == 0 else "Q4_K"
+        for j, (nm, n, k, q) in enumerate((("self_attn.q_proj", H, H, "Q4_K"), ("self_attn.k_proj", NKV * HD, H, "Q4_K"),
+                                            ("self_attn.v_proj", NKV * HD, H, hi), ("self_attn.o_proj", H, H, "Q4_K"),
+                                            ("mlp.gate_proj", F, H, "Q4_K"), ("mlp.up_proj", F, H, "Q4_K"),
+                                            ("mlp.down_proj", H, F, hi))):
+            name = f"{p}.{nm}.weight"
+            quant[name] = (n, k, q)
+            w[name] = synth.make_centered_q4_k(n, k, seed=100 * i + j) if q == "Q4_K" else \
+                synth.make_weight(q, n, k, seed=100 * i + j)
+        for nm in ("input_layernorm", "post_attention_layernorm"):
+            w[f"{p}.{nm}.weight"] = np.full(H, 0.1, np.float32)
+        for nm, n in (("q_proj", H), ("k_proj", NKV * HD), ("v_proj", NKV * HD)):
+            w[f"{p}.self_attn.{nm}.bias"] = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    quant["lm_head.weight"] = (V, H, "Q6_K")
+    w["lm_head.weight"] = synth.make_weight("Q6_K", V, H, seed=9999)
+    w["model.norm.weight"] = np.full(H, 0.1, np.float32)
+    w["model.embed_tokens.weight"] = rng.standard_normal((V, H), dtype=np.float32)
+    kv = {i: (rng.standard_normal((PRE, NKV, HD), dtype=np.float32),
+              rng.standard_normal((PRE, NKV, HD), dtype=np.float32)) for i in range(L)}
+    K, W = args.steps, args.warmup
+    e2e_steps = 0 if args.no_e2e else min(K, 200)
+    cfg = DecoderConfig(hidden=H, ffn=F, vocab=V, layers=L, heads=NH, kv_heads=NKV, eps=1e-6, rope_theta=1e6,
+                        max_pos=PRE + W + K + e2e_steps + 64)
+    eng = DecodeEngine(cfg, w, quant.get, kv_prefill=kv)
+    del w, kv
+    eng.capture()
+    st = eng.stream
+    clocks = ClockSampler(0)
+    eng.step(int(rng.integers(0, V)))
+    for _ in range(W - 1):
+        eng.step(None)
+    st.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(st)
+    for _ in range(K):
+        eng.step(None)
+    end.record(st)
+    end.synchronize()
+    clk = clocks.stop()
+    ms_tok = start.elapsed_time(end) / K
+    wbytes = config["weight_bytes_per_step"]
+    value = step_bytes / (ms_tok / 1e3) / 1e9
+    # the dominant launch: the lm_head GEMV (447 MB), timed alone K times
+    lm = eng._w["lm_head.weight"]
+    lib = eng.lib
+    y = torch.empty(V, device="cuda")
+    args_ = (lm[1], 1, (ctypes.c_void_p * 1)(lm[0].data_ptr()), (ctypes.c_size_t * 1)(lm[0].numel()),
+             (ctypes.c_int64 * 1)(V), H, eng.x.data_ptr(), None, 0, (ctypes.c_void_p * 1)(y.data_ptr()),
+             ctypes.c_void_p(st.cuda_stream))
+    for _ in range(3):
+        _lib.check(lib.frc_gemv_ex(*args_), lib)
+    nl = min(K, 200)
+    start.record(st)
+    for _ in range(nl):
+        _lib.check(lib.frc_gemv_ex(*args_), lib)
+    end.record(st)
+    end.synchronize()
+    us = start.elapsed_time(end) * 1e3 / nl
+    lm_bytes = synth.weight_bytes("Q6_K", V, H) + 4 * (H + V)
+    peak, peak_src = peaks()
+    achieved = lm_bytes / (us / 1e6) / 1e9
+    # e2e through the engine's public calls: each token's greedy pick read
+    # back to the host (a 4-byte copy and a synchronise per token)
+    e2e = None
+    if e2e_steps:
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            eng.step(None)
+            eng.argmax_host()
+        t_tok = (time.perf_counter() - t0) / e2e_steps
+        e2e = {"value": round(step_bytes / t_tok / 1e9, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
+               "d2h_bytes_per_step": 4, "ms_per_step": round(t_tok * 1e3, 4), "tokens_per_s": round(1.0 / t_tok, 2),
+               "timer": "host wall clock; each token: one graph replay, the argmax read back, a synchronise"}
+    cpu = cpu_np = None
+    if not args.no_cpu:
+        mats = wl["mats"]
+        host_w = make_host_layer(mats, 0)
+        xs = [synth.make_x(k, seed=50 + i) for i, (_, _, _, k, _) in enumerate(mats)]
+        cpu, cpu_np = cpu_baselines(mats, 1, host_w, xs, step_bytes)
+        for leg in (cpu, cpu_np):
+            leg["sample"] += "; the token's projections only (the reference's attention and norms not timed)"
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1, "steps": K, "warmup": W,
+        "ms_per_step": round(ms_tok, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic", "config": config,
+        "tokens_per_s": round(1e3 / ms_tok, 2),
+        "measurement": {"timer": "K graph replays (one token each) bracketed by CUDA events on the engine stream",
+                        "weight_bytes_per_token": wbytes, "launches_per_token": eng.launches_per_token,
+                        "l2": "inputs larger than L2: 4.37 GB of weights streamed per token"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": ncu_traffic("head_q6k"), "peak_source": peak_src,
+                     "kernel": f"gemv_b1 (fp32 activations) <Q6_K> lm_head ({lm_bytes / 1e6:.1f} MB per launch)",
+                     "timing": f"{nl} back-to-back launches bracketed by CUDA events on the engine stream"},
+        "whole_token_frac": round(value / peak, 4),
+        "cpu_baseline": cpu, "cpu_baseline_numpy": cpu_np, "e2e": e2e, "clocks": clk,
+        "gpu_launches": K * eng.launches_per_token,
+    }
+    print(json.dumps(out), flush=True)
+    eng.close()
+
 
 def make_host_layer(mats, copy: int):
     return [synth.make_weight(q, n, k, seed=1000 * copy + i) for i, (_, q, n, k, _) in enumerate(mats)]
@@ -297,7 +504,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="layer_q4k")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="layer_llama70b")
     ap.add_argument("--copies", type=int, default=0, help="distinct weight copies rotated (0 = auto, > 3x L2)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -318,31 +525,37 @@ def main() -> None:
     mats, batch = wl["mats"], wl["batch"]
     step_bytes = algorithmic_bytes(mats, batch, fused=not getattr(args, "unfused", False))
 
+    scaling = "strong" if wl.get("strong") else "weak"
+    config = config_of(wl, mats, batch, world, scaling)
+
     if args.impl == "reference":
         if rank != 0:
             return
         host_w = make_host_layer(mats, 0)
         xs = [synth.make_x(k, batch=None if batch == 1 else batch, seed=50 + i)
               for i, (_, _, _, k, _) in enumerate(mats)]
-        # bounded: at most 20 timed and 3 warm-up steps of the host kernels
-        steps = max(1, min(args.steps, 20))
-        warm = min(args.warmup, 3)
-        med, total, kind = run_cpu(mats, batch, steps, warm, host_w, xs)
-        value = step_bytes / med / 1e9
+        # every one of the K timed and W warm-up steps runs; each step is a
+        # row sample of the workload sized so that all of them take ~2 minutes
+        t_full, kind, desc = cpu_leg(mats, batch, host_w, xs, "native", args.steps, args.warmup, budget_s=120.0)
+        full_bytes = config["algorithmic_bytes_per_step"]
+        value = full_bytes / t_full / 1e9
         print(json.dumps({
-            "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
-            "steps": steps, "warmup": warm, "ms_per_step": round(med * 1e3, 3),
-            "higher_is_better": True, "scaling": "strong" if wl.get("strong") else "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic",
-            "config": {"workload": wl["desc"], "global_batch": batch},
+            "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_full * 1e3, 3),
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "config": config,
             "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": 1, "kind": kind,
-                             "sample": f"{steps} timed steps of the full workload (median), reference "
-                                       "flatrun_native._C scalar kernels (single-threaded on x86)"
-                                       + (f"; {CPU_SAMPLE_TOKENS} of the {batch} tokens per step, time scaled "
-                                          f"by {batch / CPU_SAMPLE_TOKENS:g}" if batch > CPU_SAMPLE_TOKENS else "")},
+                             "sample": desc + "; reference flatrun_native._C built from its sources (scalar, "
+                                              "single-threaded on x86: the x86 build has no threaded path)"},
             "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "tokens_per_s": round(1.0 / med, 4) if args.workload.startswith("decode") else None,
+            "tokens_per_s": round(1.0 / t_full, 4) if args.workload.startswith("decode") else None,
         }), flush=True)
+        return
+
+    if wl.get("device_decode"):
+        if world > 1:
+            raise SystemExit("the device decode workload runs on one GPU")
+        run_device_decode(args, wl, config, step_bytes)
         return
 
     import ctypes
@@ -356,7 +569,6 @@ def main() -> None:
     if wl.get("strong") and world > 1:
         mats = shard_rows(mats, world)
         step_bytes = algorithmic_bytes(mats, batch, fused=not getattr(args, "unfused", False))
-    scaling = "strong" if wl.get("strong") else "weak"
 
     if world > 1:
         import datetime
@@ -398,11 +610,15 @@ def main() -> None:
     # copies (>= 3x L2 of bytes) that no launch finds its weight in L2, even
     # when one projection is timed alone
     pools = []  # (buffer, stride, ncopies)
+    sig_bytes = {}  # weight bytes of all matrices of one shape (timed together per launch)
+    for _, q, n, k, _ in mats:
+        sig_bytes[(q, n, k)] = sig_bytes.get((q, n, k), 0) + synth.weight_bytes(q, n, k)
     for (name, q, n, k, _), raw in zip(mats, base):
         nb = max(int(raw.nbytes), 1)
         stride = (nb + 255) // 256 * 256
-        # a step that streams >= 3x L2 of weights re-reads nothing from L2
-        nc = 1 if wbytes >= 3 * l2 else int(min(1024, max(2, np.ceil(3 * l2 / nb))))
+        # the launches of one shape, timed back to back, stream >= 3x L2 of
+        # distinct weights: they re-read nothing from L2 (nor does a step)
+        nc = 1 if sig_bytes[(q, n, k)] >= 3 * l2 else int(min(1024, max(2, np.ceil(3 * l2 / nb))))
         buf = torch.empty(nc * stride, dtype=torch.uint8, device="cuda")
         src = torch.from_numpy(raw).cuda()
         for j in range(nc):
@@ -579,6 +795,7 @@ def main() -> None:
     for g in lgroups:
         sigs.setdefault(tuple((mats[i][1], mats[i][2], mats[i][3]) for i in g), []).append(g)
     per = {}
+    launch_us = {}  # per launch group: its plain GEMV time (no assembly)
     for gs in sigs.values():
         g = gs[0]
         name = "+".join(mats[i][0] for i in g) + (f" (x{len(gs)})" if len(gs) > 1 else "")
@@ -594,7 +811,43 @@ def main() -> None:
         us = replay_ms(gi) * 1e3 / K
         b = sum(mbytes[i] + batch * (mats[i][3] + mats[i][2]) * 4 for i in g) - (len(g) - 1) * batch * mats[g[0]][3] * 4
         per[name] = {"us": round(us, 3), "gbs": round(b / (us / 1e6) / 1e9, 1), "bytes": b}
+        for g_ in gs:
+            launch_us[tuple(g_)] = us
         del gi
+    gemv_us_step = sum(launch_us[tuple(g)] for g in lgroups)
+    if world > 1:
+        t = torch.tensor([gemv_us_step], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        gemv_us_step = float(t.item())
+    # the share of the step that the output assembly (stores to peers, the
+    # flag publication and waits, the skew between ranks) adds to the GEMVs
+    assembly_share = max(0.0, 1.0 - gemv_us_step / (ms_step * 1e3)) if world > 1 else None
+
+    # in-run correctness of the assembly (N > 1, every rank): one more step
+    # run eagerly; each fused group's gathered buffer must equal, bit for bit,
+    # the NCCL all-gather of the ranks' own outputs, and each rank's own
+    # outputs must equal a plain per-matrix GEMV of its rows
+    gather_check = None
+    if world > 1 and fused:
+        with torch.cuda.stream(stream):
+            launch(K)
+            for fg, _ in fused.values():
+                fg.wait(stream.cuda_stream)
+        stream.synchronize()
+        ok = True
+        for idx, (fg, sendbuf) in fused.items():
+            ref = torch.empty(world * sendbuf.numel(), device="cuda")
+            dist.all_gather_into_tensor(ref, sendbuf)
+            ok = ok and torch.equal(fg.gathered(), ref)
+            local = sendbuf.clone()
+            with torch.cuda.stream(stream):
+                for i in idx:
+                    gemv(i, K)
+            stream.synchronize()
+            ok = ok and torch.equal(local, sendbuf)
+        t = torch.tensor([0 if ok else 1], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        gather_check = "bit-exact on every rank" if int(t.item()) == 0 else "MISMATCH"
     # dominant kernel: the launch carrying the most bytes
     dom_name = max(per, key=lambda nm: per[nm]["bytes"])
     achieved = per[dom_name]["bytes"] / (per[dom_name]["us"] / 1e6) / 1e9
@@ -628,15 +881,11 @@ def main() -> None:
                "tokens_per_s": round(1.0 / t_e2e, 2) if args.workload.startswith("decode") else None,
                "timer": "host wall clock over synchronous calls (each call copies x in, y out and synchronises)"}
 
-    # CPU baseline: the reference's own native kernels on the same workload
-    cpu = None
-    if not args.no_cpu and rank == 0:
-        med, total, kind = run_cpu(mats, batch, 3, 1, base, xs_host)
-        cpu = {"value": round(step_bytes / med / 1e9, 4), "unit": UNIT, "cores": 1, "kind": kind,
-               "sample": "3 timed passes over the full workload (median) after 1 warm-up, reference "
-                         "flatrun_native._C built from its sources (scalar, single-threaded on x86)"
-                         + (f"; {CPU_SAMPLE_TOKENS} of the {batch} tokens per pass, time scaled by "
-                            f"{batch / CPU_SAMPLE_TOKENS:g}" if batch > CPU_SAMPLE_TOKENS else "")}
+    # CPU baselines (rank 0 at N = 1 only): the reference's native C++ path
+    # and its NumPy path, each on a bounded sample of the same workload
+    cpu = cpu_np = None
+    if not args.no_cpu and world == 1:
+        cpu, cpu_np = cpu_baselines(mats, batch, base, xs_host, step_bytes)
 
     if rank == 0:
         # the kernel family each call runs: batch 1 dp4a GEMV, 2..16 int8
@@ -667,23 +916,26 @@ def main() -> None:
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": dtype, "data": "synthetic",
-            "config": {"workload": wl["desc"], "global_batch": (batch if batch <= 16 else 1) * world,
-                       "seq_len": 1 if batch <= 16 else batch,
-                       "parallelism": f"row-shard x{world}" if world > 1 else "single GPU",
-                       "gather": ("fused into the GEMV: stores to every rank over NVLink; the next GEMV waits for "
-                                  "every rank's flag before reading x" if fused else "NCCL all_gather_into_tensor")
-                                 if world > 1 else None,
-                       "weight_bytes_per_step": wbytes, "algorithmic_bytes_per_step": step_bytes,
-                       "weight_copies_rotated": [p[2] for p in pools],
-                       "l2": f"inputs larger than L2: each projection rotates over distinct device copies "
-                             f"totalling >= 3x L2 ({sum(p[2] * mbytes[i] for i, p in enumerate(pools)) / 1e9:.2f} GB);"
-                             f" L2 {l2 / 2**20:.0f} MiB"},
+            "config": config,
+            "measurement": {
+                "gather": ("fused into the GEMV: stores to every rank over NVLink; the next GEMV waits for every "
+                           "rank's flag before reading x" if fused else "NCCL all_gather_into_tensor")
+                          if world > 1 else None,
+                "rank_bytes_per_step": step_bytes,
+                "weight_copies_rotated": [p[2] for p in pools],
+                "l2": f"inputs larger than L2: each projection rotates over distinct device copies totalling "
+                      f">= 3x L2 ({sum(p[2] * mbytes[i] for i, p in enumerate(pools)) / 1e9:.2f} GB); "
+                      f"L2 {l2 / 2**20:.0f} MiB"},
             "frac_of_8tbs": round(value / world / 8000.0, 4),
             "tokens_per_s": round(1e3 / ms_step, 2) if args.workload.startswith("decode") else None,
             "roofline": roof,
             "per_launch": per,
             "launches_per_step": len(lgroups),
+            "assembly_share": round(assembly_share, 4) if assembly_share is not None else None,
+            "gemv_us_per_step": round(gemv_us_step, 3),
+            "gather_check": gather_check,
             "cpu_baseline": cpu,
+            "cpu_baseline_numpy": cpu_np,
             "e2e": e2e,
             "clocks": clk,
             "gpu_launches": K * sum(calls_per_group(g) for g in lgroups),

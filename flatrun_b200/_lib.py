@@ -22,6 +22,8 @@ FRC_ERR_UNSUPPORTED = 5
 QUANT_IDS = {"Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "Q1_0": 41}
 QUANT_NAMES = {v: k for k, v in QUANT_IDS.items()}
 
+FRC_GEMV_ACCUMULATE = 1  # frc_gemv_ex flag
+
 # frc_set_option ids (include/frcuda.h FRC_OPT_*)
 OPTIONS = {"batch1_int16": 1, "batched_fp32": 2, "prefill_tc": 3, "prefill_splits": 4, "inject_oom": 5}
 
@@ -45,6 +47,15 @@ SIGNATURES: dict[str, list] = {
     "frc_set_option": [_i, _i],
     "frc_get_option": [_i, ctypes.POINTER(_i)],
     "frc_noalloc_status": [_i, ctypes.POINTER(ctypes.c_uint32)],
+    "frc_gemv_ex": [_i, _i, ctypes.POINTER(_p), ctypes.POINTER(_sz), ctypes.POINTER(_i64), _i64, _p, _p, _i,
+                    ctypes.POINTER(_p), _p],
+    "frc_rmsnorm": [_p, _p, _i64, _i64, ctypes.c_float, _p, _p],
+    "frc_rope_append": [_p, _p, _i, _i, _i, _p, _p, _p, _p, _p, _p],
+    "frc_attention_workspace": [_i, _i, _i, ctypes.POINTER(_sz)],
+    "frc_attention_decode": [_p, _p, _p, _p, _i, _i, _i, ctypes.c_float, _i, _p, _p, _p],
+    "frc_argmax": [_p, _i64, _p, _p],
+    "frc_embed_row": [_i, _p, _i64, _p, _p, _p],
+    "frc_pos_advance": [_p, _p],
     "frc_gemv": [_i, _p, _sz, _i64, _i64, _p, _i64, _p, _p],
     "frc_gemv_noalloc": [_i, _p, _sz, _i64, _i64, _p, _i64, _p, _p],
     "frc_ipc_alloc": [_sz, ctypes.POINTER(_p), _p],

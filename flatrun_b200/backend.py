@@ -113,6 +113,7 @@ class CudaBackend:
             self._ndev = 0
             self._load_error = exc
         self._cache: dict[tuple, tuple[DeviceWeight, np.ndarray]] = {}
+        self._by_id: dict[int, tuple] = {}
         self._mu = threading.Lock()
 
     # --- BackendBase properties (backend.py:62-81) ---------------------------
@@ -138,30 +139,38 @@ class CudaBackend:
 
     def weight(self, weight: Any, n: int, k: int, quant: str) -> DeviceWeight:
         """Device copy of `weight`, uploaded on first use."""
+        # fast path: the same array object as a cached entry (the entry holds
+        # a reference to it, so its id cannot be reused while cached)
+        hit = self._by_id.get(id(weight))
+        if hit is not None and hit[1] is weight and hit[0].handle is not None and hit[2] == (quant, n, k):
+            return hit[0]
         lib = self._require()
         raw = _raw_bytes(weight)
         key = (raw.ctypes.data, raw.nbytes, quant, int(n), int(k))
         with self._mu:
-            hit = self._cache.get(key)
-            if hit is not None:
-                return hit[0]
-            dw = DeviceWeight(lib, self.device, quant, raw, n, k)
-            self._cache[key] = (dw, raw)
-            return dw
+            entry = self._cache.get(key)
+            if entry is None:
+                entry = (DeviceWeight(lib, self.device, quant, raw, n, k), raw)
+                self._cache[key] = entry
+            self._by_id[id(weight)] = (entry[0], weight, (quant, n, k))
+            return entry[0]
 
     def close(self) -> None:
         with self._mu:
             for dw, _ in self._cache.values():
                 dw.free()
             self._cache.clear()
+            self._by_id.clear()
 
     @property
     def resident_bytes(self) -> int:
         return sum(dw.nbytes for dw, _ in self._cache.values())
 
     def _matmul(self, quant: str, x, weight, n: int, k: int) -> np.ndarray:
-        self._require()
-        x_c = np.ascontiguousarray(x, dtype=np.float32)
+        if self._lib is None or self.device >= self._ndev:
+            self._require()
+        x_c = x if (type(x) is np.ndarray and x.dtype == np.float32 and x.flags.c_contiguous) \
+            else np.ascontiguousarray(x, dtype=np.float32)
         if x_c.ndim == 1:
             if x_c.shape[0] != k:
                 raise ValueError(f"x.shape[0]={x_c.shape[0]} != k={k}")

@@ -130,6 +130,11 @@ struct DeviceState {
   size_t cap_x = 0;
   float* scratch_y = nullptr;
   size_t cap_y = 0;
+  // pinned staging of small host-buffer calls: x is copied in, y out through
+  // it, so both transfers are asynchronous DMA (a pageable transfer is staged
+  // by the driver through its own buffer, one synchronous copy per call)
+  uint8_t* pinned = nullptr;
+  size_t cap_pinned = 0;
   // activation records of the batched tensor-core kernel: grown on demand and
   // never freed while the process runs, so work already queued (or captured
   // in a graph) keeps a valid pointer after a larger call replaces it
@@ -160,6 +165,10 @@ struct DeviceGuard {
 // State of `dev`, created on first use (with `dev` current).
 int device_state(int dev, DeviceState** out) {
   std::lock_guard<std::mutex> lock(g_dev_mu);
+  if (dev >= 0 && static_cast<size_t>(dev) < g_devs.size() && g_devs[dev]) {  // created before
+    *out = g_devs[dev].get();
+    return FRC_OK;
+  }
   int count = 0;
   FRC_CUDA(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
   if (dev < 0 || dev >= count) return fail(FRC_ERR_INVALID, "device %d out of range (%d devices)", dev, count);
@@ -196,6 +205,27 @@ int ensure(T** buf, size_t* cap, size_t bytes, const char* what) {
   want = (want + 255) / 256 * 256;
   FRC_CUDA(cudaMalloc(reinterpret_cast<void**>(buf), want), what);
   *cap = want;
+  return FRC_OK;
+}
+
+// Host-buffer transfers up to this size go through the pinned staging
+// buffer; larger ones are copied directly.
+constexpr size_t kPinnedStageMax = size_t(4) << 20;
+
+// Pinned staging of at least `bytes` (grown on demand, freed only on
+// growth: a host-buffer call has synchronised before it returns, so no
+// transfer from an older buffer is in flight).
+int pinned_stage(DeviceState* ds, size_t bytes, uint8_t** out) {
+  if (bytes > ds->cap_pinned) {
+    size_t want = ds->cap_pinned ? 2 * ds->cap_pinned : (size_t(256) << 10);
+    while (want < bytes) want *= 2;
+    if (ds->pinned) cudaFreeHost(ds->pinned);
+    ds->pinned = nullptr;
+    ds->cap_pinned = 0;
+    FRC_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ds->pinned), want), "cudaMallocHost(staging)");
+    ds->cap_pinned = want;
+  }
+  *out = ds->pinned;
   return FRC_OK;
 }
 
@@ -344,13 +374,28 @@ int host_matmul(DeviceState* ds, int quant, const uint8_t* w_dev, const uint8_t*
   if (rc) return rc;
   rc = ensure(&ds->scratch_y, &ds->cap_y, sizeof(float) * seq * (n ? n : 1), "cudaMalloc(y scratch)");
   if (rc) return rc;
-  if (k && seq)
-    FRC_CUDA(cudaMemcpyAsync(ds->scratch_x, x, sizeof(float) * seq * k, cudaMemcpyHostToDevice, ds->stream), "x upload");
+  const size_t xb = sizeof(float) * seq * k, yb = sizeof(float) * seq * n;
+  const bool staged = xb <= kPinnedStageMax && yb <= kPinnedStageMax;
+  uint8_t* stage = nullptr;
+  if (staged) {
+    rc = pinned_stage(ds, (xb + 255) / 256 * 256 + yb, &stage);
+    if (rc) return rc;
+  }
+  float* y_stage = staged ? reinterpret_cast<float*>(stage + (xb + 255) / 256 * 256) : y;
+  if (xb) {
+    const void* src = x;
+    if (staged) {
+      std::memcpy(stage, x, xb);
+      src = stage;
+    }
+    FRC_CUDA(cudaMemcpyAsync(ds->scratch_x, src, xb, cudaMemcpyHostToDevice, ds->stream), "x upload");
+  }
   rc = gemv_device(ds, quant, w_dev, n, k, ds->scratch_x, seq, ds->scratch_y, ds->stream);
   if (rc) return rc;
-  if (n && seq)
-    FRC_CUDA(cudaMemcpyAsync(y, ds->scratch_y, sizeof(float) * seq * n, cudaMemcpyDeviceToHost, ds->stream), "y download");
-  return finish_host_call(ds);
+  if (yb) FRC_CUDA(cudaMemcpyAsync(y_stage, ds->scratch_y, yb, cudaMemcpyDeviceToHost, ds->stream), "y download");
+  rc = finish_host_call(ds);
+  if (rc == FRC_OK && staged && yb) std::memcpy(y, y_stage, yb);
+  return rc;
 }
 
 int host_dequant(DeviceState* ds, int quant, const uint8_t* w_dev, const uint8_t* w_host, size_t w_bytes,
@@ -468,6 +513,9 @@ int noalloc_device(int* dev_out, NoAllocDevice** out) {
 }  // namespace
 
 extern "C" {
+
+// Message recorder for the other translation units of the library.
+int frc__fail(int code, const char* msg) { return fail(code, "%s", msg); }
 
 int frc_version(char* buf, size_t len) {
   static const char kVersion[] = "frcuda 0.1.0 (sm_100a; Q8_0 Q4_K Q5_K Q6_K Q1_0; TMA-staged GEMV)";
@@ -608,6 +656,51 @@ int frc_gemv_noalloc(int quant, const void* w_dev, size_t w_bytes, int64_t n, in
   r.sms = d->sms;
   r.xrec = d->records;
   return launch_gemv_quant(quant, r);
+}
+
+int frc_gemv_ex(int quant, int count, const void* const* w_dev, const size_t* w_bytes, const int64_t* n, int64_t k,
+                const float* x_dev, const float* x_mul_dev, int flags, float* const* y_dev, void* stream) {
+  if (count < 1 || count > 4) return fail(FRC_ERR_INVALID, "frc_gemv_ex: count must be 1..4 (got %d)", count);
+  if (!w_dev || !w_bytes || !n || !y_dev) return fail(FRC_ERR_INVALID, "null array");
+  if (flags & ~FRC_GEMV_ACCUMULATE) return fail(FRC_ERR_INVALID, "frc_gemv_ex: unknown flags 0x%x", flags);
+  int64_t total = 0;
+  for (int m = 0; m < count; ++m) {
+    int rc = check_matmul(quant, w_bytes[m], n[m], k, 1);
+    if (rc) return rc;
+    if ((w_bytes[m] && !w_dev[m]) || (n[m] && !y_dev[m])) return fail(FRC_ERR_INVALID, "null buffer");
+    if (!aligned(w_dev[m], 16)) return fail(FRC_ERR_INVALID, "frc_gemv_ex: weight %d must be 16-byte aligned", m);
+    if (!aligned(y_dev[m], 4)) return fail(FRC_ERR_INVALID, "frc_gemv_ex: y %d must be 4-byte aligned", m);
+    total += n[m];
+  }
+  if ((k && !x_dev) || !aligned(x_dev, 16) || !aligned(x_mul_dev, 16))
+    return fail(FRC_ERR_INVALID, "frc_gemv_ex: x and x_mul must be 16-byte aligned");
+  if (k == 0 || total == 0) return fail(FRC_ERR_UNSUPPORTED, "frc_gemv_ex: empty shapes");
+  DeviceState* ds;
+  int rc = current_device_state(&ds);
+  if (rc) return rc;
+  frc::GemvRequest r{};
+  r.k = static_cast<int>(k);
+  r.x = x_dev;
+  r.batch = 1;
+  r.status = ds->status;
+  r.stream = static_cast<cudaStream_t>(stream);
+  r.device = ds->device;
+  r.sms = ds->sms;
+  r.nmat = count;
+  for (int m = 0; m < count; ++m) {
+    r.mat_w[m] = static_cast<const uint8_t*>(w_dev[m]);
+    r.mat_y[m] = y_dev[m];
+    r.mat_n[m] = n[m];
+  }
+  r.w = r.mat_w[0];
+  r.y = r.mat_y[0];
+  r.n = count == 1 ? n[0] : total;
+  r.x_mul = x_mul_dev;
+  r.y_accum = (flags & FRC_GEMV_ACCUMULATE) ? 1 : 0;
+  rc = launch_gemv_quant(quant, r);
+  if (rc == FRC_OK) return FRC_OK;
+  (void)cudaGetLastError();
+  return fail(FRC_ERR_UNSUPPORTED, "frc_gemv_ex: no batch-1 fp32 launch for this shape or option (%s)", g_err.c_str());
 }
 
 int frc_noalloc_status(int device, uint32_t* flags) {

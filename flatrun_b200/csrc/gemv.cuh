@@ -73,6 +73,11 @@ struct GemvParams {
   int w_world;
   const uint32_t* w_flags;
   const uint32_t* w_epoch;
+  // gemv_b1 with fp32 activations: x_mul != null reads the activations as
+  // silu(x) * x_mul (the SwiGLU of a gate and an up projection feeding down);
+  // y_accum adds to y instead of storing (a residual stream)
+  const float* x_mul;
+  int y_accum;
 };
 
 constexpr int kMaxMats = 4;
@@ -286,6 +291,7 @@ FRC_DEVICE_INLINE void griddep_launch_dependents() { asm volatile("griddepcontro
 // Stores one y value locally and, with a fused all-gather, into every rank's
 // gathered buffer.
 FRC_DEVICE_INLINE void put_y(const GemvParams& p, float* dst, float v) {
+  if (p.y_accum) v += *dst;
   *dst = v;
   if (p.g_world > 1) {
     const int64_t off = dst - p.g_ybase;
@@ -417,7 +423,7 @@ __global__ void __launch_bounds__(b1_max_warps<Q, UPT, F32>() * 32, 1) gemv_b1(G
     for (int i = 0; i < UPT; ++i) {
       const int u = st + i * spt;
       if (uval[i]) {
-        xu[i].load(p.x, u / I8<Q>::UPB, u % I8<Q>::UPB);
+        xu[i].load(p.x, p.x_mul, u / I8<Q>::UPB, u % I8<Q>::UPB);
       } else {
         xu[i].zero();
       }
@@ -472,27 +478,18 @@ __global__ void __launch_bounds__(b1_max_warps<Q, UPT, F32>() * 32, 1) gemv_b1(G
       // offset modulo 16 (only the low bits of the product matter)
       const uint32_t base = stages_s + static_cast<uint32_t>(s) * static_cast<uint32_t>(p.stage_stride) +
                             ((static_cast<uint32_t>(tile.local) * static_cast<uint32_t>(p.row_bytes)) & 15u);
-      if (rows == RPS) {
-        // full tile: no per-row guard, so the rows' independent instruction
-        // streams can be interleaved
+      // Every thread runs every row of the tile with no branch: a thread
+      // without a unit (its row's units do not fill the slot's last warp)
+      // reads unit 0's bytes with zero activations, and the rows past a
+      // short tile read whatever the stage held before (always inside the
+      // stage); the selects drop both.  The rows' independent instruction
+      // streams can then be interleaved.
 #pragma unroll
-        for (int i = 0; i < UPT; ++i) {
-          if (uval[i]) {
-#pragma unroll
-            for (int r = 0; r < RPS; ++r)
-              acc[r] += unit_dot<Q, F32>(base + static_cast<uint32_t>(r * p.row_bytes), cx[i], xu[i]);
-          }
-        }
-      } else {
+      for (int i = 0; i < UPT; ++i) {
 #pragma unroll
         for (int r = 0; r < RPS; ++r) {
-          if (r < rows) {
-            const uint32_t row = base + static_cast<uint32_t>(r * p.row_bytes);
-#pragma unroll
-            for (int i = 0; i < UPT; ++i) {
-              if (uval[i]) acc[r] += unit_dot<Q, F32>(row, cx[i], xu[i]);
-            }
-          }
+          const float v = unit_dot<Q, F32>(base + static_cast<uint32_t>(r * p.row_bytes), cx[i], xu[i]);
+          acc[r] += (uval[i] && r < rows) ? v : 0.0f;
         }
       }
     } else if (st == 0) {

@@ -53,6 +53,9 @@ struct GemvRequest {
   int w_world;  // batch-1: wait for an earlier fused gather before reading x
   const uint32_t* w_flags;
   const uint32_t* w_epoch;
+  // batch-1, fp32 activations: x read as silu(x) * x_mul; y accumulated
+  const float* x_mul;
+  int y_accum;
 };
 
 struct DequantRequest {
@@ -248,13 +251,19 @@ inline cudaError_t launch_b1_rps(GemvParams p, const GemvRequest& r, int slots, 
 constexpr int kSmemBudget = 227 * 1024;
 
 // Bytes of weights per tile the batch-1 kernel aims for (rows per tile = the
-// largest power of two <= 8 whose tile fits), swept on B200 with the integer
+// largest power of two <= 8 whose tile fits), swept on B200.  Integer
 // kernel: ~8 KB for short K-quant rows, 12 KB (four 2940-byte rows) for the
 // k = 3584 Q6_K lm_head (4.3 -> 5.1 TB/s), 18 KB (four rows) for k = 4096
 // Q8_0, 4 KB (four rows) for Q1_0; long rows (k > ~14K for Q4_K) two-row
 // tiles up to 32 KB.
-template <int Q>
+template <int Q, bool F32>
 inline int b1_tile_target(int row_bytes) {
+  // the fp32-activation kernel spends more per tile (its dot is longer and
+  // the per-tile reduction is the same), so it wants more rows per tile:
+  // swept on B200, a Llama-3-70B layer's gate+up (4608-byte rows) runs 0.29
+  // -> 0.50 of the copy peak with ~32 KB tiles, its down (16128-byte rows)
+  // 2.2 -> 2.8 TB/s with ~64 KB; the Qwen2-7B shapes are insensitive
+  if constexpr (F32) return row_bytes > 8192 ? 64 * 1024 : 32 * 1024;
   if (row_bytes > 8192) return 32 * 1024;
   if constexpr (Q == kQ6_K) return 12 * 1024;
   if constexpr (Q == kQ8_0) return 18 * 1024;
@@ -275,7 +284,7 @@ inline cudaError_t launch_b1(GemvParams p, const GemvRequest& r) {
   if (slots < 1) slots = 1;
   if (slots * p.wps > kMaxW) slots = kMaxW / p.wps;
   if (slots < 1) return cudaErrorInvalidValue;
-  const int tile_target = tuned(tuning().tile_bytes, b1_tile_target<Q>(p.row_bytes));
+  const int tile_target = tuned(tuning().tile_bytes, b1_tile_target<Q, F32>(p.row_bytes));
   int rps = 1;
   while (rps < 8 && 2 * rps * p.row_bytes <= tile_target) rps *= 2;
   const int forced = tuning().rps;
@@ -660,6 +669,10 @@ cudaError_t launch_gemv(const GemvRequest& r) {
     p.w_epoch = r.w_epoch;
   }
   const bool exact_batched = opt(options().batched_fp32) != 0;
+  if ((r.x_mul || r.y_accum) && (r.batch != 1 || r.g_world > 1 || opt(options().batch1_int16)))
+    return cudaErrorNotSupported;  // only the batch-1 fp32-activation kernel has them
+  p.x_mul = r.x_mul;
+  p.y_accum = r.y_accum;
   if (r.batch == 1) {
     GemvParams b1 = p;
     b1.units = (r.k / F::QK) * I8<Q>::UPB;
@@ -668,8 +681,9 @@ cudaError_t launch_gemv(const GemvRequest& r) {
     if (e != cudaErrorInvalidValue) return e;
     (void)cudaGetLastError();
     // a row longer than one CTA's threads cover: the column-reusing kernel
-    // (fp32 activations), without the fused multi-matrix or gather forms
-    if (r.nmat > 1 || r.g_world > 1 || r.w_world > 1) return cudaErrorNotSupported;
+    // (fp32 activations), without the fused multi-matrix, gather, SwiGLU or
+    // accumulating forms
+    if (r.nmat > 1 || r.g_world > 1 || r.w_world > 1 || r.x_mul || r.y_accum) return cudaErrorNotSupported;
     return launch_xb<Q, 4>(p, r);
   }
   // the fused multi-matrix launch and the fused all-gather exist only in the

@@ -35,11 +35,15 @@ struct UnitXF {
   static constexpr int E = I8<Q>::E, NG = I8<Q>::NG, GE = E / NG;
   float x[E];
   float xs[NG];
+  const float* mul_ = nullptr;  // silu(x) * mul activations (see load)
+  int j_ = 0;
 
   // Unit j of block b.  Every 16 consecutive unit elements are 16 consecutive
   // elements of x, so the unit loads as E/4 float4s, all issued before any
-  // is used; finish() then forms the group sums.
-  FRC_DEVICE_INLINE void load(const float* xg, int64_t b, int j) {
+  // is used; finish() then forms the group sums.  With `mul` the
+  // activations are silu(x) * mul, formed in finish() as the reference does
+  // (s = 1 / (1 + exp(-gate)); s * gate * up, qwen2.py:1690-1751).
+  FRC_DEVICE_INLINE void load(const float* xg, const float* mul, int64_t b, int j) {
     const float* blk = xg + b * Fmt<Q>::QK;
 #pragma unroll
     for (int r = 0; r < E / 16; ++r) {
@@ -53,8 +57,27 @@ struct UnitXF {
         x[16 * r + 4 * q + 3] = v.w;
       }
     }
+    mul_ = mul ? mul + b * Fmt<Q>::QK : nullptr;
+    j_ = j;
   }
   FRC_DEVICE_INLINE void finish() {
+    if (mul_) {
+#pragma unroll
+      for (int r = 0; r < E / 16; ++r) {
+        const float4* src = reinterpret_cast<const float4*>(mul_ + i8_pos<Q>(j_, 16 * r));
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 u = __ldg(src + q);
+          const float us[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float g = x[16 * r + 4 * q + e];
+            const float s = 1.0f / (1.0f + expf(-g));
+            x[16 * r + 4 * q + e] = (s * g) * us[e];
+          }
+        }
+      }
+    }
 #pragma unroll
     for (int g = 0; g < NG; ++g) {
       float s0 = 0.f, s1 = 0.f;
@@ -71,6 +94,7 @@ struct UnitXF {
     for (int e = 0; e < E; ++e) x[e] = 0.f;
 #pragma unroll
     for (int g = 0; g < NG; ++g) xs[g] = 0.f;
+    mul_ = nullptr;
   }
 };
 

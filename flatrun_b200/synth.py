@@ -72,6 +72,42 @@ def make_weight(fmt: str, n: int, k: int, seed: int = 0) -> np.ndarray:
     return blk.reshape(-1)
 
 
+def pack_k_scales(sc: np.ndarray, m: np.ndarray) -> np.ndarray:
+    """The 12 packed bytes of 8 six-bit scales and mins per K-quant block
+    (the inverse of the unpack in dequant/gguf.py:135-163): for j < 4 byte j
+    is sc[j] with the top two bits of sc[j+4] in bits 6-7, byte j+4 is m[j]
+    with the top bits of m[j+4]; byte j+8 holds the low nibbles of sc[j+4]
+    and m[j+4]."""
+    sc = sc.astype(np.uint8)
+    m = m.astype(np.uint8)
+    out = np.empty(sc.shape[:-1] + (12,), np.uint8)
+    out[..., 0:4] = sc[..., 0:4] | ((sc[..., 4:8] >> 4) << 6)
+    out[..., 4:8] = m[..., 0:4] | ((m[..., 4:8] >> 4) << 6)
+    out[..., 8:12] = (sc[..., 4:8] & 0x0F) | ((m[..., 4:8] & 0x0F) << 4)
+    return out
+
+
+def make_centered_q4_k(n: int, k: int, seed: int = 0) -> np.ndarray:
+    """Q4_K blocks whose weights have mean ~0, as trained K-quants do (for
+    random-init models run for many layers): dmin = d = fp16(|N(0,1)| *
+    0.01), scales uniform in [1, 8], mins round(7.5 * scale), so
+    d*sc*q - dmin*m is centred on the nibble range's middle; quant bytes
+    uniform.  The matvec benchmarks' distribution (uniform scales and mins,
+    make_weight) has mean ~1.6 per weight, which makes a residual stream
+    grow without bound over many layers."""
+    nb = n * (k // 256)
+    row_bytes("Q4_K", k)
+    rng = np.random.default_rng(seed)
+    blk = np.empty((nb, 144), np.uint8)
+    d = (np.abs(rng.standard_normal(nb)) * 0.01).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    blk[:, 0:2] = d
+    blk[:, 2:4] = d
+    sc = rng.integers(1, 9, size=(nb, 8))
+    blk[:, 4:16] = pack_k_scales(sc, np.rint(7.5 * sc))
+    blk[:, 16:144] = rng.integers(0, 256, size=(nb, 128), dtype=np.uint8)
+    return blk.reshape(-1)
+
+
 def make_random_blocks(fmt: str, n_blocks: int, seed: int = 0) -> np.ndarray:
     """Fully random bytes, scale fields included (so fp16 subnormals, inf and
     NaN scales occur): an edge-case generator for bit-exact dequant checks."""

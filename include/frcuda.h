@@ -154,6 +154,55 @@ int frc_noalloc_status(int device, uint32_t* flags);
  * reference dispatches one projection per call, flatrun/model/qwen2.py:1510-1519.) */
 int frc_gemv_multi(int quant, int count, const void* const* w_dev, const size_t* w_bytes, const int64_t* n,
                    int64_t k, const float* x_dev, int64_t batch, float* const* y_dev, void* stream);
+/* Batch-1 launch of up to 4 weights of the same quant and k sharing x (as
+ * frc_gemv_multi) with two options of the fp32-activation kernel, for a
+ * device-resident decoder step (no reference counterpart: the reference
+ * forwarder does both in NumPy, flatrun/model/qwen2.py:1617-1646, :1690-1751):
+ *  - x_mul_dev != NULL: the activations are silu(x) * x_mul elementwise,
+ *    silu(g) = g / (1 + exp(-g)) evaluated as (1 / (1 + exp(-g))) * g, so a
+ *    gate and an up projection feed the down projection with no SwiGLU pass;
+ *  - flags & FRC_GEMV_ACCUMULATE: y += W x instead of y = W x (a residual
+ *    stream).
+ * FRC_ERR_UNSUPPORTED when the batch-1 int16 option is set or the row is
+ * too long for one CTA. */
+#define FRC_GEMV_ACCUMULATE 1
+int frc_gemv_ex(int quant, int count, const void* const* w_dev, const size_t* w_bytes, const int64_t* n,
+                int64_t k, const float* x_dev, const float* x_mul_dev, int flags, float* const* y_dev,
+                void* stream);
+
+/* ---- device-resident decoder step ----------------------------------------- *
+ * The operators of a Qwen2/Llama decode token around the projections, so a
+ * whole token runs on the GPU (stream-ordered, no synchronisation, graph
+ * capturable).  They restate the reference forwarder's NumPy steps
+ * (flatrun/model/qwen2.py): RMSNorm :365-378, q/k/v bias + rotate-half RoPE
+ * + KV append :1527-1595 (tables :398-476), GQA attention :1597-1614,
+ * embedding row :2153-2159.  The token's position is read from device
+ * memory (pos_dev, one int) so the same launches replay for every token;
+ * frc_pos_advance increments it.
+ *  frc_rmsnorm: out[r] = x[r] * (1 / sqrt(mean(x[r]^2) + eps)) * w, rows of n.
+ *  frc_rope_append: qkv = [q (nh*hd) | k (nkv*hd) | v (nkv*hd)] of one token;
+ *    adds `bias` (same layout, may be NULL), rotates q in place and k at
+ *    position *pos_dev with cos/sin tables [max_pos][hd/2], writes k and v to
+ *    row *pos_dev of the caches ([max_pos][nkv][hd]).
+ *  frc_attention_decode: one query token (q, nh*hd, rotated) over cache rows
+ *    0..*pos_dev: softmax(q.k * scale) . v per head, query head h reading KV
+ *    head h / (nh/nkv); positions split into `splits` ranges (flash
+ *    decoding) whose partials (frc_attention_workspace floats in `part`) are
+ *    merged into out (nh*hd).  hd <= 128 and a multiple of 4, nh/nkv <= 16.
+ *  frc_argmax: index of the largest of n floats into *out_dev (the lowest
+ *    index among ties, as np.argmax).
+ *  frc_embed_row: row *tok_dev of a (vocab, n) table into out: quant 0 for
+ *    fp32 rows, or a GGUF quant id (dequantised bit-exactly). */
+int frc_rmsnorm(const float* x, const float* w, int64_t rows, int64_t n, float eps, float* out, void* stream);
+int frc_rope_append(float* qkv, const float* bias, int nh, int nkv, int hd, const float* cos_table,
+                    const float* sin_table, const int* pos_dev, float* k_cache, float* v_cache, void* stream);
+int frc_attention_workspace(int nh, int hd, int splits, size_t* floats);
+int frc_attention_decode(const float* q, const float* k_cache, const float* v_cache, const int* pos_dev, int nh,
+                         int nkv, int hd, float scale, int splits, float* part, float* out, void* stream);
+int frc_argmax(const float* x, int64_t n, int* out_dev, void* stream);
+int frc_embed_row(int quant, const void* table, int64_t n, const int* tok_dev, float* out, void* stream);
+int frc_pos_advance(int* pos_dev, void* stream);
+
 /* ---- row-sharded projections: all-gather fused into the GEMV ----------- *
  * No reference counterpart: the reference runs on one CPU.  One process per
  * GPU; rank r owns a contiguous row range of every projection and computes
