@@ -440,8 +440,8 @@ def run_device_decode(args, wl: dict, config: dict, step_bytes: int) -> None:
     lib = eng.lib
     y = torch.empty(V, device="cuda")
     args_ = (lm[1], 1, (ctypes.c_void_p * 1)(lm[0].data_ptr()), (ctypes.c_size_t * 1)(lm[0].numel()),
-             (ctypes.c_int64 * 1)(V), H, eng.x.data_ptr(), None, 0, (ctypes.c_void_p * 1)(y.data_ptr()),
-             ctypes.c_void_p(st.cuda_stream))
+             (ctypes.c_int64 * 1)(V), H, eng.h.data_ptr(), None, eng._norm["model.norm.weight"].data_ptr(), 1e-6, 0,
+             (ctypes.c_void_p * 1)(y.data_ptr()), ctypes.c_void_p(st.cuda_stream))
     for _ in range(3):
         _lib.check(lib.frc_gemv_ex(*args_), lib)
     nl = min(K, 200)

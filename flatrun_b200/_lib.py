@@ -47,13 +47,14 @@ SIGNATURES: dict[str, list] = {
     "frc_set_option": [_i, _i],
     "frc_get_option": [_i, ctypes.POINTER(_i)],
     "frc_noalloc_status": [_i, ctypes.POINTER(ctypes.c_uint32)],
-    "frc_gemv_ex": [_i, _i, ctypes.POINTER(_p), ctypes.POINTER(_sz), ctypes.POINTER(_i64), _i64, _p, _p, _i,
-                    ctypes.POINTER(_p), _p],
+    "frc_gemv_ex": [_i, _i, ctypes.POINTER(_p), ctypes.POINTER(_sz), ctypes.POINTER(_i64), _i64, _p, _p, _p,
+                    ctypes.c_float, _i, ctypes.POINTER(_p), _p],
     "frc_rmsnorm": [_p, _p, _i64, _i64, ctypes.c_float, _p, _p],
     "frc_rope_append": [_p, _p, _i, _i, _i, _p, _p, _p, _p, _p, _p],
     "frc_attention_workspace": [_i, _i, _i, ctypes.POINTER(_sz)],
     "frc_attention_decode": [_p, _p, _p, _p, _i, _i, _i, ctypes.c_float, _i, _p, _p, _p],
-    "frc_argmax": [_p, _i64, _p, _p],
+    "frc_argmax_workspace": [_i64, ctypes.POINTER(_sz)],
+    "frc_argmax": [_p, _i64, _p, _p, _p],
     "frc_embed_row": [_i, _p, _i64, _p, _p, _p],
     "frc_pos_advance": [_p, _p],
     "frc_gemv": [_i, _p, _sz, _i64, _i64, _p, _i64, _p, _p],

@@ -99,11 +99,72 @@ class DeviceWeight:
             pass
 
 
-class CudaBackend:
-    """B200 fused dequant + matvec backend (``--backend cuda``)."""
+class ShardedWeight:
+    """One (n, k) weight whose rows are split over several GPUs in one process.
 
-    def __init__(self, device: int = 0, lib_path: str | None = None):
+    Rows are independent and every row is a whole number of quant blocks, so
+    device i holds the contiguous rows ``shard.row_range(n, len(devices), i)``
+    (the same split as the one-process-per-GPU path).  A call runs every
+    shard at once (one host thread per device; the C ABI releases the GIL)
+    and writes each shard's outputs straight into its columns of y: the
+    assembly is the host copy the reference's API needs anyway.
+    """
+
+    def __init__(self, lib, devices: list, quant: str, raw: np.ndarray, n: int, k: int):
+        from concurrent.futures import ThreadPoolExecutor
+
+        from .shard import row_range
+        from .synth import row_bytes
+
+        self.quant, self.n, self.k, self.nbytes = quant, int(n), int(k), int(raw.nbytes)
+        rb = row_bytes(quant, k)
+        self.parts = []
+        for i, dev in enumerate(devices):
+            r0, r1 = row_range(self.n, len(devices), i)
+            if r1 > r0:
+                self.parts.append((DeviceWeight(lib, dev, quant, raw[r0 * rb:r1 * rb], r1 - r0, k), r0, r1))
+        self._pool = ThreadPoolExecutor(max_workers=max(1, len(self.parts)))
+
+    def matmul(self, x: np.ndarray) -> np.ndarray:
+        y = np.empty((self.n,) if x.ndim == 1 else (x.shape[0], self.n), dtype=np.float32)
+
+        def run(part):
+            dw, r0, r1 = part
+            y[..., r0:r1] = dw.matmul(x)
+
+        for f in [self._pool.submit(run, p) for p in self.parts]:
+            f.result()
+        return y
+
+    def dequant(self) -> np.ndarray:
+        return np.concatenate([dw.dequant() for dw, _, _ in self.parts], axis=0)
+
+    def free(self) -> None:
+        for dw, _, _ in self.parts:
+            dw.free()
+        self._pool.shutdown(wait=False)
+
+    @property
+    def handle(self):
+        return self.parts[0][0].handle if self.parts else None
+
+
+def devices_from_env(default: int = 0) -> list:
+    """GPUs named by FLATRUN_CUDA_DEVICES (comma-separated ids), else [default]."""
+    import os
+    spec = os.environ.get("FLATRUN_CUDA_DEVICES", "").strip()
+    return [int(d) for d in spec.split(",") if d.strip()] if spec else [default]
+
+
+class CudaBackend:
+    """B200 fused dequant + matvec backend (``--backend cuda``).
+
+    `devices`: GPUs to row-shard every projection over (one process); by
+    default the single `device`."""
+
+    def __init__(self, device: int = 0, lib_path: str | None = None, devices: list | None = None):
         self.device = int(device)
+        self.devices = [int(d) for d in devices] if devices else [self.device]
         self._load_error: BaseException | None = None
         try:
             self._lib = _lib.load(lib_path)
@@ -112,6 +173,8 @@ class CudaBackend:
             self._lib = None
             self._ndev = 0
             self._load_error = exc
+        if self.devices != [self.device]:
+            self.device = max(self.devices)  # availability checks the highest id
         self._cache: dict[tuple, tuple[DeviceWeight, np.ndarray]] = {}
         self._by_id: dict[int, tuple] = {}
         self._mu = threading.Lock()
@@ -150,7 +213,9 @@ class CudaBackend:
         with self._mu:
             entry = self._cache.get(key)
             if entry is None:
-                entry = (DeviceWeight(lib, self.device, quant, raw, n, k), raw)
+                dw = DeviceWeight(lib, self.devices[0], quant, raw, n, k) if len(self.devices) == 1 else \
+                    ShardedWeight(lib, self.devices, quant, raw, n, k)
+                entry = (dw, raw)
                 self._cache[key] = entry
             self._by_id[id(weight)] = (entry[0], weight, (quant, n, k))
             return entry[0]
@@ -243,4 +308,4 @@ def block_geometry(quant: str) -> tuple[int, int]:
     return FORMATS[quant]
 
 
-__all__ = ["CudaBackend", "DeviceWeight", "QUANT_DISPATCH"]
+__all__ = ["CudaBackend", "DeviceWeight", "ShardedWeight", "QUANT_DISPATCH", "devices_from_env"]

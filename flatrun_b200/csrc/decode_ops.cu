@@ -19,7 +19,7 @@
 #include <cstdio>
 
 #include "../../include/frcuda.h"
-#include "formats.cuh"
+#include "gemv.cuh"
 
 namespace frc {
 
@@ -96,157 +96,248 @@ __global__ void rope_append_kernel(float* __restrict__ qkv, const float* __restr
 // Decode attention (one query token) over positions [0, *pos] of the caches,
 // split over positions ("flash decoding"): CTA (g, c) takes KV head g and
 // the c-th of `splits` position ranges, with the G = nh / nkv query heads
-// that read that KV head (GQA: query head h reads KV head h / G).
-//   phase 1: thread t scores position t of the range for every query head;
-//   phase 2: per head, the range's max and sum of exp(score - max);
-//   phase 3: thread d accumulates sum_t exp(score - max) * V[t][d] per head.
-// Partials (max, sum, acc[G][hd]) go to `part`; attn_combine merges them.
-// hd <= 128, G <= 16, blockDim.x = 128.
+// that read that KV head (GQA: query head h reads KV head h / G).  Head dim
+// HD (64 or 128): lane l of a warp owns dimensions VEC*l.. (VEC = HD / 32),
+// so every K or V row is one coalesced warp load.  Per chunk of positions:
+//   scores: warp w takes positions w, w+4, ...; the lanes' partial dots of
+//     the G heads are summed with one butterfly (G <= 8 values, 9 shuffles);
+//   softmax: per head, the chunk's max and sum of exp(score - max);
+//   A.V: warp w accumulates exp(score - max) * V over its positions, then
+//     merges into its running (max, sum, acc) per head.
+// The four warps' accumulators are added at the end; the range's partial
+// (max, sum, acc[G][128]) goes to `part` for attn_combine.
 // ---------------------------------------------------------------------------
 constexpr int kAttnThreads = 128;
 constexpr int kAttnMaxHd = 128;
-constexpr int kAttnMaxG = 16;
-constexpr int kAttnChunk = 128;  // positions scored per pass of a range
+constexpr int kAttnMaxG = 8;
+constexpr int kAttnChunk = 256;  // positions per pass of a range
 
+// VEC consecutive floats at p (16- or 8-byte aligned).
+template <int VEC>
+FRC_DEVICE_INLINE void load_vec(const float* p, float (&v)[VEC]) {
+  if constexpr (VEC == 4) {
+    const float4 t = *reinterpret_cast<const float4*>(p);
+    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+  } else {
+    static_assert(VEC == 2, "head_dim 64 or 128");
+    const float2 t = *reinterpret_cast<const float2*>(p);
+    v[0] = t.x; v[1] = t.y;
+  }
+}
+
+template <int HD>
 __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(
     const float* __restrict__ q, const float* __restrict__ k_cache, const float* __restrict__ v_cache,
-    const int* __restrict__ pos_ptr, int nh, int nkv, int hd, float scale, int splits, float* __restrict__ part) {
+    const int* __restrict__ pos_ptr, int nh, int nkv, float scale, int splits, float* __restrict__ part) {
+  constexpr int MG = kAttnMaxG, NW = kAttnThreads / 32, VEC = HD / 32;
   const int g = blockIdx.x, c = blockIdx.y;
   const int G = nh / nkv;
   const int total = *pos_ptr + 1;
   const int per = (total + splits - 1) / splits;
   const int t0 = c * per, t1 = min(total, t0 + per);
-  __shared__ float qs[kAttnMaxG][kAttnMaxHd];
-  __shared__ float sc[kAttnMaxG][kAttnChunk];
-  __shared__ float red[kAttnMaxG][2];
-  for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i / hd][i % hd] = q[(g * G + i / hd) * hd + i % hd];
-  float m_run[kAttnMaxG], l_run[kAttnMaxG], acc[kAttnMaxG];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ __align__(16) float sc[kAttnChunk][MG];  // scores, then exp(score - max)
+  __shared__ float cmax[MG], csum[MG];
+  __shared__ __align__(16) float wacc[NW][MG][HD];
+
+  float qv[MG][VEC];
 #pragma unroll
-  for (int h = 0; h < kAttnMaxG; ++h) {
+  for (int h = 0; h < MG; ++h) {
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) qv[h][e] = 0.f;
+    if (h < G) load_vec<VEC>(q + (g * G + h) * HD + VEC * lane, qv[h]);
+  }
+  float m_run[MG], l_run[MG], acc[MG][VEC];
+#pragma unroll
+  for (int h = 0; h < MG; ++h) {
     m_run[h] = -FLT_MAX;
     l_run[h] = 0.f;
-    acc[h] = 0.f;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) acc[h][e] = 0.f;
   }
-  __syncthreads();
-  const int d = threadIdx.x;
+  const int64_t row_stride = static_cast<int64_t>(nkv) * HD;
+  const float* kb = k_cache + static_cast<int64_t>(g) * HD + VEC * lane;
+  const float* vb = v_cache + static_cast<int64_t>(g) * HD + VEC * lane;
   for (int base = t0; base < t1; base += kAttnChunk) {
     const int n_t = min(kAttnChunk, t1 - base);
-    // phase 1: scores of position base + tid for every head
-    if (threadIdx.x < n_t) {
-      const float4* kr = reinterpret_cast<const float4*>(k_cache + (static_cast<int64_t>(base + threadIdx.x) * nkv + g) * hd);
-      float s[kAttnMaxG];
+    // scores: each warp takes four positions per pass so that four row loads
+    // are in flight at once
+    for (int t = warp; t < n_t; t += 4 * NW) {
+      float kr[4][VEC];
 #pragma unroll
-      for (int h = 0; h < kAttnMaxG; ++h) s[h] = 0.f;
-      for (int i = 0; i < hd / 4; ++i) {
-        const float4 kv = kr[i];
+      for (int u = 0; u < 4; ++u) {
 #pragma unroll
-        for (int h = 0; h < kAttnMaxG; ++h) {
-          if (h < G) {
-            s[h] = fmaf(qs[h][4 * i], kv.x, s[h]);
-            s[h] = fmaf(qs[h][4 * i + 1], kv.y, s[h]);
-            s[h] = fmaf(qs[h][4 * i + 2], kv.z, s[h]);
-            s[h] = fmaf(qs[h][4 * i + 3], kv.w, s[h]);
-          }
-        }
+        for (int e = 0; e < VEC; ++e) kr[u][e] = 0.f;
+        if (t + u * NW < n_t) load_vec<VEC>(kb + (base + t + u * NW) * row_stride, kr[u]);
       }
 #pragma unroll
-      for (int h = 0; h < kAttnMaxG; ++h)
-        if (h < G) sc[h][threadIdx.x] = s[h] * scale;
+      for (int u = 0; u < 4; ++u) {
+        float sv[MG];
+#pragma unroll
+        for (int h = 0; h < MG; ++h) {
+          sv[h] = 0.f;
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) sv[h] = fmaf(qv[h][e], kr[u][e], sv[h]);
+        }
+        butterfly<MG>(sv, lane);
+        // lane l now holds head l / 4's total
+        if ((lane & 3) == 0 && (lane >> 2) < G && t + u * NW < n_t) sc[t + u * NW][lane >> 2] = sv[0] * scale;
+      }
     }
     __syncthreads();
-    // phase 2: the chunk's max per head (warp h % 4 reduces head h), the
-    // running max and sum rescaled to it
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int h = warp; h < G; h += kAttnThreads / 32) {
+    // per head: the chunk's max, then exp(score - max) and their sum
+    for (int h = warp; h < G; h += NW) {
       float m = -FLT_MAX;
-      for (int t = lane; t < n_t; t += 32) m = fmaxf(m, sc[h][t]);
+      for (int t = lane; t < n_t; t += 32) m = fmaxf(m, sc[t][h]);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
       float l = 0.f;
       for (int t = lane; t < n_t; t += 32) {
-        const float e = expf(sc[h][t] - m);
-        sc[h][t] = e;
+        const float e = expf(sc[t][h] - m);
+        sc[t][h] = e;
         l += e;
       }
       l = warp_sum(l);
       if (lane == 0) {
-        red[h][0] = m;
-        red[h][1] = l;
+        cmax[h] = m;
+        csum[h] = l;
       }
     }
     __syncthreads();
-    // phase 3: merge into the running (max, sum, acc) of every head
-    if (d < hd) {
-      for (int h = 0; h < G; ++h) {
-        const float m_new = fmaxf(m_run[h], red[h][0]);
-        const float a_old = expf(m_run[h] - m_new), a_blk = expf(red[h][0] - m_new);
-        float s = 0.f;
-        for (int t = 0; t < n_t; ++t)
-          s = fmaf(sc[h][t], v_cache[(static_cast<int64_t>(base + t) * nkv + g) * hd + d], s);
-        acc[h] = acc[h] * a_old + s * a_blk;
-        l_run[h] = l_run[h] * a_old + red[h][1] * a_blk;
+    // A.V over this warp's positions of the chunk
+    float a[MG][VEC];
+#pragma unroll
+    for (int h = 0; h < MG; ++h)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) a[h][e] = 0.f;
+    for (int t = warp; t < n_t; t += 4 * NW) {
+      float vr[4][VEC];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) vr[u][e] = 0.f;
+        if (t + u * NW < n_t) load_vec<VEC>(vb + (base + t + u * NW) * row_stride, vr[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (t + u * NW < n_t) {
+          const float4 p0 = *reinterpret_cast<const float4*>(&sc[t + u * NW][0]);
+          const float4 p1 = *reinterpret_cast<const float4*>(&sc[t + u * NW][4]);
+          const float pw[MG] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+          for (int h = 0; h < MG; ++h)
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) a[h][e] = fmaf(pw[h], vr[u][e], a[h][e]);
+        }
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < MG; ++h) {
+      if (h < G) {
+        const float m_new = fmaxf(m_run[h], cmax[h]);
+        const float e_old = expf(m_run[h] - m_new), e_blk = expf(cmax[h] - m_new);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc[h][e] = acc[h][e] * e_old + a[h][e] * e_blk;
+        l_run[h] = l_run[h] * e_old + csum[h] * e_blk;
         m_run[h] = m_new;
       }
     }
-    __syncthreads();
+    __syncthreads();  // sc and cmax are rewritten by the next chunk
   }
-  // partial layout per (head, split): [max, sum, acc[hd]]
-  if (d < hd) {
+  // add the warps' accumulators; partial layout per (head, split):
+  // [max, sum, acc[HD]]
+#pragma unroll
+  for (int h = 0; h < MG; ++h)
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) wacc[warp][h][VEC * lane + e] = acc[h][e];
+  __syncthreads();
+  for (int d = threadIdx.x; d < HD; d += kAttnThreads) {
     for (int h = 0; h < G; ++h) {
-      float* pr = part + (static_cast<int64_t>(g * G + h) * splits + c) * (hd + 2);
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) v += wacc[w][h][d];
+      float* pr = part + (static_cast<int64_t>(g * G + h) * splits + c) * (HD + 2);
       if (d == 0) {
         pr[0] = m_run[h];
         pr[1] = l_run[h];
       }
-      pr[2 + d] = acc[h];
+      pr[2 + d] = v;
     }
   }
 }
 
 // Merge the splits of every head: out[h][d] = sum_c acc_c e^(m_c - M) /
-// sum_c l_c e^(m_c - M).  One CTA per head, one thread per d.
-__global__ void attn_combine_kernel(const float* __restrict__ part, int hd, int splits, float* __restrict__ out) {
-  const int h = blockIdx.x, d = threadIdx.x;
-  if (d >= hd) return;
+// sum_c l_c e^(m_c - M).  One CTA per head (one thread per d); the splits'
+// (max, sum) pairs are read in parallel first.
+constexpr int kAttnMaxSplits = 1024;
+
+__global__ void __launch_bounds__(kAttnMaxHd) attn_combine_kernel(const float* __restrict__ part, int hd, int splits,
+                                                                 float* __restrict__ out) {
+  const int h = blockIdx.x, d = threadIdx.x;  // blockDim.x = hd
+  const int nw = (blockDim.x + 31) >> 5;
   const float* ph = part + static_cast<int64_t>(h) * splits * (hd + 2);
-  float M = -FLT_MAX;
-  for (int c = 0; c < splits; ++c) M = fmaxf(M, ph[c * (hd + 2)]);
-  float L = 0.f, A = 0.f;
-  for (int c = 0; c < splits; ++c) {
-    const float* pc = ph + c * (hd + 2);
-    if (pc[1] == 0.f) continue;  // an empty range
-    const float e = expf(pc[0] - M);
-    L = fmaf(pc[1], e, L);
-    A = fmaf(pc[2 + d], e, A);
+  __shared__ float em[kAttnMaxSplits];
+  __shared__ float red[kAttnMaxHd / 32];
+  __shared__ float bcast[2];
+  float m = -FLT_MAX;
+  for (int c = d; c < splits; c += blockDim.x) m = fmaxf(m, ph[c * (hd + 2)]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((d & 31) == 0) red[d >> 5] = m;
+  __syncthreads();
+  if (d == 0) {
+    float M = red[0];
+    for (int w = 1; w < nw; ++w) M = fmaxf(M, red[w]);
+    bcast[0] = M;
   }
-  out[h * hd + d] = A / L;
+  __syncthreads();
+  const float M = bcast[0];
+  float L = 0.f;
+  for (int c = d; c < splits; c += blockDim.x) {
+    const float* pc = ph + c * (hd + 2);
+    const float e = pc[1] == 0.f ? 0.f : expf(pc[0] - M);  // an empty range contributes nothing
+    em[c] = e;
+    L = fmaf(pc[1], e, L);
+  }
+  L = warp_sum(L);
+  __syncthreads();
+  if ((d & 31) == 0) red[d >> 5] = L;
+  __syncthreads();
+  if (d == 0) {
+    float s = 0.f;
+    for (int w = 0; w < nw; ++w) s += red[w];
+    bcast[1] = s;
+  }
+  __syncthreads();
+  float A0 = 0.f, A1 = 0.f;
+  int c = 0;
+  for (; c + 1 < splits; c += 2) {
+    A0 = fmaf(ph[c * (hd + 2) + 2 + d], em[c], A0);
+    A1 = fmaf(ph[(c + 1) * (hd + 2) + 2 + d], em[c + 1], A1);
+  }
+  if (c < splits) A0 = fmaf(ph[c * (hd + 2) + 2 + d], em[c], A0);
+  out[h * hd + d] = (A0 + A1) / bcast[1];
 }
 
 // ---------------------------------------------------------------------------
 // Index of the largest of n values (the lowest index among equal maxima, as
-// np.argmax): one CTA.
+// np.argmax).  Every CTA reduces a slice into ws (value, index); the last
+// CTA to finish (ticket in ws) reduces the slices and resets the ticket, so
+// the kernel replays in a graph.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ x, int64_t n, int* __restrict__ out) {
-  float best = -FLT_MAX;
-  int64_t bi = 0;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = x[i];
-    if (v > best) {
-      best = v;
-      bi = i;
-    }
+FRC_DEVICE_INLINE void argmax_merge(float& best, int64_t& bi, float ov, int64_t oi) {
+  if (ov > best || (ov == best && oi < bi)) {
+    best = ov;
+    bi = oi;
   }
+}
+
+FRC_DEVICE_INLINE void argmax_block(float& best, int64_t& bi) {
   __shared__ float sv[32];
   __shared__ int64_t si[32];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > best || (ov == best && oi < bi)) {
-      best = ov;
-      bi = oi;
-    }
-  }
+  for (int o = 16; o > 0; o >>= 1)
+    argmax_merge(best, bi, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, bi, o));
   if ((threadIdx.x & 31) == 0) {
     sv[threadIdx.x >> 5] = best;
     si[threadIdx.x >> 5] = bi;
@@ -257,15 +348,42 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
     best = threadIdx.x < nw ? sv[threadIdx.x] : -FLT_MAX;
     bi = threadIdx.x < nw ? si[threadIdx.x] : INT64_MAX;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-      const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > best || (ov == best && oi < bi)) {
-        best = ov;
-        bi = oi;
-      }
-    }
-    if (threadIdx.x == 0) *out = static_cast<int>(bi);
+    for (int o = 16; o > 0; o >>= 1)
+      argmax_merge(best, bi, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, bi, o));
+  }
+}
+
+constexpr int kArgmaxThreads = 256;
+
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ x, int64_t n,
+                                                               int* __restrict__ out, int64_t* __restrict__ ws) {
+  // ws: [0] ticket, [1 + 2b] value bits, [2 + 2b] index of CTA b
+  const int64_t per = (n + gridDim.x - 1) / gridDim.x;
+  const int64_t i0 = blockIdx.x * per, i1 = min(n, i0 + per);
+  float best = -FLT_MAX;
+  int64_t bi = INT64_MAX;
+  for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) argmax_merge(best, bi, x[i], i);
+  argmax_block(best, bi);
+  __shared__ bool last;
+  if (threadIdx.x == 0) {
+    ws[1 + 2 * blockIdx.x] = __float_as_int(best);
+    ws[2 + 2 * blockIdx.x] = bi;
+    __threadfence();
+    last = atomicAdd(reinterpret_cast<unsigned long long*>(ws), 1ull) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  best = -FLT_MAX;
+  bi = INT64_MAX;
+  for (int b = threadIdx.x; b < static_cast<int>(gridDim.x); b += blockDim.x) {
+    const volatile int64_t* w = ws;
+    argmax_merge(best, bi, __int_as_float(static_cast<int>(w[1 + 2 * b])), w[2 + 2 * b]);
+  }
+  argmax_block(best, bi);
+  if (threadIdx.x == 0) {
+    *out = static_cast<int>(bi);
+    ws[0] = 0;
   }
 }
 
@@ -344,13 +462,18 @@ int frc_rope_append(float* qkv, const float* bias, int nh, int nkv, int hd, cons
 
 int frc_attention_decode(const float* q, const float* k_cache, const float* v_cache, const int* pos_dev, int nh,
                          int nkv, int hd, float scale, int splits, float* part, float* out, void* stream) {
-  FRC_DECODE_CHECK(nh > 0 && nkv > 0 && nh % nkv == 0 && nh / nkv <= frc::kAttnMaxG, "frc_attention_decode: bad heads");
-  FRC_DECODE_CHECK(hd > 0 && hd <= frc::kAttnMaxHd && hd % 4 == 0, "frc_attention_decode: head_dim must be 4..128, a multiple of 4");
-  FRC_DECODE_CHECK(splits >= 1 && splits <= 1024, "frc_attention_decode: splits must be 1..1024");
+  FRC_DECODE_CHECK(nh > 0 && nkv > 0 && nh % nkv == 0 && nh / nkv <= frc::kAttnMaxG,
+                   "frc_attention_decode: needs nh a multiple of nkv and at most 8 query heads per KV head");
+  FRC_DECODE_CHECK(hd == 64 || hd == 128, "frc_attention_decode: head_dim must be 64 or 128");
+  FRC_DECODE_CHECK(splits >= 1 && splits <= frc::kAttnMaxSplits, "frc_attention_decode: splits must be 1..1024");
   FRC_DECODE_CHECK(q && k_cache && v_cache && pos_dev && part && out, "frc_attention_decode: null pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  frc::attn_partial_kernel<<<dim3(nkv, splits), frc::kAttnThreads, 0, st>>>(q, k_cache, v_cache, pos_dev, nh, nkv,
-                                                                            hd, scale, splits, part);
+  if (hd == 128)
+    frc::attn_partial_kernel<128><<<dim3(nkv, splits), frc::kAttnThreads, 0, st>>>(q, k_cache, v_cache, pos_dev, nh,
+                                                                                   nkv, scale, splits, part);
+  else
+    frc::attn_partial_kernel<64><<<dim3(nkv, splits), frc::kAttnThreads, 0, st>>>(q, k_cache, v_cache, pos_dev, nh,
+                                                                                  nkv, scale, splits, part);
   int rc = launch_status("attention launch");
   if (rc) return frc__fail(rc, g_decode_err);
   frc::attn_combine_kernel<<<nh, hd, 0, st>>>(part, hd, splits, out);
@@ -363,9 +486,18 @@ int frc_attention_workspace(int nh, int hd, int splits, size_t* floats) {
   return FRC_OK;
 }
 
-int frc_argmax(const float* x, int64_t n, int* out_dev, void* stream) {
-  FRC_DECODE_CHECK(x && out_dev && n > 0, "frc_argmax: null pointer or empty input");
-  frc::argmax_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(x, n, out_dev);
+int frc_argmax_workspace(int64_t n, size_t* bytes) {
+  FRC_DECODE_CHECK(bytes && n > 0, "frc_argmax_workspace: bad arguments");
+  *bytes = 8 * (1 + 2 * 148 * 2);  // ticket + (value, index) per CTA, up to 296 CTAs
+  return FRC_OK;
+}
+
+int frc_argmax(const float* x, int64_t n, int* out_dev, void* workspace, void* stream) {
+  FRC_DECODE_CHECK(x && out_dev && workspace && n > 0, "frc_argmax: null pointer or empty input");
+  int64_t grid = (n + 4 * frc::kArgmaxThreads - 1) / (4 * frc::kArgmaxThreads);
+  if (grid > 296) grid = 296;
+  frc::argmax_kernel<<<static_cast<unsigned>(grid), frc::kArgmaxThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, n, out_dev, static_cast<int64_t*>(workspace));
   FRC_DECODE_LAUNCHED("argmax launch");
 }
 

@@ -659,7 +659,8 @@ int frc_gemv_noalloc(int quant, const void* w_dev, size_t w_bytes, int64_t n, in
 }
 
 int frc_gemv_ex(int quant, int count, const void* const* w_dev, const size_t* w_bytes, const int64_t* n, int64_t k,
-                const float* x_dev, const float* x_mul_dev, int flags, float* const* y_dev, void* stream) {
+                const float* x_dev, const float* x_mul_dev, const float* x_norm_w, float x_norm_eps, int flags,
+                float* const* y_dev, void* stream) {
   if (count < 1 || count > 4) return fail(FRC_ERR_INVALID, "frc_gemv_ex: count must be 1..4 (got %d)", count);
   if (!w_dev || !w_bytes || !n || !y_dev) return fail(FRC_ERR_INVALID, "null array");
   if (flags & ~FRC_GEMV_ACCUMULATE) return fail(FRC_ERR_INVALID, "frc_gemv_ex: unknown flags 0x%x", flags);
@@ -672,8 +673,9 @@ int frc_gemv_ex(int quant, int count, const void* const* w_dev, const size_t* w_
     if (!aligned(y_dev[m], 4)) return fail(FRC_ERR_INVALID, "frc_gemv_ex: y %d must be 4-byte aligned", m);
     total += n[m];
   }
-  if ((k && !x_dev) || !aligned(x_dev, 16) || !aligned(x_mul_dev, 16))
-    return fail(FRC_ERR_INVALID, "frc_gemv_ex: x and x_mul must be 16-byte aligned");
+  if ((k && !x_dev) || !aligned(x_dev, 16) || !aligned(x_mul_dev, 16) || !aligned(x_norm_w, 16))
+    return fail(FRC_ERR_INVALID, "frc_gemv_ex: x, x_mul and x_norm_w must be 16-byte aligned");
+  if (x_mul_dev && x_norm_w) return fail(FRC_ERR_INVALID, "frc_gemv_ex: x_mul and x_norm_w are exclusive");
   if (k == 0 || total == 0) return fail(FRC_ERR_UNSUPPORTED, "frc_gemv_ex: empty shapes");
   DeviceState* ds;
   int rc = current_device_state(&ds);
@@ -696,6 +698,8 @@ int frc_gemv_ex(int quant, int count, const void* const* w_dev, const size_t* w_
   r.y = r.mat_y[0];
   r.n = count == 1 ? n[0] : total;
   r.x_mul = x_mul_dev;
+  r.x_norm_w = x_norm_w;
+  r.x_norm_eps = x_norm_eps;
   r.y_accum = (flags & FRC_GEMV_ACCUMULATE) ? 1 : 0;
   rc = launch_gemv_quant(quant, r);
   if (rc == FRC_OK) return FRC_OK;

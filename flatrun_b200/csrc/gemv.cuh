@@ -78,6 +78,11 @@ struct GemvParams {
   // y_accum adds to y instead of storing (a residual stream)
   const float* x_mul;
   int y_accum;
+  // gemv_b1 with fp32 activations: x_norm_w != null reads the activations
+  // as RMSNorm(x) * x_norm_w (eps x_norm_eps), the norm of the whole row of x
+  // formed inside every slot
+  const float* x_norm_w;
+  float x_norm_eps;
 };
 
 constexpr int kMaxMats = 4;
@@ -290,12 +295,12 @@ FRC_DEVICE_INLINE void griddep_launch_dependents() { asm volatile("griddepcontro
 
 // Stores one y value locally and, with a fused all-gather, into every rank's
 // gathered buffer.
-FRC_DEVICE_INLINE void put_y(const GemvParams& p, float* dst, float v) {
+FRC_DEVICE_INLINE void put_y(const GemvParams& p, int g_world, float* dst, float v) {
   if (p.y_accum) v += *dst;
   *dst = v;
-  if (p.g_world > 1) {
+  if (g_world > 1) {
     const int64_t off = dst - p.g_ybase;
-    for (int r = 0; r < p.g_world; ++r) p.g_peer_y[r][off] = v;
+    for (int r = 0; r < g_world; ++r) p.g_peer_y[r][off] = v;
   }
 }
 
@@ -311,8 +316,8 @@ FRC_DEVICE_INLINE void st_relaxed_sys(uint32_t* ptr, uint32_t v) {
 // publishes the next epoch to every rank after one system-scope fence
 // (fences are cumulative, so it covers every slot's stores, remote ones
 // included).
-FRC_DEVICE_INLINE void gather_arrive(const GemvParams& p, int slots) {
-  if (p.g_world <= 1) return;
+FRC_DEVICE_INLINE void gather_arrive(const GemvParams& p, int g_world, int slots) {
+  if (g_world <= 1) return;
   __threadfence();
   const uint32_t total = gridDim.x * static_cast<uint32_t>(slots);
   if (atomicAdd(p.g_done, 1u) + 1u == total) {
@@ -389,6 +394,10 @@ __global__ void __launch_bounds__(b1_max_warps<Q, UPT, F32>() * 32, 1) gemv_b1(G
   }
   griddep_wait();
   griddep_launch_dependents();
+  // ranks this launch's outputs go to: after a gather wait that ran out, a
+  // peer may still be reading its buffer, so this launch stores locally only
+  // and publishes nothing (the status bit tells the caller the step is void)
+  int g_world = p.g_world;
   if (p.w_world > 1) {  // an earlier fused gather must be complete on every rank
     if (threadIdx.x < static_cast<unsigned>(p.w_world)) {
       const uint32_t e = *p.w_epoch;
@@ -399,11 +408,18 @@ __global__ void __launch_bounds__(b1_max_warps<Q, UPT, F32>() * 32, 1) gemv_b1(G
         if (static_cast<int32_t>(v - e) >= 0) break;
         if (global_ns() - t0 > kWaitLimitNs) {
           atomicOr(p.status, kStatusGatherTimeout);
+          *abort_flag = 2;  // read below; the tile loop only tests for nonzero after this point
           break;
         }
       }
     }
     __syncthreads();
+    if (*abort_flag == 2) {
+      g_world = 1;
+      __syncthreads();  // every thread has read the flag
+      if (threadIdx.x == 0) *abort_flag = 0;
+      __syncthreads();
+    }
   }
 
   UnitCtx cx[UPT];
@@ -444,12 +460,34 @@ __global__ void __launch_bounds__(b1_max_warps<Q, UPT, F32>() * 32, 1) gemv_b1(G
   }
   if constexpr (!F32) __syncthreads();  // the records are complete
   if (ntiles == 0) {  // the whole slot leaves together
-    if (st == leader) gather_arrive(p, slots);
+    if (st == leader) gather_arrive(p, g_world, slots);
     return;
   }
   if constexpr (F32) {
 #pragma unroll
     for (int i = 0; i < UPT; ++i) xu[i].finish();
+    if (p.x_norm_w) {
+      // the slot's threads hold every unit of x once: reduce the sum of
+      // squares over the slot (the second half of the slot's reduction
+      // buffer is first written after the first tile's barrier)
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < UPT; ++i) ss += xu[i].sum_squares();
+      ss = warp_sum(ss);
+      if (p.wps > 1) {
+        float* rb = red + p.wps * RPS;
+        if (lane == 0) rb[warp - slot * p.wps] = ss;
+        named_barrier_sync(1 + slot, spt);
+        ss = 0.f;
+        for (int w = 0; w < p.wps; ++w) ss += rb[w];
+      }
+      const float inv = 1.0f / sqrtf(ss / static_cast<float>(p.k) + p.x_norm_eps);
+#pragma unroll
+      for (int i = 0; i < UPT; ++i)
+        if (uval[i]) xu[i].normalise(inv, p.x_norm_w);
+    }
+#pragma unroll
+    for (int i = 0; i < UPT; ++i) xu[i].sums();
   } else {
 #pragma unroll
     for (int i = 0; i < UPT; ++i) {
@@ -478,18 +516,31 @@ __global__ void __launch_bounds__(b1_max_warps<Q, UPT, F32>() * 32, 1) gemv_b1(G
       // offset modulo 16 (only the low bits of the product matter)
       const uint32_t base = stages_s + static_cast<uint32_t>(s) * static_cast<uint32_t>(p.stage_stride) +
                             ((static_cast<uint32_t>(tile.local) * static_cast<uint32_t>(p.row_bytes)) & 15u);
-      // Every thread runs every row of the tile with no branch: a thread
-      // without a unit (its row's units do not fill the slot's last warp)
-      // reads unit 0's bytes with zero activations, and the rows past a
-      // short tile read whatever the stage held before (always inside the
-      // stage); the selects drop both.  The rows' independent instruction
-      // streams can then be interleaved.
+      // A thread without a unit (its row's units do not fill the slot's last
+      // warp) runs the same instructions on unit 0's bytes with zero
+      // activations, and a select drops the result: no divergent branch.
+      // A short tile (its row count is uniform across the slot) stops at
+      // its last row; a full one has no per-row test, so the rows'
+      // independent instruction streams can be interleaved.
+      if (rows == RPS) {
 #pragma unroll
-      for (int i = 0; i < UPT; ++i) {
+        for (int i = 0; i < UPT; ++i) {
+#pragma unroll
+          for (int r = 0; r < RPS; ++r) {
+            const float v = unit_dot<Q, F32>(base + static_cast<uint32_t>(r * p.row_bytes), cx[i], xu[i]);
+            acc[r] += uval[i] ? v : 0.0f;
+          }
+        }
+      } else {
 #pragma unroll
         for (int r = 0; r < RPS; ++r) {
-          const float v = unit_dot<Q, F32>(base + static_cast<uint32_t>(r * p.row_bytes), cx[i], xu[i]);
-          acc[r] += (uval[i] && r < rows) ? v : 0.0f;
+          if (r < rows) {
+#pragma unroll
+            for (int i = 0; i < UPT; ++i) {
+              const float v = unit_dot<Q, F32>(base + static_cast<uint32_t>(r * p.row_bytes), cx[i], xu[i]);
+              acc[r] += uval[i] ? v : 0.0f;
+            }
+          }
         }
       }
     } else if (st == 0) {
@@ -523,10 +574,10 @@ __global__ void __launch_bounds__(b1_max_warps<Q, UPT, F32>() * 32, 1) gemv_b1(G
     }
     if (p.wps == 1) {
       if ((lane & (kLanesPerValue - 1)) == 0 && lane / kLanesPerValue < rows && !*abort) {
-        put_y(p, ym + lane / kLanesPerValue, acc[0]);
+        put_y(p, g_world, ym + lane / kLanesPerValue, acc[0]);
       }
     } else if (st < rows && !*abort) {
-      put_y(p, ym + st, acc[0]);
+      put_y(p, g_world, ym + st, acc[0]);
     }
     t0 = tile.t1;
     if (++s == nst) {
@@ -534,7 +585,7 @@ __global__ void __launch_bounds__(b1_max_warps<Q, UPT, F32>() * 32, 1) gemv_b1(G
       ph ^= 1u;
     }
   }
-  if (p.g_world > 1) {  // publish this slot's gathered rows
+  if (g_world > 1) {  // publish this slot's gathered rows
     // the leader's system fence after the slot barrier orders every thread's
     // stores of the slot before the arrival (fences are cumulative)
     if (p.wps == 1) {
@@ -542,7 +593,7 @@ __global__ void __launch_bounds__(b1_max_warps<Q, UPT, F32>() * 32, 1) gemv_b1(G
     } else {
       named_barrier_sync(1 + slot, spt);
     }
-    if (st == leader) gather_arrive(p, slots);
+    if (st == leader) gather_arrive(p, g_world, slots);
   }
 
   // on an abort, copies already issued must land before the CTA exits

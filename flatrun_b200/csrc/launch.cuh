@@ -56,6 +56,8 @@ struct GemvRequest {
   // batch-1, fp32 activations: x read as silu(x) * x_mul; y accumulated
   const float* x_mul;
   int y_accum;
+  const float* x_norm_w;  // batch-1, fp32 activations: x read as RMSNorm(x) * x_norm_w
+  float x_norm_eps;
 };
 
 struct DequantRequest {
@@ -669,10 +671,12 @@ cudaError_t launch_gemv(const GemvRequest& r) {
     p.w_epoch = r.w_epoch;
   }
   const bool exact_batched = opt(options().batched_fp32) != 0;
-  if ((r.x_mul || r.y_accum) && (r.batch != 1 || r.g_world > 1 || opt(options().batch1_int16)))
+  if ((r.x_mul || r.y_accum || r.x_norm_w) && (r.batch != 1 || r.g_world > 1 || opt(options().batch1_int16)))
     return cudaErrorNotSupported;  // only the batch-1 fp32-activation kernel has them
   p.x_mul = r.x_mul;
   p.y_accum = r.y_accum;
+  p.x_norm_w = r.x_norm_w;
+  p.x_norm_eps = r.x_norm_eps;
   if (r.batch == 1) {
     GemvParams b1 = p;
     b1.units = (r.k / F::QK) * I8<Q>::UPB;
@@ -683,7 +687,8 @@ cudaError_t launch_gemv(const GemvRequest& r) {
     // a row longer than one CTA's threads cover: the column-reusing kernel
     // (fp32 activations), without the fused multi-matrix, gather, SwiGLU or
     // accumulating forms
-    if (r.nmat > 1 || r.g_world > 1 || r.w_world > 1 || r.x_mul || r.y_accum) return cudaErrorNotSupported;
+    if (r.nmat > 1 || r.g_world > 1 || r.w_world > 1 || r.x_mul || r.y_accum || r.x_norm_w)
+      return cudaErrorNotSupported;
     return launch_xb<Q, 4>(p, r);
   }
   // the fused multi-matrix launch and the fused all-gather exist only in the

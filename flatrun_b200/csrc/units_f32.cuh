@@ -37,10 +37,11 @@ struct UnitXF {
   float xs[NG];
   const float* mul_ = nullptr;  // silu(x) * mul activations (see load)
   int j_ = 0;
+  int64_t b_ = 0;
 
   // Unit j of block b.  Every 16 consecutive unit elements are 16 consecutive
   // elements of x, so the unit loads as E/4 float4s, all issued before any
-  // is used; finish() then forms the group sums.  With `mul` the
+  // is used; finish() applies the SwiGLU and sums() forms the group sums.  With `mul` the
   // activations are silu(x) * mul, formed in finish() as the reference does
   // (s = 1 / (1 + exp(-gate)); s * gate * up, qwen2.py:1690-1751).
   FRC_DEVICE_INLINE void load(const float* xg, const float* mul, int64_t b, int j) {
@@ -59,7 +60,35 @@ struct UnitXF {
     }
     mul_ = mul ? mul + b * Fmt<Q>::QK : nullptr;
     j_ = j;
+    b_ = b;
   }
+  // The unit's elements of a vector laid out like x (weights of an RMSNorm).
+  FRC_DEVICE_INLINE float4 like_x(const float* v, int r, int q) const {
+    return __ldg(reinterpret_cast<const float4*>(v + b_ * Fmt<Q>::QK + i8_pos<Q>(j_, 16 * r)) + q);
+  }
+  FRC_DEVICE_INLINE float sum_squares() const {
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; e += 2) {
+      s0 = fmaf(x[e], x[e], s0);
+      s1 = fmaf(x[e + 1], x[e + 1], s1);
+    }
+    return s0 + s1;
+  }
+  // x <- (x * inv) * w: the RMSNorm of the reference (qwen2.py:365-378).
+  FRC_DEVICE_INLINE void normalise(float inv, const float* w) {
+#pragma unroll
+    for (int r = 0; r < E / 16; ++r) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 g = like_x(w, r, q);
+        const float gs[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x[16 * r + 4 * q + e] = (x[16 * r + 4 * q + e] * inv) * gs[e];
+      }
+    }
+  }
+  // silu(x) * mul when the unit was loaded with `mul`.
   FRC_DEVICE_INLINE void finish() {
     if (mul_) {
 #pragma unroll
@@ -78,6 +107,9 @@ struct UnitXF {
         }
       }
     }
+  }
+  // The group sums (after any transform of x).
+  FRC_DEVICE_INLINE void sums() {
 #pragma unroll
     for (int g = 0; g < NG; ++g) {
       float s0 = 0.f, s1 = 0.f;

@@ -7,15 +7,14 @@ device memory):
 
   embedding row                       frc_embed_row
   per layer:
-    RMSNorm                           frc_rmsnorm
-    q, k, v projections               frc_gemv_ex (one launch per quant group)
+    RMSNorm + q, k, v projections     frc_gemv_ex (norm inside the launch;
+                                      one launch per quant group)
     bias + RoPE + KV append           frc_rope_append
     GQA attention over the cache      frc_attention_decode (split positions)
     o projection + residual           frc_gemv_ex, FRC_GEMV_ACCUMULATE
-    RMSNorm                           frc_rmsnorm
-    gate + up projections             frc_gemv_ex (one fused launch)
+    RMSNorm + gate, up projections    frc_gemv_ex (one fused launch)
     SwiGLU + down + residual          frc_gemv_ex: x = silu(gate) * up, accumulate
-  final RMSNorm, lm_head, argmax      frc_rmsnorm, frc_gemv_ex, frc_argmax
+  final RMSNorm + lm_head, argmax     frc_gemv_ex, frc_argmax
 
 This is the reference forwarder's decode step (flatrun/model/qwen2.py
 ``make_qwen2_forwarder``: :1510-1646 attention, :1648-1751 MLP, :2238-2297
@@ -129,22 +128,26 @@ class DecodeEngine:
         self.gate = torch.zeros(c.ffn, dtype=f32, device=self._dev)
         self.upb = torch.zeros(c.ffn, dtype=f32, device=self._dev)
         self.logits = torch.zeros(c.vocab, dtype=f32, device=self._dev)
-        sm = torch.cuda.get_device_properties(self._dev).multi_processor_count
-        self.splits = attn_splits or max(1, sm // c.kv_heads)
+        # about 32 cached positions per attention CTA at the longest context:
+        # each of its four warps then keeps eight K (or V) rows in flight
+        self.splits = attn_splits or max(1, min(1024, -(-c.max_pos // 32)))
         ws = ctypes.c_size_t()
         _lib.check(self.lib.frc_attention_workspace(c.heads, hd, self.splits, ctypes.byref(ws)), self.lib)
         self.part = torch.zeros(int(ws.value), dtype=f32, device=self._dev)
+        _lib.check(self.lib.frc_argmax_workspace(c.vocab, ctypes.byref(ws)), self.lib)
+        self.argmax_ws = torch.zeros(int(ws.value), dtype=torch.uint8, device=self._dev)
         self._graph = None
         self.launches_per_token = 0
 
     # ---- launches ------------------------------------------------------------
-    def _gemv(self, names, x, ys, x_mul=None, accumulate=False):
+    def _gemv(self, names, x, ys, x_mul=None, norm=None, accumulate=False):
         ws = [self._w[nm] for nm in names]
         cnt = len(ws)
         rc = self.lib.frc_gemv_ex(ws[0][1], cnt, (ctypes.c_void_p * cnt)(*[w[0].data_ptr() for w in ws]),
                                   (ctypes.c_size_t * cnt)(*[w[0].numel() for w in ws]),
                                   (ctypes.c_int64 * cnt)(*[w[2] for w in ws]), ws[0][3], x.data_ptr(),
                                   x_mul.data_ptr() if x_mul is not None else None,
+                                  norm.data_ptr() if norm is not None else None, self.cfg.eps,
                                   _lib.FRC_GEMV_ACCUMULATE if accumulate else 0,
                                   (ctypes.c_void_p * cnt)(*[y.data_ptr() for y in ys]), self._st)
         _lib.check(rc, self.lib)
@@ -179,10 +182,9 @@ class DecodeEngine:
         scale = float(np.float32(1.0 / np.sqrt(hd)))
         for i in range(c.layers):
             p = f"model.layers.{i}"
-            chk(lib.frc_rmsnorm(self.h.data_ptr(), self._norm[f"{p}.input_layernorm.weight"].data_ptr(), 1,
-                                c.hidden, c.eps, self.x.data_ptr(), st))
+            ln1 = self._norm[f"{p}.input_layernorm.weight"]
             for grp in self._groups([f"{p}.{nm}.weight" for nm in _PROJ[:3]]):
-                self._gemv(grp, self.x, [outs[g[len(p) + 1:-len(".weight")]] for g in grp])
+                self._gemv(grp, self.h, [outs[g[len(p) + 1:-len(".weight")]] for g in grp], norm=ln1)
             bias = self._bias.get(i)
             chk(lib.frc_rope_append(self.qkv.data_ptr(), bias.data_ptr() if bias is not None else None, c.heads,
                                     c.kv_heads, hd, self._cos.data_ptr(), self._sin.data_ptr(), self.pos.data_ptr(),
@@ -191,16 +193,14 @@ class DecodeEngine:
                                          self.pos.data_ptr(), c.heads, c.kv_heads, hd, scale, self.splits,
                                          self.part.data_ptr(), self.ctx.data_ptr(), st), kernels=2)
             self._gemv([f"{p}.self_attn.o_proj.weight"], self.ctx, [self.h], accumulate=True)
-            chk(lib.frc_rmsnorm(self.h.data_ptr(), self._norm[f"{p}.post_attention_layernorm.weight"].data_ptr(), 1,
-                                c.hidden, c.eps, self.x.data_ptr(), st))
+            ln2 = self._norm[f"{p}.post_attention_layernorm.weight"]
             gu = [f"{p}.mlp.gate_proj.weight", f"{p}.mlp.up_proj.weight"]
             for grp in self._groups(gu):
-                self._gemv(grp, self.x, [self.gate if g.endswith("gate_proj.weight") else self.upb for g in grp])
+                self._gemv(grp, self.h, [self.gate if g.endswith("gate_proj.weight") else self.upb for g in grp],
+                           norm=ln2)
             self._gemv([f"{p}.mlp.down_proj.weight"], self.gate, [self.h], x_mul=self.upb, accumulate=True)
-        chk(lib.frc_rmsnorm(self.h.data_ptr(), self._norm["model.norm.weight"].data_ptr(), 1, c.hidden, c.eps,
-                            self.x.data_ptr(), st))
-        self._gemv(["lm_head.weight"], self.x, [self.logits])
-        chk(lib.frc_argmax(self.logits.data_ptr(), c.vocab, self.tok_out.data_ptr(), st))
+        self._gemv(["lm_head.weight"], self.h, [self.logits], norm=self._norm["model.norm.weight"])
+        chk(lib.frc_argmax(self.logits.data_ptr(), c.vocab, self.tok_out.data_ptr(), self.argmax_ws.data_ptr(), st))
         chk(lib.frc_pos_advance(self.pos.data_ptr(), st))
         # the greedy pick is the next token's input unless step() overrides it
         self.tok_in.copy_(self.tok_out)

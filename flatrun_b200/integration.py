@@ -25,15 +25,19 @@ from __future__ import annotations
 
 from typing import Any
 
-from .backend import CudaBackend
+from .backend import CudaBackend, devices_from_env
 
 
 def _make_classes(rb):
     class CudaSlotBackend(rb.BackendBase):
         """``BackendBase`` implementation over :class:`CudaBackend`."""
 
-        def __init__(self, device: int = 0) -> None:
-            self._cuda = CudaBackend(device)
+        def __init__(self, device: int | None = None) -> None:
+            # the reference's get_backend(name) passes no arguments: the GPUs
+            # come from FLATRUN_CUDA_DEVICES (several ids: every projection's
+            # rows are split over them), else device 0
+            devs = [device] if device is not None else devices_from_env()
+            self._cuda = CudaBackend(devs[0], devices=devs)
 
         @property
         def name(self) -> str:

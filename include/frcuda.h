@@ -161,14 +161,18 @@ int frc_gemv_multi(int quant, int count, const void* const* w_dev, const size_t*
  *  - x_mul_dev != NULL: the activations are silu(x) * x_mul elementwise,
  *    silu(g) = g / (1 + exp(-g)) evaluated as (1 / (1 + exp(-g))) * g, so a
  *    gate and an up projection feed the down projection with no SwiGLU pass;
+ *  - x_norm_w != NULL: the activations are RMSNorm(x) * x_norm_w,
+ *    x * (1 / sqrt(mean(x^2) + x_norm_eps)) * w (qwen2.py:365-378), the mean
+ *    taken over the whole row inside the launch, so no separate norm pass
+ *    (exclusive with x_mul);
  *  - flags & FRC_GEMV_ACCUMULATE: y += W x instead of y = W x (a residual
  *    stream).
  * FRC_ERR_UNSUPPORTED when the batch-1 int16 option is set or the row is
  * too long for one CTA. */
 #define FRC_GEMV_ACCUMULATE 1
 int frc_gemv_ex(int quant, int count, const void* const* w_dev, const size_t* w_bytes, const int64_t* n,
-                int64_t k, const float* x_dev, const float* x_mul_dev, int flags, float* const* y_dev,
-                void* stream);
+                int64_t k, const float* x_dev, const float* x_mul_dev, const float* x_norm_w, float x_norm_eps,
+                int flags, float* const* y_dev, void* stream);
 
 /* ---- device-resident decoder step ----------------------------------------- *
  * The operators of a Qwen2/Llama decode token around the projections, so a
@@ -188,9 +192,11 @@ int frc_gemv_ex(int quant, int count, const void* const* w_dev, const size_t* w_
  *    0..*pos_dev: softmax(q.k * scale) . v per head, query head h reading KV
  *    head h / (nh/nkv); positions split into `splits` ranges (flash
  *    decoding) whose partials (frc_attention_workspace floats in `part`) are
- *    merged into out (nh*hd).  hd <= 128 and a multiple of 4, nh/nkv <= 16.
+ *    merged into out (nh*hd).  hd 64 or 128, nh/nkv <= 8, splits <= 1024.
  *  frc_argmax: index of the largest of n floats into *out_dev (the lowest
- *    index among ties, as np.argmax).
+ *    index among ties, as np.argmax); `workspace` holds
+ *    frc_argmax_workspace bytes, zeroed before the first call (the kernel
+ *    leaves it ready for the next).
  *  frc_embed_row: row *tok_dev of a (vocab, n) table into out: quant 0 for
  *    fp32 rows, or a GGUF quant id (dequantised bit-exactly). */
 int frc_rmsnorm(const float* x, const float* w, int64_t rows, int64_t n, float eps, float* out, void* stream);
@@ -199,7 +205,8 @@ int frc_rope_append(float* qkv, const float* bias, int nh, int nkv, int hd, cons
 int frc_attention_workspace(int nh, int hd, int splits, size_t* floats);
 int frc_attention_decode(const float* q, const float* k_cache, const float* v_cache, const int* pos_dev, int nh,
                          int nkv, int hd, float scale, int splits, float* part, float* out, void* stream);
-int frc_argmax(const float* x, int64_t n, int* out_dev, void* stream);
+int frc_argmax_workspace(int64_t n, size_t* bytes);
+int frc_argmax(const float* x, int64_t n, int* out_dev, void* workspace, void* stream);
 int frc_embed_row(int quant, const void* table, int64_t n, const int* tok_dev, float* out, void* stream);
 int frc_pos_advance(int* pos_dev, void* stream);
 

@@ -441,3 +441,30 @@ def test_no_device_status_raised(cuda_backend):
     flags = ctypes.c_uint32(123)
     _lib.check(lib.frc_device_status(0, ctypes.byref(flags)), lib)
     assert flags.value == 0
+
+
+@pytest.mark.parametrize("devices", [[0, 0], [0, 0, 0, 0], "all"])
+@pytest.mark.parametrize("batch", [1, 3])
+def test_row_sharded_backend_matches_one_device(cuda_backend, devices, batch):
+    """CudaBackend(devices=...) splits every projection's rows over GPUs in
+    one process (the reference API's route to several GPUs, e.g.
+    FLATRUN_CUDA_DEVICES=0,1,2,3): each row is computed by the same kernel
+    arithmetic as on one device, so y is bit-identical.  Shards on one GPU
+    check the split and assembly; "all" uses every visible GPU (skipped with
+    one)."""
+    from flatrun_b200 import CudaBackend
+    if devices == "all":
+        if _lib.device_count() < 2:
+            pytest.skip("one GPU visible")
+        devices = list(range(_lib.device_count()))
+    fmt, n, k = "Q4_K", 1000, 3584
+    raw = synth.make_weight(fmt, n, k, seed=81)
+    x = synth.make_x(k, batch=None if batch == 1 else batch, seed=82)
+    ref = cuda_backend.matmul_q4k(x, raw, n, k)
+    sb = CudaBackend(devices=devices)
+    y = sb.matmul_q4k(x, raw, n, k)
+    assert y.shape == ref.shape
+    assert O.same_bits(y, ref)
+    assert O.same_bits(sb.dequant_q4k(raw, (n, k)), O.dequant(fmt, raw, n, k))
+    sb.close()
+    cuda_backend.close()

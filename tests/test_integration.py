@@ -183,3 +183,36 @@ def test_reference_forwarder_routes_projections_to_adapter(rb):
     assert ("matmul_q6k", KVD, H) in seen and ("matmul_q4k", KVD, H) in seen
     # prefill calls carry the whole (seq, k) activation, decode calls one row
     assert any(shape == (6, H) for _, shape, _, _ in calls) and any(shape == (1, H) for _, shape, _, _ in calls)
+
+
+def test_cli_launcher_accepts_backend_cuda(rb):
+    """`python -m flatrun_b200.cli run ... --backend cuda` reaches the
+    reference CLI with the choice accepted (its --help lists it), and
+    get_backend("cuda") then builds the adapter the forwarder dispatches to."""
+    import subprocess
+
+    env = dict(os.environ, PYTHONPATH=os.pathsep.join([REF_SRC, REPO, os.environ.get("PYTHONPATH", "")]))
+    for sub in ("run", "chat", "serve"):
+        r = subprocess.run([sys.executable, "-m", "flatrun_b200.cli", sub, "--help"], capture_output=True, text=True,
+                           env=env, timeout=120)
+        assert r.returncode == 0, r.stderr[-1000:]
+        assert "cuda" in r.stdout.split("--backend", 1)[1][:80]
+    from flatrun_b200 import cli, integration
+    adapter = cli.install(rb)
+    b = rb.get_backend("cuda")
+    assert isinstance(b, adapter) and b.name == "native"
+    integration.register(rb)  # restore the plain registry entry for the other tests
+
+
+def test_cli_choice_patch_is_scoped():
+    import argparse
+
+    from flatrun_b200.cli import backend_choice_added
+    with backend_choice_added("cuda"):
+        p = argparse.ArgumentParser()
+        p.add_argument("--backend", choices=["python", "native"])
+        assert p.parse_args(["--backend", "cuda"]).backend == "cuda"
+    p = argparse.ArgumentParser()
+    p.add_argument("--backend", choices=["python", "native"])
+    with pytest.raises(SystemExit):
+        p.parse_args(["--backend", "cuda"])
