@@ -23,11 +23,21 @@
 
 namespace frc {
 
+// Programmatic dependent launch: every kernel here waits for the previous
+// kernel of the stream before touching memory, and lets the next one launch
+// at once (its own wait keeps it ordered after this kernel's end), so the
+// next GEMV can stream its first weight tiles while this kernel runs.
+FRC_DEVICE_INLINE void pdl_enter() {
+  griddep_wait();
+  griddep_launch_dependents();
+}
+
 // ---------------------------------------------------------------------------
 // RMSNorm of `rows` rows of n fp32 values: one CTA per row.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                       int n, float eps, float* __restrict__ out) {
+  pdl_enter();
   const float* xr = x + static_cast<int64_t>(blockIdx.x) * n;
   float* yr = out + static_cast<int64_t>(blockIdx.x) * n;
   float s = 0.f;
@@ -57,6 +67,7 @@ __global__ void rope_append_kernel(float* __restrict__ qkv, const float* __restr
                                    const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                    const int* __restrict__ pos_ptr, float* __restrict__ k_cache,
                                    float* __restrict__ v_cache) {
+  pdl_enter();
   const int pos = *pos_ptr;
   const int half = hd / 2;
   const int nq_pairs = nh * half, nk_pairs = nkv * half, nv = nkv * hd;
@@ -99,15 +110,15 @@ __global__ void rope_append_kernel(float* __restrict__ qkv, const float* __restr
 // that read that KV head (GQA: query head h reads KV head h / G).  Head dim
 // HD (64 or 128): lane l of a warp owns dimensions VEC*l.. (VEC = HD / 32),
 // so every K or V row is one coalesced warp load.  Per chunk of positions:
-//   scores: warp w takes positions w, w+4, ...; the lanes' partial dots of
+//   scores: warp w takes positions w, w+8, ...; the lanes' partial dots of
 //     the G heads are summed with one butterfly (G <= 8 values, 9 shuffles);
 //   softmax: per head, the chunk's max and sum of exp(score - max);
 //   A.V: warp w accumulates exp(score - max) * V over its positions, then
 //     merges into its running (max, sum, acc) per head.
-// The four warps' accumulators are added at the end; the range's partial
+// The eight warps' accumulators are added at the end; the range's partial
 // (max, sum, acc[G][128]) goes to `part` for attn_combine.
 // ---------------------------------------------------------------------------
-constexpr int kAttnThreads = 128;
+constexpr int kAttnThreads = 256;
 constexpr int kAttnMaxHd = 128;
 constexpr int kAttnMaxG = 8;
 constexpr int kAttnChunk = 256;  // positions per pass of a range
@@ -129,6 +140,7 @@ template <int HD>
 __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(
     const float* __restrict__ q, const float* __restrict__ k_cache, const float* __restrict__ v_cache,
     const int* __restrict__ pos_ptr, int nh, int nkv, float scale, int splits, float* __restrict__ part) {
+  pdl_enter();
   constexpr int MG = kAttnMaxG, NW = kAttnThreads / 32, VEC = HD / 32;
   const int g = blockIdx.x, c = blockIdx.y;
   const int G = nh / nkv;
@@ -160,18 +172,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(
   const float* vb = v_cache + static_cast<int64_t>(g) * HD + VEC * lane;
   for (int base = t0; base < t1; base += kAttnChunk) {
     const int n_t = min(kAttnChunk, t1 - base);
-    // scores: each warp takes four positions per pass so that four row loads
-    // are in flight at once
-    for (int t = warp; t < n_t; t += 4 * NW) {
-      float kr[4][VEC];
+    // scores: each warp takes eight positions per pass so that eight row
+    // loads are in flight at once
+    for (int t = warp; t < n_t; t += 8 * NW) {
+      float kr[8][VEC];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
 #pragma unroll
         for (int e = 0; e < VEC; ++e) kr[u][e] = 0.f;
         if (t + u * NW < n_t) load_vec<VEC>(kb + (base + t + u * NW) * row_stride, kr[u]);
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
         float sv[MG];
 #pragma unroll
         for (int h = 0; h < MG; ++h) {
@@ -210,16 +222,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(
     for (int h = 0; h < MG; ++h)
 #pragma unroll
       for (int e = 0; e < VEC; ++e) a[h][e] = 0.f;
-    for (int t = warp; t < n_t; t += 4 * NW) {
-      float vr[4][VEC];
+    for (int t = warp; t < n_t; t += 8 * NW) {
+      float vr[8][VEC];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
 #pragma unroll
         for (int e = 0; e < VEC; ++e) vr[u][e] = 0.f;
         if (t + u * NW < n_t) load_vec<VEC>(vb + (base + t + u * NW) * row_stride, vr[u]);
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
         if (t + u * NW < n_t) {
           const float4 p0 = *reinterpret_cast<const float4*>(&sc[t + u * NW][0]);
           const float4 p1 = *reinterpret_cast<const float4*>(&sc[t + u * NW][4]);
@@ -271,29 +283,34 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(
 // (max, sum) pairs are read in parallel first.
 constexpr int kAttnMaxSplits = 1024;
 
-__global__ void __launch_bounds__(kAttnMaxHd) attn_combine_kernel(const float* __restrict__ part, int hd, int splits,
-                                                                 float* __restrict__ out) {
-  const int h = blockIdx.x, d = threadIdx.x;  // blockDim.x = hd
-  const int nw = (blockDim.x + 31) >> 5;
+constexpr int kCombineGroups = 8;  // threads per output element: split groups
+
+__global__ void __launch_bounds__(kAttnMaxHd * kCombineGroups) attn_combine_kernel(
+    const float* __restrict__ part, int hd, int splits, float* __restrict__ out) {
+  pdl_enter();
+  // blockDim = (hd, kCombineGroups): thread (d, j) sums the splits c = j mod G
+  const int h = blockIdx.x, d = threadIdx.x, j = threadIdx.y;
+  const int tid = j * blockDim.x + d, nthreads = blockDim.x * blockDim.y;
   const float* ph = part + static_cast<int64_t>(h) * splits * (hd + 2);
   __shared__ float em[kAttnMaxSplits];
-  __shared__ float red[kAttnMaxHd / 32];
+  __shared__ float red[32];
+  __shared__ float sums[kCombineGroups][kAttnMaxHd];
   __shared__ float bcast[2];
   float m = -FLT_MAX;
-  for (int c = d; c < splits; c += blockDim.x) m = fmaxf(m, ph[c * (hd + 2)]);
+  for (int c = tid; c < splits; c += nthreads) m = fmaxf(m, ph[c * (hd + 2)]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if ((d & 31) == 0) red[d >> 5] = m;
+  if ((tid & 31) == 0) red[tid >> 5] = m;
   __syncthreads();
-  if (d == 0) {
+  if (tid == 0) {
     float M = red[0];
-    for (int w = 1; w < nw; ++w) M = fmaxf(M, red[w]);
+    for (int w = 1; w < nthreads / 32; ++w) M = fmaxf(M, red[w]);
     bcast[0] = M;
   }
   __syncthreads();
   const float M = bcast[0];
   float L = 0.f;
-  for (int c = d; c < splits; c += blockDim.x) {
+  for (int c = tid; c < splits; c += nthreads) {
     const float* pc = ph + c * (hd + 2);
     const float e = pc[1] == 0.f ? 0.f : expf(pc[0] - M);  // an empty range contributes nothing
     em[c] = e;
@@ -301,22 +318,24 @@ __global__ void __launch_bounds__(kAttnMaxHd) attn_combine_kernel(const float* _
   }
   L = warp_sum(L);
   __syncthreads();
-  if ((d & 31) == 0) red[d >> 5] = L;
+  if ((tid & 31) == 0) red[tid >> 5] = L;
   __syncthreads();
-  if (d == 0) {
-    float s = 0.f;
-    for (int w = 0; w < nw; ++w) s += red[w];
-    bcast[1] = s;
+  if (tid == 0) {
+    float t = 0.f;
+    for (int w = 0; w < nthreads / 32; ++w) t += red[w];
+    bcast[1] = t;
   }
+  float A = 0.f;
+#pragma unroll 4
+  for (int c = j; c < splits; c += kCombineGroups) A = fmaf(ph[c * (hd + 2) + 2 + d], em[c], A);
+  sums[j][d] = A;
   __syncthreads();
-  float A0 = 0.f, A1 = 0.f;
-  int c = 0;
-  for (; c + 1 < splits; c += 2) {
-    A0 = fmaf(ph[c * (hd + 2) + 2 + d], em[c], A0);
-    A1 = fmaf(ph[(c + 1) * (hd + 2) + 2 + d], em[c + 1], A1);
+  if (j == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int g = 0; g < kCombineGroups; ++g) t += sums[g][d];
+    out[h * hd + d] = t / bcast[1];
   }
-  if (c < splits) A0 = fmaf(ph[c * (hd + 2) + 2 + d], em[c], A0);
-  out[h * hd + d] = (A0 + A1) / bcast[1];
 }
 
 // ---------------------------------------------------------------------------
@@ -357,6 +376,7 @@ constexpr int kArgmaxThreads = 256;
 
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ x, int64_t n,
                                                                int* __restrict__ out, int64_t* __restrict__ ws) {
+  pdl_enter();
   // ws: [0] ticket, [1 + 2b] value bits, [2 + 2b] index of CTA b
   const int64_t per = (n + gridDim.x - 1) / gridDim.x;
   const int64_t i0 = blockIdx.x * per, i1 = min(n, i0 + per);
@@ -393,6 +413,7 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __r
 // ---------------------------------------------------------------------------
 __global__ void embed_f32_kernel(const float* __restrict__ table, int n, const int* __restrict__ tok,
                                  float* __restrict__ out) {
+  pdl_enter();
   const float* row = table + static_cast<int64_t>(*tok) * n;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) out[i] = row[i];
 }
@@ -400,6 +421,7 @@ __global__ void embed_f32_kernel(const float* __restrict__ table, int n, const i
 template <int Q>
 __global__ void embed_q_kernel(const uint8_t* __restrict__ table, int n, const int* __restrict__ tok,
                                float* __restrict__ out) {
+  pdl_enter();
   using F = Fmt<Q>;
   const uint8_t* row = table + static_cast<int64_t>(*tok) * (n / F::QK) * F::TS;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
@@ -407,7 +429,25 @@ __global__ void embed_q_kernel(const uint8_t* __restrict__ table, int n, const i
 }
 
 // Increment the device position (one thread): the last launch of a token.
-__global__ void pos_advance_kernel(int* pos) { *pos += 1; }
+__global__ void pos_advance_kernel(int* pos) {
+  pdl_enter();
+  *pos += 1;
+}
+
+// Launch with the programmatic-stream-serialization attribute.
+template <typename... P, typename... A>
+cudaError_t launch_dep(void (*kernel)(P...), dim3 grid, dim3 block, cudaStream_t st, A... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<P>(args)...);
+}
 
 }  // namespace frc
 
@@ -445,8 +485,8 @@ int frc_rmsnorm(const float* x, const float* w, int64_t rows, int64_t n, float e
   FRC_DECODE_CHECK(rows >= 0 && n > 0 && n <= (int64_t(1) << 30), "frc_rmsnorm: bad shape");
   FRC_DECODE_CHECK(x && w && out, "frc_rmsnorm: null pointer");
   if (rows == 0) return FRC_OK;
-  frc::rmsnorm_kernel<<<static_cast<unsigned>(rows), 1024, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, w, static_cast<int>(n), eps, out);
+  frc::launch_dep(frc::rmsnorm_kernel, dim3(static_cast<unsigned>(rows)), dim3(1024), static_cast<cudaStream_t>(stream),
+                  x, w, static_cast<int>(n), eps, out);
   FRC_DECODE_LAUNCHED("rmsnorm launch");
 }
 
@@ -455,8 +495,8 @@ int frc_rope_append(float* qkv, const float* bias, int nh, int nkv, int hd, cons
   FRC_DECODE_CHECK(nh > 0 && nkv > 0 && nh % nkv == 0 && hd > 0 && hd % 2 == 0, "frc_rope_append: bad heads");
   FRC_DECODE_CHECK(qkv && cos_table && sin_table && pos_dev && k_cache && v_cache, "frc_rope_append: null pointer");
   const int threads = nh * hd / 2 + nkv * hd / 2 + nkv * hd;
-  frc::rope_append_kernel<<<(threads + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      qkv, bias, nh, nkv, hd, cos_table, sin_table, pos_dev, k_cache, v_cache);
+  frc::launch_dep(frc::rope_append_kernel, dim3((threads + 255) / 256), dim3(256), static_cast<cudaStream_t>(stream),
+                  qkv, bias, nh, nkv, hd, cos_table, sin_table, pos_dev, k_cache, v_cache);
   FRC_DECODE_LAUNCHED("rope_append launch");
 }
 
@@ -469,14 +509,14 @@ int frc_attention_decode(const float* q, const float* k_cache, const float* v_ca
   FRC_DECODE_CHECK(q && k_cache && v_cache && pos_dev && part && out, "frc_attention_decode: null pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (hd == 128)
-    frc::attn_partial_kernel<128><<<dim3(nkv, splits), frc::kAttnThreads, 0, st>>>(q, k_cache, v_cache, pos_dev, nh,
-                                                                                   nkv, scale, splits, part);
+    frc::launch_dep(frc::attn_partial_kernel<128>, dim3(nkv, splits), dim3(frc::kAttnThreads), st, q, k_cache, v_cache,
+                    pos_dev, nh, nkv, scale, splits, part);
   else
-    frc::attn_partial_kernel<64><<<dim3(nkv, splits), frc::kAttnThreads, 0, st>>>(q, k_cache, v_cache, pos_dev, nh,
-                                                                                  nkv, scale, splits, part);
+    frc::launch_dep(frc::attn_partial_kernel<64>, dim3(nkv, splits), dim3(frc::kAttnThreads), st, q, k_cache, v_cache,
+                    pos_dev, nh, nkv, scale, splits, part);
   int rc = launch_status("attention launch");
   if (rc) return frc__fail(rc, g_decode_err);
-  frc::attn_combine_kernel<<<nh, hd, 0, st>>>(part, hd, splits, out);
+  frc::launch_dep(frc::attn_combine_kernel, dim3(nh), dim3(hd, frc::kCombineGroups), st, part, hd, splits, out);
   FRC_DECODE_LAUNCHED("attention combine launch");
 }
 
@@ -496,8 +536,8 @@ int frc_argmax(const float* x, int64_t n, int* out_dev, void* workspace, void* s
   FRC_DECODE_CHECK(x && out_dev && workspace && n > 0, "frc_argmax: null pointer or empty input");
   int64_t grid = (n + 4 * frc::kArgmaxThreads - 1) / (4 * frc::kArgmaxThreads);
   if (grid > 296) grid = 296;
-  frc::argmax_kernel<<<static_cast<unsigned>(grid), frc::kArgmaxThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, n, out_dev, static_cast<int64_t*>(workspace));
+  frc::launch_dep(frc::argmax_kernel, dim3(static_cast<unsigned>(grid)), dim3(frc::kArgmaxThreads),
+                  static_cast<cudaStream_t>(stream), x, n, out_dev, static_cast<int64_t*>(workspace));
   FRC_DECODE_LAUNCHED("argmax launch");
 }
 
@@ -507,7 +547,10 @@ int frc_embed_row(int quant, const void* table, int64_t n, const int* tok_dev, f
   const unsigned blocks = static_cast<unsigned>((n + 255) / 256 < 64 ? (n + 255) / 256 : 64);
   const int in = static_cast<int>(n);
   switch (quant) {
-    case 0: frc::embed_f32_kernel<<<blocks, 256, 0, st>>>(static_cast<const float*>(table), in, tok_dev, out); break;
+    case 0:
+      frc::launch_dep(frc::embed_f32_kernel, dim3(blocks), dim3(256), st, static_cast<const float*>(table), in, tok_dev,
+                      out);
+      break;
     case FRC_Q8_0:
     case FRC_Q4_K:
     case FRC_Q5_K:
@@ -516,11 +559,11 @@ int frc_embed_row(int quant, const void* table, int64_t n, const int* tok_dev, f
       const int qk = quant == FRC_Q8_0 ? 32 : (quant == FRC_Q1_0 ? 128 : 256);
       FRC_DECODE_CHECK(n % qk == 0, "frc_embed_row: row length must be a multiple of the block size");
       const uint8_t* t = static_cast<const uint8_t*>(table);
-      if (quant == FRC_Q8_0) frc::embed_q_kernel<frc::kQ8_0><<<blocks, 256, 0, st>>>(t, in, tok_dev, out);
-      if (quant == FRC_Q4_K) frc::embed_q_kernel<frc::kQ4_K><<<blocks, 256, 0, st>>>(t, in, tok_dev, out);
-      if (quant == FRC_Q5_K) frc::embed_q_kernel<frc::kQ5_K><<<blocks, 256, 0, st>>>(t, in, tok_dev, out);
-      if (quant == FRC_Q6_K) frc::embed_q_kernel<frc::kQ6_K><<<blocks, 256, 0, st>>>(t, in, tok_dev, out);
-      if (quant == FRC_Q1_0) frc::embed_q_kernel<frc::kQ1_0><<<blocks, 256, 0, st>>>(t, in, tok_dev, out);
+      if (quant == FRC_Q8_0) frc::launch_dep(frc::embed_q_kernel<frc::kQ8_0>, dim3(blocks), dim3(256), st, t, in, tok_dev, out);
+      if (quant == FRC_Q4_K) frc::launch_dep(frc::embed_q_kernel<frc::kQ4_K>, dim3(blocks), dim3(256), st, t, in, tok_dev, out);
+      if (quant == FRC_Q5_K) frc::launch_dep(frc::embed_q_kernel<frc::kQ5_K>, dim3(blocks), dim3(256), st, t, in, tok_dev, out);
+      if (quant == FRC_Q6_K) frc::launch_dep(frc::embed_q_kernel<frc::kQ6_K>, dim3(blocks), dim3(256), st, t, in, tok_dev, out);
+      if (quant == FRC_Q1_0) frc::launch_dep(frc::embed_q_kernel<frc::kQ1_0>, dim3(blocks), dim3(256), st, t, in, tok_dev, out);
       break;
     }
     default: return frc__fail(FRC_ERR_INVALID, "frc_embed_row: quant must be 0 (fp32) or a supported GGUF type");
@@ -530,7 +573,7 @@ int frc_embed_row(int quant, const void* table, int64_t n, const int* tok_dev, f
 
 int frc_pos_advance(int* pos_dev, void* stream) {
   FRC_DECODE_CHECK(pos_dev, "frc_pos_advance: null pointer");
-  frc::pos_advance_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(pos_dev);
+  frc::launch_dep(frc::pos_advance_kernel, dim3(1), dim3(1), static_cast<cudaStream_t>(stream), pos_dev);
   FRC_DECODE_LAUNCHED("pos_advance launch");
 }
 

@@ -128,9 +128,10 @@ class DecodeEngine:
         self.gate = torch.zeros(c.ffn, dtype=f32, device=self._dev)
         self.upb = torch.zeros(c.ffn, dtype=f32, device=self._dev)
         self.logits = torch.zeros(c.vocab, dtype=f32, device=self._dev)
-        # about 32 cached positions per attention CTA at the longest context:
-        # each of its four warps then keeps eight K (or V) rows in flight
-        self.splits = attn_splits or max(1, min(1024, -(-c.max_pos // 32)))
+        # one attention CTA per SM and KV head: each of its eight warps keeps
+        # eight K (or V) rows in flight
+        sm = torch.cuda.get_device_properties(self._dev).multi_processor_count
+        self.splits = attn_splits or max(1, sm // c.kv_heads)
         ws = ctypes.c_size_t()
         _lib.check(self.lib.frc_attention_workspace(c.heads, hd, self.splits, ctypes.byref(ws)), self.lib)
         self.part = torch.zeros(int(ws.value), dtype=f32, device=self._dev)
