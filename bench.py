@@ -514,6 +514,8 @@ def main() -> None:
                     help="one launch per projection, each with its own x (no shared-x fusion)")
     ap.add_argument("--batch1-int16", action="store_true",
                     help="batch 1 on the 16-bit activation grid kernel (dp4a) instead of fp32 activations")
+    ap.add_argument("--cuda-core", action="store_true",
+                    help="batch-1 Q4_K on the CUDA-core fp32 kernel instead of the tensor-core one (same arithmetic)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -583,6 +585,8 @@ def main() -> None:
     lib = _lib.load()
     if args.batch1_int16:
         _lib.set_option("batch1_int16", 1)
+    if args.cuda_core:
+        _lib.set_option("batch1_tc", 0)
     be = CudaBackend(dev)
     if not be.available:
         raise RuntimeError(f"CUDA backend unavailable: {be._load_error}")
@@ -892,7 +896,14 @@ def main() -> None:
         # tensor-core GEMV (pre-pass + main), more: tcgen05 GEMM (fp16 pre-pass
         # + main)
         if batch == 1:
-            kname, dtype, calls_per_group = "gemv_b1 (fp32 activations)", "f32", lambda g: 1
+            dom_q, dom_k = next((mats[i][1], mats[i][3]) for g in lgroups for i in g
+                                if dom_name.startswith("+".join(mats[j][0] for j in g)))
+            if _lib.batch1_kernel(dom_q, dom_k) == "tensor_fp32":
+                kname = ("gemv_tc1 (fp32 activations: x as three exact fp16 terms, weights as exact fp16 "
+                         "q*sc, products on the tensor cores (mma.sync), fp32 accumulation)")
+            else:
+                kname = "gemv_b1 (fp32 activations, fp32 FMAs)"
+            dtype, calls_per_group = "f32", lambda g: 1
         elif batch <= 16:
             kname, dtype, calls_per_group = "gemv_mma", "s8 x s8 -> s32 (mma.sync), fp32 scales", lambda g: 2 * len(g)
         else:

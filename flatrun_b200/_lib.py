@@ -25,7 +25,8 @@ QUANT_NAMES = {v: k for k, v in QUANT_IDS.items()}
 FRC_GEMV_ACCUMULATE = 1  # frc_gemv_ex flag
 
 # frc_set_option ids (include/frcuda.h FRC_OPT_*)
-OPTIONS = {"batch1_int16": 1, "batched_fp32": 2, "prefill_tc": 3, "prefill_splits": 4, "inject_oom": 5}
+OPTIONS = {"batch1_int16": 1, "batched_fp32": 2, "prefill_tc": 3, "prefill_splits": 4, "inject_oom": 5,
+           "batch1_tc": 6}
 
 _i = ctypes.c_int
 _i64 = ctypes.c_int64
@@ -46,6 +47,7 @@ SIGNATURES: dict[str, list] = {
     "frc_device_status": [_i, ctypes.POINTER(ctypes.c_uint32)],
     "frc_set_option": [_i, _i],
     "frc_get_option": [_i, ctypes.POINTER(_i)],
+    "frc_batch1_kernel": [_i, ctypes.c_int64, ctypes.POINTER(_i)],
     "frc_noalloc_status": [_i, ctypes.POINTER(ctypes.c_uint32)],
     "frc_gemv_ex": [_i, _i, ctypes.POINTER(_p), ctypes.POINTER(_sz), ctypes.POINTER(_i64), _i64, _p, _p, _p,
                     ctypes.c_float, _i, ctypes.POINTER(_p), _p],
@@ -164,6 +166,18 @@ def get_option(name: str) -> int:
     v = ctypes.c_int(0)
     check(lib.frc_get_option(OPTIONS[name], ctypes.byref(v)), lib)
     return int(v.value)
+
+
+BATCH1_KERNELS = {0: "cuda_core_fp32", 1: "tensor_fp32", 2: "int16"}
+
+
+def batch1_kernel(quant: str, k: int) -> str:
+    """Which batch-1 kernel a launch of (quant, k) runs under the current
+    options: "tensor_fp32" (gemv_tc1), "cuda_core_fp32" or "int16"."""
+    lib = load()
+    v = ctypes.c_int(-1)
+    check(lib.frc_batch1_kernel(QUANT_IDS[quant], int(k), ctypes.byref(v)), lib)
+    return BATCH1_KERNELS[int(v.value)]
 
 
 class option:

@@ -580,6 +580,7 @@ int frc_set_option(int option, int value) {
       o.prefill_splits.store(value);
       return FRC_OK;
     case FRC_OPT_INJECT_OOM: o.inject_oom.store(value ? 1 : 0); return FRC_OK;
+    case FRC_OPT_BATCH1_TC: o.batch1_tc.store(value ? 1 : 0); return FRC_OK;
     default: return fail(FRC_ERR_INVALID, "frc_set_option: unknown option %d", option);
   }
 }
@@ -593,8 +594,27 @@ int frc_get_option(int option, int* value) {
     case FRC_OPT_PREFILL_TC: *value = frc::opt(o.prefill_tc); return FRC_OK;
     case FRC_OPT_PREFILL_SPLITS: *value = frc::opt(o.prefill_splits); return FRC_OK;
     case FRC_OPT_INJECT_OOM: *value = frc::opt(o.inject_oom); return FRC_OK;
+    case FRC_OPT_BATCH1_TC: *value = frc::opt(o.batch1_tc); return FRC_OK;
     default: return fail(FRC_ERR_INVALID, "frc_get_option: unknown option %d", option);
   }
+}
+
+int frc_batch1_kernel(int quant, int64_t k, int* kind) {
+  if (!kind) return fail(FRC_ERR_INVALID, "null pointer");
+  int qk, ts;
+  if (!geometry(quant, &qk, &ts)) return fail(FRC_ERR_INVALID, "unsupported quant id %d", quant);
+  if (k <= 0 || k % qk != 0 || k > (int64_t(1) << 30))
+    return fail(FRC_ERR_INVALID, "frc_batch1_kernel: k=%lld is not a positive multiple of %d", (long long)k, qk);
+  const frc::Options& o = frc::options();
+  frc::Tc1Config c;
+  if (frc::opt(o.batch1_int16)) {
+    *kind = FRC_B1_INT16;
+  } else if (quant == FRC_Q4_K && frc::opt(o.batch1_tc) && frc::tc1_config(static_cast<int>(k), &c)) {
+    *kind = FRC_B1_TENSOR_FP32;
+  } else {
+    *kind = FRC_B1_CUDA_CORE_FP32;
+  }
+  return FRC_OK;
 }
 
 int frc_gemv(int quant, const void* w_dev, size_t w_bytes, int64_t n, int64_t k, const float* x_dev, int64_t batch,
@@ -799,7 +819,12 @@ int frc_weight_create(int device, int quant, const void* host, size_t nbytes, in
   const size_t alloc = ((nbytes ? nbytes : 1) + 255) / 256 * 256;
   FRC_CUDA(cudaMalloc(&dev, alloc), "cudaMalloc(weight)");
   if (nbytes) {
-    cudaError_t e = cudaMemcpy(dev, host, nbytes, cudaMemcpyHostToDevice);
+    // A pageable cudaMemcpy may return before its DMA has landed, and the
+    // kernels that read the weight run on non-blocking streams that do not
+    // order behind the legacy stream: copy on this device's stream and wait
+    // for it, so the weight is complete when the handle is returned.
+    cudaError_t e = cudaMemcpyAsync(dev, host, nbytes, cudaMemcpyHostToDevice, ds->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ds->stream);
     if (e != cudaSuccess) {
       cudaFree(dev);
       return cuda_fail(e, "weight upload");

@@ -83,6 +83,12 @@ struct GemvParams {
   // formed inside every slot
   const float* x_norm_w;
   float x_norm_eps;
+  // gemv_tc1: super-blocks per chunk (= compute warps), chunks per row, the
+  // row stride of a stage in bytes, and the fp16 pair 1024, 1024 (0x64006400;
+  // a parameter, so the mask-and-or of a quant word is one instruction with
+  // the pair as its register operand)
+  int tc_kc, tc_nchunk, tc_stride;
+  uint32_t tc_bias;
 };
 
 constexpr int kMaxMats = 4;

@@ -1,0 +1,549 @@
+// Batch-1 GEMV on the tensor cores with exact fp32 activations: gemv_tc1<Q>
+// (Q4_K).
+//
+// The reference multiplies dequantised fp32 weights by fp32 x and sums in
+// fp32 (src/flatrun_native/kernels/q4_k.h:153-184; the NumPy path is dequant
+// + fp32 BLAS).  This kernel computes the same sums with every product exact:
+//   * a Q4_K weight is d * sc * q - dmin * m (q a nibble, sc and m 6-bit
+//     integers of its 32-element sub-block, d and dmin fp16 per 256-element
+//     super-block).  q * sc <= 945 is an integer, exact in fp16;
+//   * x is scaled by a power of two per super-block (s, so that |x s| < 2^15)
+//     and written as the sum of three fp16 terms, hi + mid + lo, each the
+//     round-to-nearest fp16 of what the previous terms leave: 33 significand
+//     bits cover fp32's 24, so the three terms sum to x s exactly (short of
+//     fp16 underflow for elements below 2^-9 of the super-block's largest,
+//     whose lost bits are below 2^-39 of that largest element);
+//   * one mma.sync m16n8k16 (f16 x f16, fp32 accumulate) multiplies 16 rows
+//     of q * sc by the three terms in columns 0..2 of B; fp16 x fp16 products
+//     (11 x 11 significant bits) are exact in fp32, so the MMA's column sums
+//     are fp32 sums of exact products, as the reference's dot is;
+//   * per super-block and row, y += d / s * (hi + mid + lo column sums) -
+//     dmin * sum_j m_j xs_j, with xs_j the fp32 sum of x over sub-block j:
+//     the reference's algebra with the scales applied per group instead of
+//     per weight.
+//
+// Why warp-level mma.sync and not tcgen05 here: at batch 1 the products are
+// a few percent of the tensor pipe, and what costs is turning raw quant
+// bytes into MMA operands.  mma.sync takes A from registers, so each thread
+// converts its bytes (a mask and one fp16 FMA per two weights, no shared-
+// memory round trip for the dequantised tile) straight into its fragment;
+// tcgen05 would need the converted tile written to shared memory or TMEM
+// and a single-thread issue per tile.
+//
+// Operand layout (m16n8k16, thread (g = lane / 4, t = lane % 4)):
+//   * A: rows g and g + 8 of a 16-row group; thread t converts quant bytes
+//     [32t, 32t + 32) of each super-block's qs (its chunk t: low nibbles are
+//     sub-block 2t, high nibbles sub-block 2t + 1).  Word i of the chunk gives
+//     two MMAs: low nibbles (bytes 0, 2 -> k-slots 2t, 2t+1; bytes 1, 3 ->
+//     2t+8, 2t+9) and high nibbles likewise.  A nibble becomes fp16 1024 + q
+//     by a mask-or (0x64006400), then one fp16 FMA applies the sub-block
+//     scale and removes the bias: (1024 + q) sc - 1024 sc = q sc, exact
+//     because the FMA rounds once and q sc is representable.  High nibbles
+//     stay in place (1024 + 16 q) and take sc / 16 and -64 sc.
+//   * B: lane 4T + t (T = 0, 1, 2: hi, mid, lo) holds term T of the x values
+//     of the k-slots above; the other lanes hold zeros.  These fragments are
+//     the same for every row, so each CTA builds them once per launch in
+//     shared memory (6 bytes per element), indexed [super-block][MMA][lane].
+//   * C: thread t = 0 holds the hi and mid sums, t = 1 the lo sum (and a
+//     zero column), t = 2, 3 zeros; the four lanes of a row are summed at
+//     the end of the row group.
+//
+// Work split: each CTA owns rows [c0, c1) (balanced to one row), in row
+// groups of 16 (clipped at matrix ends).  A row group is streamed in chunks
+// of NW super-blocks (one per warp): one bulk copy per row into a stage whose
+// row stride is padded to 16 mod 32 bytes (the conflict-free layout for the
+// quant loads).  Warp w takes super-block w of every chunk; at the end of a
+// row group the warps' partial sums meet in shared memory and the first 16
+// threads write y.  A producer warp (its lane 0) fills the ring before the
+// grid dependency wait and refills each stage once every compute warp has
+// released it.  All waits are bounded as in the other kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include "gemv.cuh"
+
+namespace frc {
+
+constexpr int kTc1Rows = 16;         // rows per row group: the MMA's M
+constexpr int kTc1MaxWarps = 16;     // compute warps (one super-block each per chunk)
+constexpr int kTc1Lanes = 12;        // lanes of a B fragment that carry x terms
+constexpr int kTc1FragBytes = 16 * kTc1Lanes * 8;  // per super-block: 16 MMAs x 12 lanes x 8 bytes
+constexpr int kTc1Rounds = 2;        // 32-element sub-blocks of x per compute thread, at most
+constexpr int kTc1ZeroBytes = 16 * kTc1Lanes * 8;  // the zero B fragment of lanes >= 12
+
+// Shared-memory layout of gemv_tc1 (host and device).
+struct Tc1Layout {
+  int bars, red, scr, sums, invs, frags, zeros, stages, total;
+};
+
+__host__ __device__ constexpr int tc1_align(int v, int a) { return (v + a - 1) / a * a; }
+
+__host__ __device__ inline Tc1Layout tc1_layout(int nst, int sbs, int stage_bytes) {
+  Tc1Layout L{};
+  L.bars = 0;                                        // full[nst], empty[nst], abort and void flags
+  L.red = tc1_align(16 * nst + 8, 16);               // [2][kTc1MaxWarps][16] row partials
+  L.scr = L.red + 2 * kTc1MaxWarps * kTc1Rows * 4;   // [kTc1MaxWarps] reduction scratch
+  L.sums = L.scr + kTc1MaxWarps * 4;                 // [sbs][8] fp32 sub-block sums of x
+  L.invs = L.sums + sbs * 32;                        // [sbs] 1 / s per super-block
+  L.frags = tc1_align(L.invs + sbs * 4, 128);        // [sbs][16][12] uint2
+  L.zeros = L.frags + sbs * kTc1FragBytes;            // kTc1ZeroBytes of zeros
+  L.stages = tc1_align(L.zeros + kTc1ZeroBytes, 128);
+  L.total = L.stages + nst * stage_bytes;
+  return L;
+}
+
+// Row stride of a stage: the chunk's bytes padded to 16 mod 32 (a 16-byte
+// load by lanes of rows g and g + 1 then covers all 32 banks).
+__host__ __device__ constexpr int tc1_row_stride(int kc) { return (kc & 1) ? kc * 144 : kc * 144 + 16; }
+
+FRC_DEVICE_INLINE uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+FRC_DEVICE_INLINE uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+FRC_DEVICE_INLINE uint32_t hadd2_u(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+FRC_DEVICE_INLINE uint32_t hmul2_u(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+FRC_DEVICE_INLINE void mma_f16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                     uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+FRC_DEVICE_INLINE uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+FRC_DEVICE_INLINE void sts64(uint32_t a, uint32_t x, uint32_t y) {
+  asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(a), "r"(x), "r"(y) : "memory");
+}
+
+// fp16 constants, two per word
+constexpr uint32_t kH2Bias = 0x64006400u;      // 1024, 1024 (with a nibble or byte in the mantissa)
+constexpr uint32_t kH2Neg1024 = 0xE400E400u;   // -1024
+constexpr uint32_t kH2Sixteenth = 0x2C002C00u; // 1/16
+constexpr uint32_t kH2Neg64 = 0xD400D400u;     // -64
+
+// The three fp16 terms of a and b (low and high halves of each word).
+FRC_DEVICE_INLINE void split3(float a, float b, uint32_t& t0, uint32_t& t1, uint32_t& t2) {
+  const __half2 h0 = __floats2half2_rn(a, b);
+  const float2 f0 = __half22float2(h0);
+  const float ra = a - f0.x, rb = b - f0.y;
+  const __half2 h1 = __floats2half2_rn(ra, rb);
+  const float2 f1 = __half22float2(h1);
+  const __half2 h2 = __floats2half2_rn(ra - f1.x, rb - f1.y);
+  t0 = *reinterpret_cast<const uint32_t*>(&h0);
+  t1 = *reinterpret_cast<const uint32_t*>(&h1);
+  t2 = *reinterpret_cast<const uint32_t*>(&h2);
+}
+
+// Power-of-two scale s with |m s| < 2^15 for the largest magnitude m of a
+// super-block (exponent clamped so s and 1 / s stay normal), and 1 / s.
+FRC_DEVICE_INLINE void tc1_scale(float m, float& s, float& inv) {
+  int e = static_cast<int>((__float_as_uint(m) >> 23) & 0xFFu) - 127;  // floor(log2 m) for normal m
+  int se = 14 - e;
+  se = se < -100 ? -100 : (se > 100 ? 100 : se);
+  s = __uint_as_float(static_cast<uint32_t>(127 + se) << 23);
+  inv = __uint_as_float(static_cast<uint32_t>(127 - se) << 23);
+}
+
+// Q4_K scale and min bytes of sub-blocks 2t and 2t+1 from a block header
+// (h.y = scales[0..3], h.z = scales[4..7], h.w = scales[8..11]): byte 0 of
+// the results is sub-block 2t, byte 1 sub-block 2t+1.  sh = 16 (t & 1);
+// lanes t >= 2 take the split 4+2-bit form (ggml's get_scale_min_k4).
+FRC_DEVICE_INLINE void tc1_q4k_scales(const uint4& h, uint32_t sh, bool hi_t, uint32_t m1, uint32_t m2, uint32_t& sc,
+                                      uint32_t& mn) {
+  const uint32_t a = h.y >> sh, b = h.z >> sh, c = h.w >> sh;
+  const uint32_t x1 = hi_t ? c : a;
+  const uint32_t x2 = hi_t ? (c >> 4) : b;
+  sc = (x1 & m1) | ((a >> 2) & m2);
+  mn = (x2 & m1) | ((b >> 2) & m2);
+}
+
+// One super-block of a 16-row group for this warp.  row: shared address of
+// row g's block; xf: this lane's B fragment words for the super-block (lanes
+// >= 12 point at a zero fragment), fragment m at xf[12 m]; sums: the
+// super-block's 8 sub-block sums.
+FRC_DEVICE_INLINE void tc1_q4k_sb(uint32_t row, uint32_t stride, const uint2* xf, uint32_t sums, float inv_s,
+                                  int t, uint32_t sh, bool hi_t, uint32_t m1, uint32_t m2, uint32_t bias, float& acc0,
+                                  float& acc8, float& mn0, float& mn8) {
+  const uint32_t row8 = row + 8u * stride;
+  const uint4 h0 = lds128<0>(row), h8 = lds128<0>(row8);
+  const uint32_t q0 = row + 16u + 32u * static_cast<uint32_t>(t), q8 = row8 + 16u + 32u * static_cast<uint32_t>(t);
+  uint32_t sc0, mnw0, sc8, mnw8;
+  tc1_q4k_scales(h0, sh, hi_t, m1, m2, sc0, mnw0);
+  tc1_q4k_scales(h8, sh, hi_t, m1, m2, sc8, mnw8);
+  // (sc, sc) of the low sub-block, and (sc/16, sc/16) of the high one, with
+  // their bias terms -1024 sc and -64 sc
+  const uint32_t sl0 = hadd2_u(prmt(sc0, kH2Bias, 0x7050), kH2Neg1024);
+  const uint32_t nl0 = hmul2_u(sl0, kH2Neg1024);
+  const uint32_t sg0 = hfma2_u(prmt(sc0, kH2Bias, 0x7151), kH2Sixteenth, kH2Neg64);
+  const uint32_t ng0 = hmul2_u(sg0, kH2Neg1024);
+  const uint32_t sl8 = hadd2_u(prmt(sc8, kH2Bias, 0x7050), kH2Neg1024);
+  const uint32_t nl8 = hmul2_u(sl8, kH2Neg1024);
+  const uint32_t sg8 = hfma2_u(prmt(sc8, kH2Bias, 0x7151), kH2Sixteenth, kH2Neg64);
+  const uint32_t ng8 = hmul2_u(sg8, kH2Neg1024);
+
+  float cl[4] = {0.f, 0.f, 0.f, 0.f}, ch[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    // words 4 half .. 4 half + 3 of chunk t in rows g and g + 8
+    const uint4 a0 = half ? lds128<16>(q0) : lds128<0>(q0);
+    const uint4 a8 = half ? lds128<16>(q8) : lds128<0>(q8);
+    const uint32_t w0[4] = {a0.x, a0.y, a0.z, a0.w};
+    const uint32_t w8[4] = {a8.x, a8.y, a8.z, a8.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = 4 * half + j;
+      const uint32_t x0 = w0[j], x8 = w8[j];
+      const uint32_t s0 = x0 >> 8, s8 = x8 >> 8;
+      const uint2 bl0 = xf[(2 * i) * kTc1Lanes], bh0 = xf[(2 * i + 1) * kTc1Lanes];
+      mma_f16_16816(cl, hfma2_u((x0 & 0x000F000Fu) | bias, sl0, nl0), hfma2_u((x8 & 0x000F000Fu) | bias, sl8, nl8),
+                    hfma2_u((s0 & 0x000F000Fu) | bias, sl0, nl0), hfma2_u((s8 & 0x000F000Fu) | bias, sl8, nl8), bl0.x,
+                    bl0.y);
+      mma_f16_16816(ch, hfma2_u((x0 & 0x00F000F0u) | bias, sg0, ng0), hfma2_u((x8 & 0x00F000F0u) | bias, sg8, ng8),
+                    hfma2_u((s0 & 0x00F000F0u) | bias, sg0, ng0), hfma2_u((s8 & 0x00F000F0u) | bias, sg8, ng8), bh0.x,
+                    bh0.y);
+    }
+  }
+  // columns 2t, 2t+1 of rows g and g+8: (hi, mid) for t = 0, (lo, 0) for
+  // t = 1, zeros beyond
+  const float s_0 = (cl[0] + ch[0]) + (cl[1] + ch[1]);
+  const float s_8 = (cl[2] + ch[2]) + (cl[3] + ch[3]);
+  const float d0 = half_bits_to_float(h0.x), dm0 = half_bits_to_float(h0.x >> 16);
+  const float d8 = half_bits_to_float(h8.x), dm8 = half_bits_to_float(h8.x >> 16);
+  acc0 = fmaf(d0 * inv_s, s_0, acc0);
+  acc8 = fmaf(d8 * inv_s, s_8, acc8);
+  // mins of sub-blocks 2t and 2t+1 against their x sums
+  const uint2 xsw = lds64(sums + 8u * static_cast<uint32_t>(t));
+  const float xs0 = __uint_as_float(xsw.x), xs1 = __uint_as_float(xsw.y);
+  mn0 = fmaf(dm0, fmaf(static_cast<float>(mnw0 & 0xFFu), xs0, static_cast<float>((mnw0 >> 8) & 0xFFu) * xs1), mn0);
+  mn8 = fmaf(dm8, fmaf(static_cast<float>(mnw8 & 0xFFu), xs0, static_cast<float>((mnw8 >> 8) & 0xFFu) * xs1), mn8);
+}
+
+// Non-blocking test of an mbarrier phase.
+FRC_DEVICE_INLINE bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+template <int OFF>
+FRC_DEVICE_INLINE uint2 lds64i(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2+%3];" : "=r"(v.x), "=r"(v.y) : "r"(a), "n"(OFF));
+  return v;
+}
+FRC_DEVICE_INLINE float ldsf(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+
+// Activations of sub-block j (32 consecutive elements of x), with the
+// SwiGLU applied when x_mul is set (silu(gate) * up as the reference forms
+// it, qwen2.py:1690-1751).
+FRC_DEVICE_INLINE void tc1_load_sub(const GemvParams& p, int j, float (&v)[32]) {
+  const float4* src = reinterpret_cast<const float4*>(p.x + static_cast<int64_t>(j) * 32);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 f = __ldg(src + q);
+    v[4 * q] = f.x;
+    v[4 * q + 1] = f.y;
+    v[4 * q + 2] = f.z;
+    v[4 * q + 3] = f.w;
+  }
+  if (p.x_mul) {
+    const float4* us = reinterpret_cast<const float4*>(p.x_mul + static_cast<int64_t>(j) * 32);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 u = __ldg(us + q);
+      const float uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float g = v[4 * q + e];
+        const float sg = 1.0f / (1.0f + expf(-g));
+        v[4 * q + e] = (sg * g) * uu[e];
+      }
+    }
+  }
+}
+
+// The producer's position in the CTA's tile sequence (row groups of 16 rows,
+// each in nch chunks), and the issue of one tile: one bulk copy per row.
+struct Tc1Cursor {
+  int64_t t0;  // first row of the current row group
+  Tile T;      // the current row group (valid while ch > 0 or after begin)
+  int rows;
+  int ch;      // next chunk of the current row group
+};
+
+FRC_DEVICE_INLINE void tc1_issue(const GemvParams& p, Tc1Cursor& c, int64_t c1, uint8_t* dst, uint64_t* bar) {
+  if (c.ch == 0) {
+    c.T = tile_at(p, c.t0, c1, kTc1Rows);
+    c.rows = static_cast<int>(c.T.t1 - c.t0);
+  }
+  const int kc = p.tc_kc, sbs = p.k / 256;
+  const int nsb = (c.ch + 1) * kc <= sbs ? kc : sbs - c.ch * kc;
+  const uint32_t cb = static_cast<uint32_t>(nsb) * 144u;
+  mbar_arrive_expect_tx(bar, cb * static_cast<uint32_t>(c.rows));
+  const uint8_t* src =
+      p.mat_w[c.T.m] + static_cast<uint64_t>(c.T.local) * p.row_bytes + static_cast<uint64_t>(c.ch) * kc * 144;
+  for (int r = 0; r < c.rows; ++r)
+    bulk_g2s(dst + r * p.tc_stride, src + static_cast<uint64_t>(r) * p.row_bytes, cb, bar);
+  if (++c.ch == p.tc_nchunk) {
+    c.ch = 0;
+    c.t0 = c.T.t1;
+  }
+}
+
+template <int Q>
+__global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(GemvParams p) {
+  static_assert(Q == kQ4_K, "gemv_tc1 covers Q4_K");
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nw = static_cast<int>(blockDim.x >> 5) - 1;  // compute warps; the last warp produces
+  const int nct = nw * 32;
+  const int ct = threadIdx.x;
+  const int nst = p.nstage;
+  const int sbs = p.k / 256;
+  const int stage_bytes = p.stage_stride;
+  const Tc1Layout L = tc1_layout(nst, sbs, stage_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + nst;
+  int* abort_flag = reinterpret_cast<int*>(empty + nst);
+  int* void_flag = abort_flag + 1;  // an earlier gather's wait ran out
+  float* red = reinterpret_cast<float*>(smem + L.red);
+  float* scr = reinterpret_cast<float*>(smem + L.scr);
+  float* sums = reinterpret_cast<float*>(smem + L.sums);
+  float* invs = reinterpret_cast<float*>(smem + L.invs);
+  uint8_t* stages = smem + L.stages;
+
+  if (ct == 0) {
+    for (int i = 0; i < nst; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], static_cast<uint32_t>(nw));
+    }
+    *abort_flag = 0;
+    *void_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  volatile int* abort = abort_flag;
+
+  int64_t c0, c1;
+  cta_rows(p.n, c0, c1);
+  const int nch = p.tc_nchunk;
+  const int ntiles = count_tiles(p, c0, c1, kTc1Rows) * nch;
+
+  if (warp == nw) {
+    // the producer warp: the weights are never written by another kernel, so
+    // it streams them before the previous kernel in the stream has finished
+    // (programmatic dependent launch)
+    griddep_launch_dependents();
+    if (lane == 0) {
+      Tc1Cursor cur{c0, Tile{}, 0, 0};
+      int issued = 0;
+      for (; issued < ntiles; ++issued) {
+        const int si = issued % nst;
+        if (issued >= nst && !wait_phase(&empty[si], static_cast<uint32_t>(issued / nst - 1) & 1u, abort)) {
+          atomicOr(p.status, kStatusEmptyWaitTimeout);
+          break;
+        }
+        tc1_issue(p, cur, c1, stages + si * stage_bytes, &full[si]);
+      }
+      // the last stage-full of copies must land before the CTA may exit
+      int zero = 0;
+      for (int i = issued > nst ? issued - nst : 0; i < issued; ++i) {
+        if (!wait_phase(&full[i % nst], static_cast<uint32_t>(i / nst) & 1u, &zero))
+          atomicOr(p.status, kStatusDrainTimeout);
+      }
+    }
+    return;
+  }
+  griddep_wait();
+  griddep_launch_dependents();
+  int g_world = p.g_world;
+  if (p.w_world > 1) {  // an earlier fused gather must be complete on every rank
+    if (ct < p.w_world) {
+      const uint32_t e = *p.w_epoch;
+      const uint64_t t0 = global_ns();
+      while (true) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p.w_flags + ct) : "memory");
+        if (static_cast<int32_t>(v - e) >= 0) break;
+        if (global_ns() - t0 > kWaitLimitNs) {
+          atomicOr(p.status, kStatusGatherTimeout);
+          *void_flag = 1;  // read after the barrier below
+          break;
+        }
+      }
+    }
+    named_barrier_sync(1, nct);
+    // after a gather wait that ran out a peer may still read its buffer:
+    // keep the outputs local and publish nothing (the status bit tells the
+    // caller the step is void)
+    if (*reinterpret_cast<volatile int*>(void_flag)) g_world = 1;
+  }
+
+  // ---- x fragments: thread ct owns sub-blocks ct, ct + nct, ... ------------
+  const int nsub = p.k / 32;
+  const int rounds = (nsub + nct - 1) / nct;  // 1 or 2 (tc1_config)
+  float inv_norm = 1.f;
+  if (p.x_norm_w) {  // RMSNorm of the whole row of x (qwen2.py:365-378)
+    float ss = 0.f;
+    for (int r = 0; r < rounds; ++r) {
+      const int j = ct + r * nct;
+      if (j < nsub) {
+        float v[32];
+        tc1_load_sub(p, j, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) ss = fmaf(v[e], v[e], ss);
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) scr[warp] = ss;
+    named_barrier_sync(1, nct);
+    ss = 0.f;
+    for (int w = 0; w < nw; ++w) ss += scr[w];
+    inv_norm = 1.0f / sqrtf(ss / static_cast<float>(p.k) + p.x_norm_eps);
+  }
+  const uint32_t frag_base = smem_u32(smem + L.frags);
+  for (int r = 0; r < rounds; ++r) {
+    const int j = ct + r * nct;  // sub-block; lanes 8a .. 8a+7 hold one super-block
+    float v[32];
+    if (j < nsub) {
+      tc1_load_sub(p, j, v);
+      if (p.x_norm_w) {
+        const float4* ws = reinterpret_cast<const float4*>(p.x_norm_w + static_cast<int64_t>(j) * 32);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 g = __ldg(ws + q);
+          const float gg[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[4 * q + e] = (v[4 * q + e] * inv_norm) * gg[e];
+        }
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) v[e] = 0.f;
+    }
+    float m = 0.f, xsum = 0.f;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      m = fmaxf(m, fabsf(v[e]));
+      xsum += v[e];
+    }
+    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
+    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
+    if (j < nsub) {
+      float sc, inv;
+      tc1_scale(m, sc, inv);
+      const int sb = j >> 3, jj = j & 7, t = jj >> 1, h = jj & 1;
+      sums[j] = xsum;
+      if (jj == 0) invs[sb] = inv;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        uint32_t p0, p1, p2, q0, q1, q2;
+        split3(v[4 * i] * sc, v[4 * i + 2] * sc, p0, p1, p2);
+        split3(v[4 * i + 1] * sc, v[4 * i + 3] * sc, q0, q1, q2);
+        const uint32_t a = frag_base + static_cast<uint32_t>(((sb * 16 + 2 * i + h) * kTc1Lanes + t) * 8);
+        sts64(a, p0, q0);
+        sts64(a + 32u, p1, q1);
+        sts64(a + 64u, p2, q2);
+      }
+    }
+  }
+  // the zero fragment read by lanes >= 12 (columns 3..7 of B)
+  const uint32_t zero_base = smem_u32(smem + L.zeros);
+  for (int i = ct; i < kTc1ZeroBytes / 8; i += nct) sts64(zero_base + 8u * i, 0u, 0u);
+  named_barrier_sync(1, nct);  // fragments, sums, scales and zeros complete
+
+  // ---- row groups ------------------------------------------------------------
+  const int g = lane >> 2, t = lane & 3;
+  const bool hi_t = t >= 2;
+  const uint32_t sh = static_cast<uint32_t>(t & 1) * 16u;
+  const uint32_t m1 = hi_t ? 0x0F0Fu : 0x3F3Fu, m2 = hi_t ? 0x3030u : 0u;
+  // lanes < 12 read their fragment words (stride one super-block), the rest
+  // the zero fragment (stride 0)
+  const uint2* xf_lane = lane < kTc1Lanes ? reinterpret_cast<const uint2*>(smem + L.frags) + lane
+                                           : reinterpret_cast<const uint2*>(smem + L.zeros);
+  const int xf_step = lane < kTc1Lanes ? kTc1FragBytes / 8 : 0;
+  const int kc = p.tc_kc;
+  const uint32_t stride = static_cast<uint32_t>(p.tc_stride);
+  const uint32_t row_lane = smem_u32(stages) + static_cast<uint32_t>(g) * stride + static_cast<uint32_t>(warp) * 144u;
+  const uint32_t sums_s = smem_u32(sums), invs_s = smem_u32(invs);
+  int s = 0;
+  uint32_t ph = 0u;
+  int par = 0;
+  for (int64_t t0 = c0; t0 < c1;) {
+    const Tile T = tile_at(p, t0, c1, kTc1Rows);
+    const int rows = static_cast<int>(T.t1 - t0);
+    float acc0 = 0.f, acc8 = 0.f, mn0 = 0.f, mn8 = 0.f;
+    for (int ch = 0; ch < nch; ++ch) {
+      const int sb = ch * kc + warp;
+      if (wait_phase(&full[s], ph, abort)) {
+        if (sb < sbs) {
+          tc1_q4k_sb(row_lane + static_cast<uint32_t>(s * stage_bytes), stride, xf_lane + sb * xf_step,
+                     sums_s + static_cast<uint32_t>(sb * 32), ldsf(invs_s + 4u * static_cast<uint32_t>(sb)), t, sh,
+                     hi_t, m1, m2, p.tc_bias, acc0, acc8, mn0, mn8);
+        }
+      } else if (lane == 0) {
+        atomicOr(p.status, kStatusFullWaitTimeout);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (++s == nst) {
+        s = 0;
+        ph ^= 1u;
+      }
+    }
+    // rows g and g+8: the four lanes t of a row, then the warps
+    float v0 = acc0 - mn0, v8 = acc8 - mn8;
+    v0 += __shfl_xor_sync(0xFFFFFFFFu, v0, 1);
+    v8 += __shfl_xor_sync(0xFFFFFFFFu, v8, 1);
+    v0 += __shfl_xor_sync(0xFFFFFFFFu, v0, 2);
+    v8 += __shfl_xor_sync(0xFFFFFFFFu, v8, 2);
+    float* rb = red + par * kTc1MaxWarps * kTc1Rows;
+    if (t == 0) {
+      rb[warp * kTc1Rows + g] = v0;
+      rb[warp * kTc1Rows + g + 8] = v8;
+    }
+    named_barrier_sync(1, nct);
+    if (ct < rows) {
+      float y = 0.f;
+      for (int w = 0; w < nw; ++w) y += rb[w * kTc1Rows + ct];
+      if (!*abort) put_y(p, g_world, p.mat_y[T.m] + T.local + ct, y);
+    }
+    par ^= 1;
+    t0 = T.t1;
+  }
+  if (g_world > 1) {  // publish this CTA's gathered rows
+    named_barrier_sync(1, nct);
+    if (ct == 0) gather_arrive(p, g_world, 1);
+  }
+}
+
+}  // namespace frc

@@ -15,6 +15,7 @@
 #include <tuple>
 
 #include "gemv.cuh"
+#include "gemv_tc1.cuh"
 #include "gemm_tc.cuh"
 #include "gemv_mma.cuh"
 
@@ -76,6 +77,7 @@ struct Options {
   std::atomic<int> prefill_tc{1};      // FRC_OPT_PREFILL_TC
   std::atomic<int> prefill_splits{0};  // FRC_OPT_PREFILL_SPLITS
   std::atomic<int> inject_oom{0};      // FRC_OPT_INJECT_OOM
+  std::atomic<int> batch1_tc{1};       // FRC_OPT_BATCH1_TC
 };
 inline Options& options() {
   static Options o;
@@ -618,6 +620,74 @@ inline cudaError_t launch_gather_wait(const uint32_t* flags, int world, const ui
   return cudaGetLastError();
 }
 
+// Batch-1 tensor-core kernel (gemv_tc1, Q4_K).  Compute warps = super-blocks
+// per chunk: the whole row when it has at most 16 super-blocks, else the
+// largest divisor of the row's super-blocks in [8, 16], else 16; as many
+// stages (up to 8) as shared memory holds beside the activation fragments.
+struct Tc1Config {
+  int nw = 0, nch = 0, stride = 0, stage_bytes = 0, nst = 0;
+  size_t smem = 0;
+};
+
+inline bool tc1_config(int k, Tc1Config* c) {
+  if (k % 256 != 0 || k <= 0) return false;
+  const int sbs = k / 256;
+  int nw = 0;
+  if (sbs <= kTc1MaxWarps) {
+    nw = sbs;
+  } else {
+    for (int d = kTc1MaxWarps; d >= 8 && !nw; --d)
+      if (sbs % d == 0) nw = d;
+    if (!nw) nw = kTc1MaxWarps;
+  }
+  const int forced = tuning().nwarps;
+  if (forced >= 1 && forced <= kTc1MaxWarps) nw = forced;
+  if (k / 32 > kTc1Rounds * 32 * nw) return false;  // x longer than the prologue covers
+  c->nw = nw;
+  c->nch = (sbs + nw - 1) / nw;
+  c->stride = tc1_row_stride(nw);
+  c->stage_bytes = round_up(kTc1Rows * c->stride, 128);
+  const int budget = tuned(tuning().smem_bytes, kSmemBudget);
+  int nst = tuning().nstage > 0 ? tuning().nstage : 8;
+  for (; nst >= 2; --nst) {
+    if (tc1_layout(nst, sbs, c->stage_bytes).total <= budget) break;
+  }
+  if (nst < 2) return false;
+  c->nst = nst;
+  c->smem = static_cast<size_t>(tc1_layout(nst, sbs, c->stage_bytes).total);
+  return true;
+}
+
+template <int Q>
+inline cudaError_t launch_tc1(GemvParams p, const GemvRequest& r, const Tc1Config& c) {
+  p.tc_kc = c.nw;
+  p.tc_nchunk = c.nch;
+  p.tc_stride = c.stride;
+  p.tc_bias = kH2Bias;
+  p.stage_stride = c.stage_bytes;
+  p.nstage = c.nst;
+  const int threads = (c.nw + 1) * 32;
+  int per_sm = 0;
+  cudaError_t e = kernel_occupancy(reinterpret_cast<const void*>(gemv_tc1<Q>), r.device, threads, c.smem, &per_sm);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  int64_t grid = static_cast<int64_t>(per_sm) * r.sms;
+  const int64_t groups = (p.n + kTc1Rows - 1) / kTc1Rows;
+  if (grid > groups) grid = groups;
+  if (grid < 1) grid = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = c.smem;
+  cfg.stream = r.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = tuned(tuning().pdl, 1) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemv_tc1<Q>, p);
+}
+
 // Largest tile footprint must fit in shared memory with two stages.
 template <int Q>
 inline bool tiles_fit(int row_bytes) {
@@ -680,6 +750,11 @@ cudaError_t launch_gemv(const GemvRequest& r) {
   if (r.batch == 1) {
     GemvParams b1 = p;
     b1.units = (r.k / F::QK) * I8<Q>::UPB;
+    if constexpr (Q == kQ4_K) {
+      Tc1Config c;
+      if (!opt(options().batch1_int16) && opt(options().batch1_tc) && tc1_config(r.k, &c))
+        return launch_tc1<Q>(b1, r, c);
+    }
     const cudaError_t e =
         opt(options().batch1_int16) ? launch_b1_any<Q, false>(b1, r) : launch_b1_any<Q, true>(b1, r);
     if (e != cudaErrorInvalidValue) return e;

@@ -96,14 +96,28 @@ int frc_device_status(int device, uint32_t* flags);
  *  FRC_OPT_PREFILL_SPLITS 0 (default): k-splits of the prefill GEMM chosen from
  *                         the shape; n > 0: n splits (clamped to 1..16).
  *  FRC_OPT_INJECT_OOM     1: frc_weight_create fails with FRC_ERR_NOMEM before
- *                         any CUDA call (a test of the error path); default 0. */
+ *                         any CUDA call (a test of the error path); default 0.
+ *  FRC_OPT_BATCH1_TC      1 (default): batch-1 Q4_K with x in fp32 runs on the
+ *                         tensor cores (weights as exact fp16 integers q * sc,
+ *                         x as an exact sum of three fp16 terms, fp32
+ *                         accumulation) where the row fits its shared-memory
+ *                         layout; 0: on the CUDA-core fp32 kernel. */
 #define FRC_OPT_BATCH1_INT16   1
 #define FRC_OPT_BATCHED_FP32   2
 #define FRC_OPT_PREFILL_TC     3
 #define FRC_OPT_PREFILL_SPLITS 4
 #define FRC_OPT_INJECT_OOM     5
+#define FRC_OPT_BATCH1_TC      6
 int frc_set_option(int option, int value);
 int frc_get_option(int option, int* value);
+/* The batch-1 kernel a launch of (quant, k) runs under the current options
+ * (no reference counterpart): FRC_B1_CUDA_CORE_FP32 (x in fp32, fp32 FMAs),
+ * FRC_B1_TENSOR_FP32 (x in fp32 as three exact fp16 terms, tensor-core
+ * products, fp32 accumulation) or FRC_B1_INT16 (16-bit grid, dp4a). */
+#define FRC_B1_CUDA_CORE_FP32 0
+#define FRC_B1_TENSOR_FP32    1
+#define FRC_B1_INT16          2
+int frc_batch1_kernel(int quant, int64_t k, int* kind);
 
 /* ---- stream-ordered device-pointer kernels ------------------------------ *
  * No synchronisation: the work is enqueued on `stream` (a cudaStream_t;

@@ -326,6 +326,61 @@ def test_batch1_activation_outliers(cuda_backend, fmt, int16):
     cuda_backend.close()
 
 
+# Q4_K batch-1 shapes for the tensor-core kernel: one super-block, odd (9)
+# and even super-block counts per chunk, two chunks (5120: 10 warps; 8192:
+# 16), a ragged last chunk (18944: 74 super-blocks, chunks of 16), ragged
+# row groups (1, 15, 17, 33, 37 rows), and a row too long for the shared-
+# memory fragments (36864: falls back to the CUDA-core kernel)
+TC1_SHAPES = [(1, 256), (15, 512), (16, 2304), (17, 3584), (33, 4096), (300, 5120), (100, 8192), (37, 18944),
+              (64, 36864)]
+
+
+@pytest.mark.parametrize("n,k", TC1_SHAPES)
+def test_batch1_tensor_core_q4k(cuda_backend, n, k):
+    """Q4_K batch 1 on the tensor-core kernel (default: weights as exact fp16
+    integers, x as an exact sum of three fp16 terms, fp32 accumulation) and on
+    the CUDA-core fp32 kernel (batch1_tc = 0): both within the fp32 tolerance
+    of fp64, normalised by the term magnitude (few rows can cancel)."""
+    raw = synth.make_weight("Q4_K", n, k, seed=k + n)
+    x = synth.make_x(k, seed=k - n)
+    ref = O.matvec_fp64("Q4_K", raw, x, n, k)
+    scale = O.term_scale("Q4_K", raw, x, n, k)
+    for tc in (1, 0):
+        with _lib.option("batch1_tc", tc):
+            y = cuda_backend.weight(raw, n, k, "Q4_K").matmul(x)
+        assert O.norm_err(y, ref, scale) < 5e-6, (n, k, tc)
+        assert O.rel_err(y, ref) < TOL, (n, k, tc)
+    cuda_backend.close()
+
+
+def test_batch1_tensor_core_q4k_wide_range(cuda_backend):
+    """Activations spanning 60 decades, runs of exact zeros and sign changes:
+    each super-block takes its own power-of-two scale, so the three fp16 terms
+    stay exact where the magnitude matters."""
+    n, k = 256, 4096
+    raw = synth.make_weight("Q4_K", n, k, seed=7)
+    rng = np.random.default_rng(8)
+    x = (rng.standard_normal(k) * 10.0 ** rng.uniform(-30, 30, k)).astype(np.float32)
+    x[100:300] = 0.0
+    y = cuda_backend.weight(raw, n, k, "Q4_K").matmul(x)
+    ref = O.matvec_fp64("Q4_K", raw, x, n, k)
+    assert O.norm_err(y, ref, O.term_scale("Q4_K", raw, x, n, k)) < 1e-6
+    cuda_backend.close()
+
+
+def test_batch1_tensor_core_q4k_repeatable(cuda_backend):
+    """The kernel's sums run in a fixed order: repeated launches agree bit
+    for bit."""
+    n, k = 1000, 8192
+    raw = synth.make_weight("Q4_K", n, k, seed=11)
+    x = synth.make_x(k, seed=12)
+    w = cuda_backend.weight(raw, n, k, "Q4_K")
+    y0 = w.matmul(x)
+    for _ in range(3):
+        assert O.same_bits(w.matmul(x), y0)
+    cuda_backend.close()
+
+
 # ---- device-pointer entry point ---------------------------------------------
 
 @pytest.mark.parametrize("fmt", FMTS)
