@@ -50,15 +50,16 @@
 //
 // Work split: each CTA owns rows [c0, c1) (balanced to one row), in row
 // groups of 16 (clipped at matrix ends).  A row group is streamed in chunks
-// of NW super-blocks (one per warp): one bulk copy per row into a stage whose
-// row stride is padded to 16 mod 32 bytes (the conflict-free layout for the
-// quant loads).  Warp w takes super-block w of every chunk; at the end of a
+// of NW super-blocks (one per warp): one 3-D tensor copy (TMA, no multicast)
+// of 16 rows x NW super-blocks per tile, or, for a short row group, one bulk
+// copy per row.  Warp w takes super-block w of every chunk; at the end of a
 // row group the warps' partial sums meet in shared memory and the first 16
 // threads write y.  A producer warp (its lane 0) fills the ring before the
 // grid dependency wait and refills each stage once every compute warp has
 // released it.  All waits are bounded as in the other kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 
 #include "gemv.cuh"
@@ -93,9 +94,16 @@ __host__ __device__ inline Tc1Layout tc1_layout(int nst, int sbs, int stage_byte
   return L;
 }
 
-// Row stride of a stage: the chunk's bytes padded to 16 mod 32 (a 16-byte
-// load by lanes of rows g and g + 1 then covers all 32 banks).
-__host__ __device__ constexpr int tc1_row_stride(int kc) { return (kc & 1) ? kc * 144 : kc * 144 + 16; }
+// Row stride of a stage: the chunk's bytes, dense (the layout a 3-D tensor
+// copy of 16 rows x kc super-blocks lands in).
+__host__ __device__ constexpr int tc1_row_stride(int kc) { return kc * 144; }
+
+// One tensor map per matrix of the launch: the matrix as a 3-D tensor of
+// 8-byte words [rows][super-blocks][18] (strides row_bytes and 144 bytes);
+// a box of 16 rows x kc super-blocks x 18 words is one tile.
+struct Tc1Maps {
+  CUtensorMap m[4];
+};
 
 FRC_DEVICE_INLINE uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
@@ -126,7 +134,7 @@ FRC_DEVICE_INLINE void mma_f16_16816(float (&c)[4], uint32_t a0, uint32_t a1, ui
 }
 FRC_DEVICE_INLINE uint2 lds64(uint32_t a) {
   uint2 v;
-  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
   return v;
 }
 FRC_DEVICE_INLINE void sts64(uint32_t a, uint32_t x, uint32_t y) {
@@ -176,10 +184,10 @@ FRC_DEVICE_INLINE void tc1_q4k_scales(const uint4& h, uint32_t sh, bool hi_t, ui
 }
 
 // One super-block of a 16-row group for this warp.  row: shared address of
-// row g's block; xf: this lane's B fragment words for the super-block (lanes
-// >= 12 point at a zero fragment), fragment m at xf[12 m]; sums: the
-// super-block's 8 sub-block sums.
-FRC_DEVICE_INLINE void tc1_q4k_sb(uint32_t row, uint32_t stride, const uint2* xf, uint32_t sums, float inv_s,
+// row g's block; xf: shared address of this lane's B fragment words for the
+// super-block (lanes >= 12 point at a zero fragment), fragment m at xf + 96 m;
+// sums: the super-block's 8 sub-block sums.
+FRC_DEVICE_INLINE void tc1_q4k_sb(uint32_t row, uint32_t stride, uint32_t xf, uint32_t sums, float inv_s,
                                   int t, uint32_t sh, bool hi_t, uint32_t m1, uint32_t m2, uint32_t bias, float& acc0,
                                   float& acc8, float& mn0, float& mn8) {
   const uint32_t row8 = row + 8u * stride;
@@ -212,7 +220,8 @@ FRC_DEVICE_INLINE void tc1_q4k_sb(uint32_t row, uint32_t stride, const uint2* xf
       const int i = 4 * half + j;
       const uint32_t x0 = w0[j], x8 = w8[j];
       const uint32_t s0 = x0 >> 8, s8 = x8 >> 8;
-      const uint2 bl0 = xf[(2 * i) * kTc1Lanes], bh0 = xf[(2 * i + 1) * kTc1Lanes];
+      const uint2 bl0 = lds64(xf + static_cast<uint32_t>(2 * i * kTc1Lanes * 8)),
+                  bh0 = lds64(xf + static_cast<uint32_t>((2 * i + 1) * kTc1Lanes * 8));
       mma_f16_16816(cl, hfma2_u((x0 & 0x000F000Fu) | bias, sl0, nl0), hfma2_u((x8 & 0x000F000Fu) | bias, sl8, nl8),
                     hfma2_u((s0 & 0x000F000Fu) | bias, sl0, nl0), hfma2_u((s8 & 0x000F000Fu) | bias, sl8, nl8), bl0.x,
                     bl0.y);
@@ -299,19 +308,33 @@ struct Tc1Cursor {
   int ch;      // next chunk of the current row group
 };
 
-FRC_DEVICE_INLINE void tc1_issue(const GemvParams& p, Tc1Cursor& c, int64_t c1, uint8_t* dst, uint64_t* bar) {
+FRC_DEVICE_INLINE void tc1_issue(const GemvParams& p, const Tc1Maps& maps, Tc1Cursor& c, int64_t c1, uint8_t* dst,
+                                 uint64_t* bar) {
   if (c.ch == 0) {
     c.T = tile_at(p, c.t0, c1, kTc1Rows);
     c.rows = static_cast<int>(c.T.t1 - c.t0);
   }
   const int kc = p.tc_kc, sbs = p.k / 256;
-  const int nsb = (c.ch + 1) * kc <= sbs ? kc : sbs - c.ch * kc;
-  const uint32_t cb = static_cast<uint32_t>(nsb) * 144u;
-  mbar_arrive_expect_tx(bar, cb * static_cast<uint32_t>(c.rows));
-  const uint8_t* src =
-      p.mat_w[c.T.m] + static_cast<uint64_t>(c.T.local) * p.row_bytes + static_cast<uint64_t>(c.ch) * kc * 144;
-  for (int r = 0; r < c.rows; ++r)
-    bulk_g2s(dst + r * p.tc_stride, src + static_cast<uint64_t>(r) * p.row_bytes, cb, bar);
+  if (c.rows == kTc1Rows) {
+    // a whole row group: one tensor copy of 16 rows x kc super-blocks (the
+    // super-blocks past the row's end read as zeros and are not used)
+    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(kTc1Rows * kc * 144));
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(&maps.m[c.T.m])), "r"(0), "r"(c.ch * kc),
+        "r"(static_cast<int>(c.T.local)), "r"(smem_u32(bar))
+        : "memory");
+  } else {
+    // a short row group (the end of a matrix or of the CTA's rows): one bulk
+    // copy per row, so no byte past the CTA's rows is read
+    const int nsb = (c.ch + 1) * kc <= sbs ? kc : sbs - c.ch * kc;
+    const uint32_t cb = static_cast<uint32_t>(nsb) * 144u;
+    mbar_arrive_expect_tx(bar, cb * static_cast<uint32_t>(c.rows));
+    const uint8_t* src =
+        p.mat_w[c.T.m] + static_cast<uint64_t>(c.T.local) * p.row_bytes + static_cast<uint64_t>(c.ch) * kc * 144;
+    for (int r = 0; r < c.rows; ++r)
+      bulk_g2s(dst + r * p.tc_stride, src + static_cast<uint64_t>(r) * p.row_bytes, cb, bar);
+  }
   if (++c.ch == p.tc_nchunk) {
     c.ch = 0;
     c.t0 = c.T.t1;
@@ -319,7 +342,8 @@ FRC_DEVICE_INLINE void tc1_issue(const GemvParams& p, Tc1Cursor& c, int64_t c1, 
 }
 
 template <int Q>
-__global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(GemvParams p) {
+__global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(const __grid_constant__ Tc1Maps maps,
+                                                                       GemvParams p) {
   static_assert(Q == kQ4_K, "gemv_tc1 covers Q4_K");
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -371,7 +395,7 @@ __global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(GemvParam
           atomicOr(p.status, kStatusEmptyWaitTimeout);
           break;
         }
-        tc1_issue(p, cur, c1, stages + si * stage_bytes, &full[si]);
+        tc1_issue(p, maps, cur, c1, stages + si * stage_bytes, &full[si]);
       }
       // the last stage-full of copies must land before the CTA may exit
       int zero = 0;
@@ -488,9 +512,8 @@ __global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(GemvParam
   const uint32_t m1 = hi_t ? 0x0F0Fu : 0x3F3Fu, m2 = hi_t ? 0x3030u : 0u;
   // lanes < 12 read their fragment words (stride one super-block), the rest
   // the zero fragment (stride 0)
-  const uint2* xf_lane = lane < kTc1Lanes ? reinterpret_cast<const uint2*>(smem + L.frags) + lane
-                                           : reinterpret_cast<const uint2*>(smem + L.zeros);
-  const int xf_step = lane < kTc1Lanes ? kTc1FragBytes / 8 : 0;
+  const uint32_t xf_lane = lane < kTc1Lanes ? frag_base + static_cast<uint32_t>(lane) * 8u : zero_base;
+  const uint32_t xf_step = lane < kTc1Lanes ? static_cast<uint32_t>(kTc1FragBytes) : 0u;
   const int kc = p.tc_kc;
   const uint32_t stride = static_cast<uint32_t>(p.tc_stride);
   const uint32_t row_lane = smem_u32(stages) + static_cast<uint32_t>(g) * stride + static_cast<uint32_t>(warp) * 144u;
@@ -506,7 +529,7 @@ __global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(GemvParam
       const int sb = ch * kc + warp;
       if (wait_phase(&full[s], ph, abort)) {
         if (sb < sbs) {
-          tc1_q4k_sb(row_lane + static_cast<uint32_t>(s * stage_bytes), stride, xf_lane + sb * xf_step,
+          tc1_q4k_sb(row_lane + static_cast<uint32_t>(s * stage_bytes), stride, xf_lane + static_cast<uint32_t>(sb) * xf_step,
                      sums_s + static_cast<uint32_t>(sb * 32), ldsf(invs_s + 4u * static_cast<uint32_t>(sb)), t, sh,
                      hi_t, m1, m2, p.tc_bias, acc0, acc8, mn0, mn8);
         }

@@ -671,6 +671,23 @@ inline cudaError_t launch_tc1(GemvParams p, const GemvRequest& r, const Tc1Confi
   cudaError_t e = kernel_occupancy(reinterpret_cast<const void*>(gemv_tc1<Q>), r.device, threads, c.smem, &per_sm);
   if (e != cudaSuccess) return e;
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  // one tensor map per matrix: [rows][super-blocks][18 x 8 bytes]
+  Tc1Maps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  auto encode = tensor_map_encoder();
+  if (!encode) return cudaErrorNotSupported;
+  const int sbs = p.k / 256;
+  for (int m = 0; m < p.nmat; ++m) {
+    const int64_t rows = p.mat_end[m] - (m ? p.mat_end[m - 1] : 0);
+    const cuuint64_t dims[3] = {18, static_cast<cuuint64_t>(sbs), static_cast<cuuint64_t>(rows > 0 ? rows : 1)};
+    const cuuint64_t strides[2] = {144, static_cast<cuuint64_t>(p.row_bytes)};
+    const cuuint32_t box[3] = {18, static_cast<cuuint32_t>(c.nw), static_cast<cuuint32_t>(kTc1Rows)};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (encode(&maps.m[m], CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<uint8_t*>(p.mat_w[m]), dims, strides, box,
+               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
   int64_t grid = static_cast<int64_t>(per_sm) * r.sms;
   const int64_t groups = (p.n + kTc1Rows - 1) / kTc1Rows;
   if (grid > groups) grid = groups;
@@ -685,7 +702,7 @@ inline cudaError_t launch_tc1(GemvParams p, const GemvRequest& r, const Tc1Confi
   attr[0].val.programmaticStreamSerializationAllowed = tuned(tuning().pdl, 1) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemv_tc1<Q>, p);
+  return cudaLaunchKernelEx(&cfg, gemv_tc1<Q>, maps, p);
 }
 
 // Largest tile footprint must fit in shared memory with two stages.
