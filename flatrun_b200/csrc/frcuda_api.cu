@@ -580,7 +580,10 @@ int frc_set_option(int option, int value) {
       o.prefill_splits.store(value);
       return FRC_OK;
     case FRC_OPT_INJECT_OOM: o.inject_oom.store(value ? 1 : 0); return FRC_OK;
-    case FRC_OPT_BATCH1_TC: o.batch1_tc.store(value ? 1 : 0); return FRC_OK;
+    case FRC_OPT_BATCH1_TC:
+      if (value < 0 || value > 2) return fail(FRC_ERR_INVALID, "frc_set_option: batch1_tc must be 0, 1 or 2 (got %d)", value);
+      o.batch1_tc.store(value);
+      return FRC_OK;
     default: return fail(FRC_ERR_INVALID, "frc_set_option: unknown option %d", option);
   }
 }
@@ -609,7 +612,7 @@ int frc_batch1_kernel(int quant, int64_t k, int* kind) {
   frc::Tc1Config c;
   if (frc::opt(o.batch1_int16)) {
     *kind = FRC_B1_INT16;
-  } else if (quant == FRC_Q4_K && frc::opt(o.batch1_tc) && frc::tc1_config(static_cast<int>(k), &c)) {
+  } else if (quant == FRC_Q4_K && frc::opt(o.batch1_tc) && frc::tc1_config(static_cast<int>(k), 148, 148, frc::opt(o.batch1_tc) == 2, &c)) {
     *kind = FRC_B1_TENSOR_FP32;
   } else {
     *kind = FRC_B1_CUDA_CORE_FP32;

@@ -89,6 +89,9 @@ struct GemvParams {
   // the pair as its register operand)
   int tc_kc, tc_nchunk, tc_stride;
   uint32_t tc_bias;
+  // gemv_tc1: chunks per part of k (the activation fragments a CTA holds at
+  // a time) and the most rows one CTA owns
+  int tc_part_chunks, tc_rows_max;
 };
 
 constexpr int kMaxMats = 4;

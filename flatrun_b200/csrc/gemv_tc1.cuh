@@ -56,7 +56,9 @@
 // row group the warps' partial sums meet in shared memory and the first 16
 // threads write y.  A producer warp (its lane 0) fills the ring before the
 // grid dependency wait and refills each stage once every compute warp has
-// released it.  All waits are bounded as in the other kernels.
+// released it.  Rows longer than the activation fragments shared memory holds are done in
+// parts of k, the rows' partial sums carried in shared memory and added in
+// order.  All waits are bounded as in the other kernels.
 #pragma once
 
 #include <cuda.h>
@@ -70,25 +72,27 @@ constexpr int kTc1Rows = 16;         // rows per row group: the MMA's M
 constexpr int kTc1MaxWarps = 16;     // compute warps (one super-block each per chunk)
 constexpr int kTc1Lanes = 12;        // lanes of a B fragment that carry x terms
 constexpr int kTc1FragBytes = 16 * kTc1Lanes * 8;  // per super-block: 16 MMAs x 12 lanes x 8 bytes
-constexpr int kTc1Rounds = 2;        // 32-element sub-blocks of x per compute thread, at most
 constexpr int kTc1ZeroBytes = 16 * kTc1Lanes * 8;  // the zero B fragment of lanes >= 12
 
 // Shared-memory layout of gemv_tc1 (host and device).
 struct Tc1Layout {
-  int bars, red, scr, sums, invs, frags, zeros, stages, total;
+  int bars, red, scr, yacc, sums, invs, frags, zeros, stages, total;
 };
 
 __host__ __device__ constexpr int tc1_align(int v, int a) { return (v + a - 1) / a * a; }
 
-__host__ __device__ inline Tc1Layout tc1_layout(int nst, int sbs, int stage_bytes) {
+// psb: super-blocks per part of k (the fragments held at a time); rows:
+// the most rows one CTA owns (partial sums carried across parts).
+__host__ __device__ inline Tc1Layout tc1_layout(int nst, int psb, int rows, int stage_bytes) {
   Tc1Layout L{};
   L.bars = 0;                                        // full[nst], empty[nst], abort and void flags
   L.red = tc1_align(16 * nst + 8, 16);               // [2][kTc1MaxWarps][16] row partials
   L.scr = L.red + 2 * kTc1MaxWarps * kTc1Rows * 4;   // [kTc1MaxWarps] reduction scratch
-  L.sums = L.scr + kTc1MaxWarps * 4;                 // [sbs][8] fp32 sub-block sums of x
-  L.invs = L.sums + sbs * 32;                        // [sbs] 1 / s per super-block
-  L.frags = tc1_align(L.invs + sbs * 4, 128);        // [sbs][16][12] uint2
-  L.zeros = L.frags + sbs * kTc1FragBytes;            // kTc1ZeroBytes of zeros
+  L.yacc = L.scr + kTc1MaxWarps * 4;                 // [rows] partial row sums over parts of k
+  L.sums = tc1_align(L.yacc + rows * 4, 16);         // [psb][8] fp32 sub-block sums of x
+  L.invs = L.sums + psb * 32;                        // [psb] 1 / s per super-block
+  L.frags = tc1_align(L.invs + psb * 4, 128);        // [psb][16][12] uint2
+  L.zeros = L.frags + psb * kTc1FragBytes;           // kTc1ZeroBytes of zeros
   L.stages = tc1_align(L.zeros + kTc1ZeroBytes, 128);
   L.total = L.stages + nst * stage_bytes;
   return L;
@@ -299,18 +303,20 @@ FRC_DEVICE_INLINE void tc1_load_sub(const GemvParams& p, int j, float (&v)[32]) 
   }
 }
 
-// The producer's position in the CTA's tile sequence (row groups of 16 rows,
-// each in nch chunks), and the issue of one tile: one bulk copy per row.
+// The producer's position in the CTA's tile sequence: parts of k outermost,
+// then row groups of 16 rows, then the part's chunks.
 struct Tc1Cursor {
   int64_t t0;  // first row of the current row group
-  Tile T;      // the current row group (valid while ch > 0 or after begin)
+  Tile T;      // the current row group (set when its first chunk is issued)
   int rows;
-  int ch;      // next chunk of the current row group
+  int ch;      // next chunk (index over the whole row)
+  int part;    // current part of k
 };
 
-FRC_DEVICE_INLINE void tc1_issue(const GemvParams& p, const Tc1Maps& maps, Tc1Cursor& c, int64_t c1, uint8_t* dst,
-                                 uint64_t* bar) {
-  if (c.ch == 0) {
+FRC_DEVICE_INLINE void tc1_issue(const GemvParams& p, const Tc1Maps& maps, Tc1Cursor& c, int64_t c0, int64_t c1,
+                                 uint8_t* dst, uint64_t* bar) {
+  const int pc = p.tc_part_chunks;
+  if (c.ch == c.part * pc) {
     c.T = tile_at(p, c.t0, c1, kTc1Rows);
     c.rows = static_cast<int>(c.T.t1 - c.t0);
   }
@@ -335,9 +341,14 @@ FRC_DEVICE_INLINE void tc1_issue(const GemvParams& p, const Tc1Maps& maps, Tc1Cu
     for (int r = 0; r < c.rows; ++r)
       bulk_g2s(dst + r * p.tc_stride, src + static_cast<uint64_t>(r) * p.row_bytes, cb, bar);
   }
-  if (++c.ch == p.tc_nchunk) {
-    c.ch = 0;
+  const int part_end = (c.part + 1) * pc < p.tc_nchunk ? (c.part + 1) * pc : p.tc_nchunk;
+  if (++c.ch == part_end) {  // the row group's share of this part is issued
     c.t0 = c.T.t1;
+    if (c.t0 >= c1) {  // every row group: on to the next part
+      ++c.part;
+      c.t0 = c0;
+    }
+    c.ch = c.part * pc;
   }
 }
 
@@ -353,13 +364,16 @@ __global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(const __g
   const int nst = p.nstage;
   const int sbs = p.k / 256;
   const int stage_bytes = p.stage_stride;
-  const Tc1Layout L = tc1_layout(nst, sbs, stage_bytes);
+  const int kc = p.tc_kc, nch = p.tc_nchunk, pc = p.tc_part_chunks;
+  const int nparts = (nch + pc - 1) / pc;
+  const Tc1Layout L = tc1_layout(nst, pc * kc, p.tc_rows_max, stage_bytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + nst;
   int* abort_flag = reinterpret_cast<int*>(empty + nst);
   int* void_flag = abort_flag + 1;  // an earlier gather's wait ran out
   float* red = reinterpret_cast<float*>(smem + L.red);
   float* scr = reinterpret_cast<float*>(smem + L.scr);
+  float* yacc = reinterpret_cast<float*>(smem + L.yacc);
   float* sums = reinterpret_cast<float*>(smem + L.sums);
   float* invs = reinterpret_cast<float*>(smem + L.invs);
   uint8_t* stages = smem + L.stages;
@@ -378,7 +392,6 @@ __global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(const __g
 
   int64_t c0, c1;
   cta_rows(p.n, c0, c1);
-  const int nch = p.tc_nchunk;
   const int ntiles = count_tiles(p, c0, c1, kTc1Rows) * nch;
 
   if (warp == nw) {
@@ -387,7 +400,7 @@ __global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(const __g
     // (programmatic dependent launch)
     griddep_launch_dependents();
     if (lane == 0) {
-      Tc1Cursor cur{c0, Tile{}, 0, 0};
+      Tc1Cursor cur{c0, Tile{}, 0, 0, 0};
       int issued = 0;
       for (; issued < ntiles; ++issued) {
         const int si = issued % nst;
@@ -395,7 +408,7 @@ __global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(const __g
           atomicOr(p.status, kStatusEmptyWaitTimeout);
           break;
         }
-        tc1_issue(p, maps, cur, c1, stages + si * stage_bytes, &full[si]);
+        tc1_issue(p, maps, cur, c0, c1, stages + si * stage_bytes, &full[si]);
       }
       // the last stage-full of copies must land before the CTA may exit
       int zero = 0;
@@ -431,20 +444,15 @@ __global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(const __g
     if (*reinterpret_cast<volatile int*>(void_flag)) g_world = 1;
   }
 
-  // ---- x fragments: thread ct owns sub-blocks ct, ct + nct, ... ------------
   const int nsub = p.k / 32;
-  const int rounds = (nsub + nct - 1) / nct;  // 1 or 2 (tc1_config)
   float inv_norm = 1.f;
   if (p.x_norm_w) {  // RMSNorm of the whole row of x (qwen2.py:365-378)
     float ss = 0.f;
-    for (int r = 0; r < rounds; ++r) {
-      const int j = ct + r * nct;
-      if (j < nsub) {
-        float v[32];
-        tc1_load_sub(p, j, v);
+    for (int j = ct; j < nsub; j += nct) {
+      float v[32];
+      tc1_load_sub(p, j, v);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) ss = fmaf(v[e], v[e], ss);
-      }
+      for (int e = 0; e < 32; ++e) ss = fmaf(v[e], v[e], ss);
     }
     ss = warp_sum(ss);
     if (lane == 0) scr[warp] = ss;
@@ -453,115 +461,130 @@ __global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(const __g
     for (int w = 0; w < nw; ++w) ss += scr[w];
     inv_norm = 1.0f / sqrtf(ss / static_cast<float>(p.k) + p.x_norm_eps);
   }
-  const uint32_t frag_base = smem_u32(smem + L.frags);
-  for (int r = 0; r < rounds; ++r) {
-    const int j = ct + r * nct;  // sub-block; lanes 8a .. 8a+7 hold one super-block
-    float v[32];
-    if (j < nsub) {
-      tc1_load_sub(p, j, v);
-      if (p.x_norm_w) {
-        const float4* ws = reinterpret_cast<const float4*>(p.x_norm_w + static_cast<int64_t>(j) * 32);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float4 g = __ldg(ws + q);
-          const float gg[4] = {g.x, g.y, g.z, g.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) v[4 * q + e] = (v[4 * q + e] * inv_norm) * gg[e];
-        }
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < 32; ++e) v[e] = 0.f;
-    }
-    float m = 0.f, xsum = 0.f;
-#pragma unroll
-    for (int e = 0; e < 32; ++e) {
-      m = fmaxf(m, fabsf(v[e]));
-      xsum += v[e];
-    }
-    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
-    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
-    if (j < nsub) {
-      float sc, inv;
-      tc1_scale(m, sc, inv);
-      const int sb = j >> 3, jj = j & 7, t = jj >> 1, h = jj & 1;
-      sums[j] = xsum;
-      if (jj == 0) invs[sb] = inv;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        uint32_t p0, p1, p2, q0, q1, q2;
-        split3(v[4 * i] * sc, v[4 * i + 2] * sc, p0, p1, p2);
-        split3(v[4 * i + 1] * sc, v[4 * i + 3] * sc, q0, q1, q2);
-        const uint32_t a = frag_base + static_cast<uint32_t>(((sb * 16 + 2 * i + h) * kTc1Lanes + t) * 8);
-        sts64(a, p0, q0);
-        sts64(a + 32u, p1, q1);
-        sts64(a + 64u, p2, q2);
-      }
-    }
-  }
   // the zero fragment read by lanes >= 12 (columns 3..7 of B)
   const uint32_t zero_base = smem_u32(smem + L.zeros);
   for (int i = ct; i < kTc1ZeroBytes / 8; i += nct) sts64(zero_base + 8u * i, 0u, 0u);
-  named_barrier_sync(1, nct);  // fragments, sums, scales and zeros complete
 
-  // ---- row groups ------------------------------------------------------------
   const int g = lane >> 2, t = lane & 3;
   const bool hi_t = t >= 2;
   const uint32_t sh = static_cast<uint32_t>(t & 1) * 16u;
   const uint32_t m1 = hi_t ? 0x0F0Fu : 0x3F3Fu, m2 = hi_t ? 0x3030u : 0u;
+  const uint32_t frag_base = smem_u32(smem + L.frags);
   // lanes < 12 read their fragment words (stride one super-block), the rest
   // the zero fragment (stride 0)
   const uint32_t xf_lane = lane < kTc1Lanes ? frag_base + static_cast<uint32_t>(lane) * 8u : zero_base;
   const uint32_t xf_step = lane < kTc1Lanes ? static_cast<uint32_t>(kTc1FragBytes) : 0u;
-  const int kc = p.tc_kc;
   const uint32_t stride = static_cast<uint32_t>(p.tc_stride);
   const uint32_t row_lane = smem_u32(stages) + static_cast<uint32_t>(g) * stride + static_cast<uint32_t>(warp) * 144u;
   const uint32_t sums_s = smem_u32(sums), invs_s = smem_u32(invs);
   int s = 0;
   uint32_t ph = 0u;
   int par = 0;
-  for (int64_t t0 = c0; t0 < c1;) {
-    const Tile T = tile_at(p, t0, c1, kTc1Rows);
-    const int rows = static_cast<int>(T.t1 - t0);
-    float acc0 = 0.f, acc8 = 0.f, mn0 = 0.f, mn8 = 0.f;
-    for (int ch = 0; ch < nch; ++ch) {
-      const int sb = ch * kc + warp;
-      if (wait_phase(&full[s], ph, abort)) {
-        if (sb < sbs) {
-          tc1_q4k_sb(row_lane + static_cast<uint32_t>(s * stage_bytes), stride, xf_lane + static_cast<uint32_t>(sb) * xf_step,
-                     sums_s + static_cast<uint32_t>(sb * 32), ldsf(invs_s + 4u * static_cast<uint32_t>(sb)), t, sh,
-                     hi_t, m1, m2, p.tc_bias, acc0, acc8, mn0, mn8);
+  for (int part = 0; part < nparts; ++part) {
+    const int ch0 = part * pc, ch1 = (part + 1) * pc < nch ? (part + 1) * pc : nch;
+    const int sb0 = ch0 * kc, sb1 = ch1 * kc < sbs ? ch1 * kc : sbs;
+    // ---- x fragments of super-blocks [sb0, sb1): thread ct owns sub-blocks
+    // 8 sb0 + ct, + nct, ...; lanes 8a .. 8a+7 hold one super-block.  The
+    // previous part's fragments are free: every warp has passed the barrier
+    // that ended its last row group.
+    for (int j = 8 * sb0 + ct; j < 8 * sb0 + ((8 * (sb1 - sb0) + nct - 1) / nct) * nct; j += nct) {
+      float v[32];
+      if (j < 8 * sb1) {
+        tc1_load_sub(p, j, v);
+        if (p.x_norm_w) {
+          const float4* ws = reinterpret_cast<const float4*>(p.x_norm_w + static_cast<int64_t>(j) * 32);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 gw = __ldg(ws + q);
+            const float gg[4] = {gw.x, gw.y, gw.z, gw.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[4 * q + e] = (v[4 * q + e] * inv_norm) * gg[e];
+          }
         }
-      } else if (lane == 0) {
-        atomicOr(p.status, kStatusFullWaitTimeout);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = 0.f;
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-      if (++s == nst) {
-        s = 0;
-        ph ^= 1u;
+      float m = 0.f, xsum = 0.f;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        m = fmaxf(m, fabsf(v[e]));
+        xsum += v[e];
+      }
+      m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
+      m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
+      m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
+      if (j < 8 * sb1) {
+        float sc, inv;
+        tc1_scale(m, sc, inv);
+        const int lj = j - 8 * sb0, sb = lj >> 3, jj = lj & 7, tt = jj >> 1, h = jj & 1;
+        sums[lj] = xsum;
+        if (jj == 0) invs[sb] = inv;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          uint32_t p0, p1, p2, q0, q1, q2;
+          split3(v[4 * i] * sc, v[4 * i + 2] * sc, p0, p1, p2);
+          split3(v[4 * i + 1] * sc, v[4 * i + 3] * sc, q0, q1, q2);
+          const uint32_t a = frag_base + static_cast<uint32_t>(((sb * 16 + 2 * i + h) * kTc1Lanes + tt) * 8);
+          sts64(a, p0, q0);
+          sts64(a + 32u, p1, q1);
+          sts64(a + 64u, p2, q2);
+        }
       }
     }
-    // rows g and g+8: the four lanes t of a row, then the warps
-    float v0 = acc0 - mn0, v8 = acc8 - mn8;
-    v0 += __shfl_xor_sync(0xFFFFFFFFu, v0, 1);
-    v8 += __shfl_xor_sync(0xFFFFFFFFu, v8, 1);
-    v0 += __shfl_xor_sync(0xFFFFFFFFu, v0, 2);
-    v8 += __shfl_xor_sync(0xFFFFFFFFu, v8, 2);
-    float* rb = red + par * kTc1MaxWarps * kTc1Rows;
-    if (t == 0) {
-      rb[warp * kTc1Rows + g] = v0;
-      rb[warp * kTc1Rows + g + 8] = v8;
+    named_barrier_sync(1, nct);  // fragments, sums, scales (and zeros) complete
+
+    // ---- row groups over this part's chunks ------------------------------
+    for (int64_t t0 = c0; t0 < c1;) {
+      const Tile T = tile_at(p, t0, c1, kTc1Rows);
+      const int rows = static_cast<int>(T.t1 - t0);
+      float acc0 = 0.f, acc8 = 0.f, mn0 = 0.f, mn8 = 0.f;
+      for (int ch = ch0; ch < ch1; ++ch) {
+        const int sb = ch * kc + warp;  // this warp's super-block of the chunk
+        if (wait_phase(&full[s], ph, abort)) {
+          if (sb < sbs) {
+            const uint32_t lsb = static_cast<uint32_t>(sb - sb0);
+            tc1_q4k_sb(row_lane + static_cast<uint32_t>(s * stage_bytes), stride, xf_lane + lsb * xf_step,
+                       sums_s + lsb * 32u, ldsf(invs_s + 4u * lsb), t, sh, hi_t, m1, m2, p.tc_bias, acc0, acc8, mn0,
+                       mn8);
+          }
+        } else if (lane == 0) {
+          atomicOr(p.status, kStatusFullWaitTimeout);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == nst) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+      // rows g and g+8: the four lanes t of a row, then the warps
+      float v0 = acc0 - mn0, v8 = acc8 - mn8;
+      v0 += __shfl_xor_sync(0xFFFFFFFFu, v0, 1);
+      v8 += __shfl_xor_sync(0xFFFFFFFFu, v8, 1);
+      v0 += __shfl_xor_sync(0xFFFFFFFFu, v0, 2);
+      v8 += __shfl_xor_sync(0xFFFFFFFFu, v8, 2);
+      float* rb = red + par * kTc1MaxWarps * kTc1Rows;
+      if (t == 0) {
+        rb[warp * kTc1Rows + g] = v0;
+        rb[warp * kTc1Rows + g + 8] = v8;
+      }
+      named_barrier_sync(1, nct);
+      if (ct < rows) {
+        // parts of k are added in order: ((part 0 + part 1) + part 2) ...
+        float y = 0.f;
+        for (int w = 0; w < nw; ++w) y += rb[w * kTc1Rows + ct];
+        float* acc = yacc + (t0 - c0) + ct;
+        if (part > 0) y = *acc + y;
+        if (part + 1 < nparts) {
+          *acc = y;
+        } else if (!*abort) {
+          put_y(p, g_world, p.mat_y[T.m] + T.local + ct, y);
+        }
+      }
+      par ^= 1;
+      t0 = T.t1;
     }
-    named_barrier_sync(1, nct);
-    if (ct < rows) {
-      float y = 0.f;
-      for (int w = 0; w < nw; ++w) y += rb[w * kTc1Rows + ct];
-      if (!*abort) put_y(p, g_world, p.mat_y[T.m] + T.local + ct, y);
-    }
-    par ^= 1;
-    t0 = T.t1;
   }
   if (g_world > 1) {  // publish this CTA's gathered rows
     named_barrier_sync(1, nct);

@@ -77,7 +77,7 @@ struct Options {
   std::atomic<int> prefill_tc{1};      // FRC_OPT_PREFILL_TC
   std::atomic<int> prefill_splits{0};  // FRC_OPT_PREFILL_SPLITS
   std::atomic<int> inject_oom{0};      // FRC_OPT_INJECT_OOM
-  std::atomic<int> batch1_tc{1};       // FRC_OPT_BATCH1_TC
+  std::atomic<int> batch1_tc{1};       // FRC_OPT_BATCH1_TC (0, 1, 2)
 };
 inline Options& options() {
   static Options o;
@@ -622,15 +622,17 @@ inline cudaError_t launch_gather_wait(const uint32_t* flags, int world, const ui
 
 // Batch-1 tensor-core kernel (gemv_tc1, Q4_K).  Compute warps = super-blocks
 // per chunk: the whole row when it has at most 16 super-blocks, else the
-// largest divisor of the row's super-blocks in [8, 16], else 16; as many
-// stages (up to 8) as shared memory holds beside the activation fragments.
+// largest divisor of the row's super-blocks in [8, 16], else 16.  The
+// activation fragments of as many whole chunks as leave room for 4 stages
+// (else 3, else 2) are held at a time (a part of k); then as many stages as
+// fit, up to 8.
 struct Tc1Config {
-  int nw = 0, nch = 0, stride = 0, stage_bytes = 0, nst = 0;
+  int nw = 0, nch = 0, stride = 0, stage_bytes = 0, nst = 0, part_chunks = 0, rows_max = 0;
   size_t smem = 0;
 };
 
-inline bool tc1_config(int k, Tc1Config* c) {
-  if (k % 256 != 0 || k <= 0) return false;
+inline bool tc1_config(int k, int64_t n, int grid, bool long_rows, Tc1Config* c) {
+  if (k % 256 != 0 || k <= 0 || grid < 1) return false;
   const int sbs = k / 256;
   int nw = 0;
   if (sbs <= kTc1MaxWarps) {
@@ -642,20 +644,47 @@ inline bool tc1_config(int k, Tc1Config* c) {
   }
   const int forced = tuning().nwarps;
   if (forced >= 1 && forced <= kTc1MaxWarps) nw = forced;
-  if (k / 32 > kTc1Rounds * 32 * nw) return false;  // x longer than the prologue covers
   c->nw = nw;
   c->nch = (sbs + nw - 1) / nw;
   c->stride = tc1_row_stride(nw);
   c->stage_bytes = round_up(kTc1Rows * c->stride, 128);
+  const int64_t rows_max = (n + grid - 1) / grid;
+  if (rows_max > (1 << 20)) return false;
+  c->rows_max = static_cast<int>(rows_max);
   const int budget = tuned(tuning().smem_bytes, kSmemBudget);
-  int nst = tuning().nstage > 0 ? tuning().nstage : 8;
-  for (; nst >= 2; --nst) {
-    if (tc1_layout(nst, sbs, c->stage_bytes).total <= budget) break;
+  int pc = 0;
+  for (int want = 4; want >= 2 && !pc; --want) {
+    for (int q = c->nch; q >= 1; --q) {
+      if (tc1_layout(want, q * nw, c->rows_max, c->stage_bytes).total <= budget) {
+        pc = q;
+        break;
+      }
+    }
   }
+  if (!pc) return false;
+  // rows longer than one part of k (the down projections of the models
+  // measured, k = 18944 and 28672) rebuild the fragments per part while the
+  // ring drains: measured on B200 at or below the CUDA-core kernel there
+  // (Llama-3-70B down 48.6 against 47.0 us, Qwen2-7B down 21.0 against 20.5),
+  // so they stay on it unless long_rows (FRC_OPT_BATCH1_TC = 2)
+  if (pc < c->nch && !long_rows) return false;
+  const int forced_nst = tuning().nstage;
+  int nst = forced_nst > 0 ? forced_nst : 8;
+  for (; nst >= 2; --nst)
+    if (tc1_layout(nst, pc * nw, c->rows_max, c->stage_bytes).total <= budget) break;
   if (nst < 2) return false;
+  c->part_chunks = pc;
   c->nst = nst;
-  c->smem = static_cast<size_t>(tc1_layout(nst, sbs, c->stage_bytes).total);
+  c->smem = static_cast<size_t>(tc1_layout(nst, pc * nw, c->rows_max, c->stage_bytes).total);
   return true;
+}
+
+// CTAs of a batch-1 tensor-core launch of n rows (one per SM, at least one
+// row group each).
+inline int tc1_grid(int64_t n, int sms) {
+  int64_t g = (n + kTc1Rows - 1) / kTc1Rows;
+  if (g > sms) g = sms;
+  return g < 1 ? 1 : static_cast<int>(g);
 }
 
 template <int Q>
@@ -664,6 +693,8 @@ inline cudaError_t launch_tc1(GemvParams p, const GemvRequest& r, const Tc1Confi
   p.tc_nchunk = c.nch;
   p.tc_stride = c.stride;
   p.tc_bias = kH2Bias;
+  p.tc_part_chunks = c.part_chunks;
+  p.tc_rows_max = c.rows_max;
   p.stage_stride = c.stage_bytes;
   p.nstage = c.nst;
   const int threads = (c.nw + 1) * 32;
@@ -688,10 +719,7 @@ inline cudaError_t launch_tc1(GemvParams p, const GemvRequest& r, const Tc1Confi
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
-  int64_t grid = static_cast<int64_t>(per_sm) * r.sms;
-  const int64_t groups = (p.n + kTc1Rows - 1) / kTc1Rows;
-  if (grid > groups) grid = groups;
-  if (grid < 1) grid = 1;
+  const int grid = tc1_grid(p.n, r.sms);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(threads);
@@ -769,7 +797,8 @@ cudaError_t launch_gemv(const GemvRequest& r) {
     b1.units = (r.k / F::QK) * I8<Q>::UPB;
     if constexpr (Q == kQ4_K) {
       Tc1Config c;
-      if (!opt(options().batch1_int16) && opt(options().batch1_tc) && tc1_config(r.k, &c))
+      if (!opt(options().batch1_int16) && opt(options().batch1_tc) &&
+          tc1_config(r.k, b1.n, tc1_grid(b1.n, r.sms), opt(options().batch1_tc) == 2, &c))
         return launch_tc1<Q>(b1, r, c);
     }
     const cudaError_t e =

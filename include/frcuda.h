@@ -100,8 +100,10 @@ int frc_device_status(int device, uint32_t* flags);
  *  FRC_OPT_BATCH1_TC      1 (default): batch-1 Q4_K with x in fp32 runs on the
  *                         tensor cores (weights as exact fp16 integers q * sc,
  *                         x as an exact sum of three fp16 terms, fp32
- *                         accumulation) where the row fits its shared-memory
- *                         layout; 0: on the CUDA-core fp32 kernel. */
+ *                         accumulation) where the whole row's activation
+ *                         fragments fit in shared memory (k <= 16384 at 16
+ *                         warps); 2: longer rows too, in parts of k; 0: on
+ *                         the CUDA-core fp32 kernel. */
 #define FRC_OPT_BATCH1_INT16   1
 #define FRC_OPT_BATCHED_FP32   2
 #define FRC_OPT_PREFILL_TC     3

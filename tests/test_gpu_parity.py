@@ -328,24 +328,26 @@ def test_batch1_activation_outliers(cuda_backend, fmt, int16):
 
 # Q4_K batch-1 shapes for the tensor-core kernel: one super-block, odd (9)
 # and even super-block counts per chunk, two chunks (5120: 10 warps; 8192:
-# 16), a ragged last chunk (18944: 74 super-blocks, chunks of 16), ragged
-# row groups (1, 15, 17, 33, 37 rows), and a row too long for the shared-
-# memory fragments (36864: falls back to the CUDA-core kernel)
+# 16), ragged row groups (1, 15, 17, 33, 37 rows), and rows longer than one
+# part of k (18944: 74 super-blocks, chunks of 16 with a ragged last one, in
+# two parts; 36864: three parts), which batch1_tc = 2 runs on the tensor
+# cores and the default leaves on the CUDA-core kernel
 TC1_SHAPES = [(1, 256), (15, 512), (16, 2304), (17, 3584), (33, 4096), (300, 5120), (100, 8192), (37, 18944),
               (64, 36864)]
 
 
 @pytest.mark.parametrize("n,k", TC1_SHAPES)
 def test_batch1_tensor_core_q4k(cuda_backend, n, k):
-    """Q4_K batch 1 on the tensor-core kernel (default: weights as exact fp16
-    integers, x as an exact sum of three fp16 terms, fp32 accumulation) and on
-    the CUDA-core fp32 kernel (batch1_tc = 0): both within the fp32 tolerance
-    of fp64, normalised by the term magnitude (few rows can cancel)."""
+    """Q4_K batch 1 on the tensor-core kernel (weights as exact fp16 integers,
+    x as an exact sum of three fp16 terms, fp32 accumulation; batch1_tc = 1
+    and 2) and on the CUDA-core fp32 kernel (batch1_tc = 0): each within the
+    fp32 tolerance of fp64, normalised by the term magnitude (few rows can
+    cancel)."""
     raw = synth.make_weight("Q4_K", n, k, seed=k + n)
     x = synth.make_x(k, seed=k - n)
     ref = O.matvec_fp64("Q4_K", raw, x, n, k)
     scale = O.term_scale("Q4_K", raw, x, n, k)
-    for tc in (1, 0):
+    for tc in (1, 2, 0):
         with _lib.option("batch1_tc", tc):
             y = cuda_backend.weight(raw, n, k, "Q4_K").matmul(x)
         assert O.norm_err(y, ref, scale) < 5e-6, (n, k, tc)
