@@ -43,7 +43,8 @@
 //   * B: lane 4T + t (T = 0, 1, 2: hi, mid, lo) holds term T of the x values
 //     of the k-slots above; the other lanes hold zeros.  These fragments are
 //     the same for every row, so each CTA builds them once per launch in
-//     shared memory (6 bytes per element), indexed [super-block][MMA][lane].
+//     shared memory (6 bytes per element), indexed [super-block][word i]
+//     [lane][MMA 2i, 2i+1] so a lane reads both of a word's fragments at once.
 //   * C: thread t = 0 holds the hi and mid sums, t = 1 the lo sum (and a
 //     zero column), t = 2, 3 zeros; the four lanes of a row are summed at
 //     the end of the row group.
@@ -136,6 +137,19 @@ FRC_DEVICE_INLINE void mma_f16_16816(float (&c)[4], uint32_t a0, uint32_t a1, ui
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+// d = a b (the accumulator starts at zero)
+FRC_DEVICE_INLINE void mma_f16_16816_z(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
+}
+FRC_DEVICE_INLINE uint4 lds128u(uint32_t a) {
+  uint4 v;
+  asm("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
 FRC_DEVICE_INLINE uint2 lds64(uint32_t a) {
   uint2 v;
   asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
@@ -189,8 +203,8 @@ FRC_DEVICE_INLINE void tc1_q4k_scales(const uint4& h, uint32_t sh, bool hi_t, ui
 
 // One super-block of a 16-row group for this warp.  row: shared address of
 // row g's block; xf: shared address of this lane's B fragment words for the
-// super-block (lanes >= 12 point at a zero fragment), fragment m at xf + 96 m;
-// sums: the super-block's 8 sub-block sums.
+// super-block (lanes >= 12 point at a zero fragment), fragments 2i and 2i + 1
+// at xf + 192 i; sums: the super-block's 8 sub-block sums.
 FRC_DEVICE_INLINE void tc1_q4k_sb(uint32_t row, uint32_t stride, uint32_t xf, uint32_t sums, float inv_s,
                                   int t, uint32_t sh, bool hi_t, uint32_t m1, uint32_t m2, uint32_t bias, float& acc0,
                                   float& acc8, float& mn0, float& mn8) {
@@ -211,7 +225,9 @@ FRC_DEVICE_INLINE void tc1_q4k_sb(uint32_t row, uint32_t stride, uint32_t xf, ui
   const uint32_t sg8 = hfma2_u(prmt(sc8, kH2Bias, 0x7151), kH2Sixteenth, kH2Neg64);
   const uint32_t ng8 = hmul2_u(sg8, kH2Neg1024);
 
-  float cl[4] = {0.f, 0.f, 0.f, 0.f}, ch[4] = {0.f, 0.f, 0.f, 0.f};
+  // one accumulator over the super-block's 16 MMAs (the first starts it at
+  // zero): low nibbles (sub-block 2t) and high nibbles (2t + 1) of each word
+  float c[4];
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     // words 4 half .. 4 half + 3 of chunk t in rows g and g + 8
@@ -224,20 +240,24 @@ FRC_DEVICE_INLINE void tc1_q4k_sb(uint32_t row, uint32_t stride, uint32_t xf, ui
       const int i = 4 * half + j;
       const uint32_t x0 = w0[j], x8 = w8[j];
       const uint32_t s0 = x0 >> 8, s8 = x8 >> 8;
-      const uint2 bl0 = lds64(xf + static_cast<uint32_t>(2 * i * kTc1Lanes * 8)),
-                  bh0 = lds64(xf + static_cast<uint32_t>((2 * i + 1) * kTc1Lanes * 8));
-      mma_f16_16816(cl, hfma2_u((x0 & 0x000F000Fu) | bias, sl0, nl0), hfma2_u((x8 & 0x000F000Fu) | bias, sl8, nl8),
-                    hfma2_u((s0 & 0x000F000Fu) | bias, sl0, nl0), hfma2_u((s8 & 0x000F000Fu) | bias, sl8, nl8), bl0.x,
-                    bl0.y);
-      mma_f16_16816(ch, hfma2_u((x0 & 0x00F000F0u) | bias, sg0, ng0), hfma2_u((x8 & 0x00F000F0u) | bias, sg8, ng8),
-                    hfma2_u((s0 & 0x00F000F0u) | bias, sg0, ng0), hfma2_u((s8 & 0x00F000F0u) | bias, sg8, ng8), bh0.x,
-                    bh0.y);
+      // B fragments of MMAs 2i (low) and 2i + 1 (high), side by side
+      const uint4 b = lds128u(xf + static_cast<uint32_t>(i * kTc1Lanes * 16));
+      const uint32_t l0 = hfma2_u((x0 & 0x000F000Fu) | bias, sl0, nl0), l1 = hfma2_u((x8 & 0x000F000Fu) | bias, sl8, nl8);
+      const uint32_t l2 = hfma2_u((s0 & 0x000F000Fu) | bias, sl0, nl0), l3 = hfma2_u((s8 & 0x000F000Fu) | bias, sl8, nl8);
+      if (i == 0) {
+        mma_f16_16816_z(c, l0, l1, l2, l3, b.x, b.y);
+      } else {
+        mma_f16_16816(c, l0, l1, l2, l3, b.x, b.y);
+      }
+      mma_f16_16816(c, hfma2_u((x0 & 0x00F000F0u) | bias, sg0, ng0), hfma2_u((x8 & 0x00F000F0u) | bias, sg8, ng8),
+                    hfma2_u((s0 & 0x00F000F0u) | bias, sg0, ng0), hfma2_u((s8 & 0x00F000F0u) | bias, sg8, ng8), b.z,
+                    b.w);
     }
   }
   // columns 2t, 2t+1 of rows g and g+8: (hi, mid) for t = 0, (lo, 0) for
   // t = 1, zeros beyond
-  const float s_0 = (cl[0] + ch[0]) + (cl[1] + ch[1]);
-  const float s_8 = (cl[2] + ch[2]) + (cl[3] + ch[3]);
+  const float s_0 = c[0] + c[1];
+  const float s_8 = c[2] + c[3];
   const float d0 = half_bits_to_float(h0.x), dm0 = half_bits_to_float(h0.x >> 16);
   const float d8 = half_bits_to_float(h8.x), dm8 = half_bits_to_float(h8.x >> 16);
   acc0 = fmaf(d0 * inv_s, s_0, acc0);
@@ -472,7 +492,7 @@ __global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(const __g
   const uint32_t frag_base = smem_u32(smem + L.frags);
   // lanes < 12 read their fragment words (stride one super-block), the rest
   // the zero fragment (stride 0)
-  const uint32_t xf_lane = lane < kTc1Lanes ? frag_base + static_cast<uint32_t>(lane) * 8u : zero_base;
+  const uint32_t xf_lane = lane < kTc1Lanes ? frag_base + static_cast<uint32_t>(lane) * 16u : zero_base;
   const uint32_t xf_step = lane < kTc1Lanes ? static_cast<uint32_t>(kTc1FragBytes) : 0u;
   const uint32_t stride = static_cast<uint32_t>(p.tc_stride);
   const uint32_t row_lane = smem_u32(stages) + static_cast<uint32_t>(g) * stride + static_cast<uint32_t>(warp) * 144u;
@@ -525,10 +545,10 @@ __global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(const __g
           uint32_t p0, p1, p2, q0, q1, q2;
           split3(v[4 * i] * sc, v[4 * i + 2] * sc, p0, p1, p2);
           split3(v[4 * i + 1] * sc, v[4 * i + 3] * sc, q0, q1, q2);
-          const uint32_t a = frag_base + static_cast<uint32_t>(((sb * 16 + 2 * i + h) * kTc1Lanes + tt) * 8);
+          const uint32_t a = frag_base + static_cast<uint32_t>(((sb * 8 + i) * kTc1Lanes + tt) * 16 + h * 8);
           sts64(a, p0, q0);
-          sts64(a + 32u, p1, q1);
-          sts64(a + 64u, p2, q2);
+          sts64(a + 64u, p1, q1);
+          sts64(a + 128u, p2, q2);
         }
       }
     }
