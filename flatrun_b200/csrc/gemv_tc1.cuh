@@ -590,16 +590,25 @@ __global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(const __g
         rb[warp * kTc1Rows + g + 8] = v8;
       }
       named_barrier_sync(1, nct);
-      if (ct < rows) {
-        // parts of k are added in order: ((part 0 + part 1) + part 2) ...
-        float y = 0.f;
-        for (int w = 0; w < nw; ++w) y += rb[w * kTc1Rows + ct];
-        float* acc = yacc + (t0 - c0) + ct;
-        if (part > 0) y = *acc + y;
-        if (part + 1 < nparts) {
-          *acc = y;
-        } else if (!*abort) {
-          put_y(p, g_world, p.mat_y[T.m] + T.local + ct, y);
+      if (warp == 0) {
+        // lane l adds the partials of row l & 15 from warps 8 (l >> 4) ..
+        // 8 (l >> 4) + 7 (independent loads), then the two halves meet:
+        // the same order for every row and every launch
+        const int r = lane & 15, w0 = 8 * (lane >> 4);
+        float h = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) h += w0 + w < nw ? rb[(w0 + w) * kTc1Rows + r] : 0.f;
+        h += __shfl_xor_sync(0xFFFFFFFFu, h, 16);
+        if (lane < rows) {
+          // parts of k are added in order: ((part 0 + part 1) + part 2) ...
+          float y = h;
+          float* acc = yacc + (t0 - c0) + lane;
+          if (part > 0) y = *acc + y;
+          if (part + 1 < nparts) {
+            *acc = y;
+          } else if (!*abort) {
+            put_y(p, g_world, p.mat_y[T.m] + T.local + lane, y);
+          }
         }
       }
       par ^= 1;

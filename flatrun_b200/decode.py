@@ -65,10 +65,10 @@ def rope_tables(head_dim: int, theta: float, max_pos: int) -> tuple[np.ndarray, 
 class DecodeEngine:
     """Greedy decode of one sequence with every weight and the KV cache in HBM.
 
-    `weights` maps the reference's tensor names to host arrays: raw GGUF
-    block bytes (uint8, with `quant_of(name)` -> (n, k, quant)) for the
-    projections and the head, fp32 arrays for norms, biases and an fp32
-    embedding table (or raw bytes with its quant).  `kv_prefill` optionally
+    `weights` maps the reference's tensor names to host arrays or device
+    tensors: raw GGUF block bytes (uint8, with `quant_of(name)` -> (n, k,
+    quant)) for the projections and the head, fp32 arrays for norms, biases
+    and an fp32 embedding table (or raw bytes with its quant).  `kv_prefill` optionally
     maps a layer to (keys, values) of shape (positions, kv_heads, head_dim)
     already in the cache before the first token.
     """
@@ -87,36 +87,41 @@ class DecodeEngine:
         hd, kvd = c.head_dim, c.kv_heads * c.head_dim
         f32 = torch.float32
 
-        def up(a):
-            return torch.from_numpy(np.ascontiguousarray(a)).to(self._dev)
+        def up(a, dtype):
+            # host arrays are copied in; device tensors (a streamed GGUF
+            # file, gguf_stream.load_decoder) are used where they are
+            if isinstance(a, torch.Tensor):
+                return a.to(self._dev).reshape(-1).view(torch.uint8) if dtype is np.uint8 \
+                    else a.to(self._dev, torch.float32)
+            a = np.asarray(a, dtype)
+            return torch.from_numpy(np.ascontiguousarray(a.reshape(-1) if dtype is np.uint8 else a)).to(self._dev)
 
         self._w = {}  # name -> (device tensor, quant id, n, k)
         for name, arr in weights.items():
             q = quant_of(name)
             if q is not None:
                 n, k, quant = q
-                self._w[name] = (up(np.asarray(arr, np.uint8).reshape(-1)), _lib.QUANT_IDS[quant], n, k)
-        self._norm = {name: up(np.asarray(a, np.float32)) for name, a in weights.items()
-                      if name.endswith("norm.weight")}
+                self._w[name] = (up(arr, np.uint8), _lib.QUANT_IDS[quant], n, k)
+        self._norm = {name: up(a, np.float32) for name, a in weights.items() if name.endswith("norm.weight")}
         self._bias = {}
         for i in range(c.layers):
             p = f"model.layers.{i}.self_attn"
             if f"{p}.q_proj.bias" in weights:
-                self._bias[i] = up(np.concatenate([np.asarray(weights[f"{p}.{n}.bias"], np.float32)
-                                                   for n in ("q_proj", "k_proj", "v_proj")]))
+                self._bias[i] = torch.cat([up(weights[f"{p}.{n}.bias"], np.float32).reshape(-1)
+                                           for n in ("q_proj", "k_proj", "v_proj")])
         emb = weights["model.embed_tokens.weight"]
         eq = quant_of("model.embed_tokens.weight")
         self._emb_quant = 0 if eq is None else _lib.QUANT_IDS[eq[2]]
-        self._emb = up(np.asarray(emb, np.float32) if eq is None else np.asarray(emb, np.uint8).reshape(-1))
+        self._emb = up(emb, np.float32 if eq is None else np.uint8)
         cos, sin = rope_tables(hd, c.rope_theta, c.max_pos)
-        self._cos, self._sin = up(cos), up(sin)
+        self._cos, self._sin = up(cos, np.float32), up(sin, np.float32)
         self.k_cache = [torch.zeros((c.max_pos, c.kv_heads, hd), dtype=f32, device=self._dev) for _ in range(c.layers)]
         self.v_cache = [torch.zeros((c.max_pos, c.kv_heads, hd), dtype=f32, device=self._dev) for _ in range(c.layers)]
         start = 0
         for i, (kp, vp) in (kv_prefill or {}).items():
             t = kp.shape[0]
-            self.k_cache[i][:t] = up(kp)
-            self.v_cache[i][:t] = up(vp)
+            self.k_cache[i][:t] = up(kp, np.float32).reshape(kp.shape)
+            self.v_cache[i][:t] = up(vp, np.float32).reshape(vp.shape)
             start = t
         self.pos = torch.tensor([start], dtype=torch.int32, device=self._dev)
         self.tok_in = torch.zeros(1, dtype=torch.int32, device=self._dev)
