@@ -23,7 +23,12 @@ value  = algorithmic bytes (weights + x + y) per step / device time per step,
 e2e    = the same metric through the public call a user makes,
          CudaBackend.matmul_q4k(x, weight, n, k) with x in pinned host memory:
          x host->device, kernel, y device->host and a synchronise per call
-         (N = 1).
+         (N > 1: each rank its own shard, the slowest rank's time).
+kernels: batch-1 Q4_K on gemv_tc1 (x in fp32 as three exact fp16 terms,
+         weights as exact fp16 q*sc, products on the tensor cores, fp32
+         accumulation) where the row's activation fragments fit in shared
+         memory, else (and for the other formats) the fp32 CUDA-core gemv_b1;
+         --cuda-core forces the latter for Q4_K too.
 roofline: achieved GB/s of the dominant launch (the one carrying the most
          bytes: gate+up for the layer workloads) from K back-to-back launches
          timed with CUDA events, against the measured copy bandwidth in
@@ -858,9 +863,11 @@ def main() -> None:
     peak, peak_src = peaks()
     traffic = ncu_traffic(args.workload)
 
-    # e2e through the public call, host buffers (pinned x), synchronous calls
+    # e2e through the public call, host buffers (pinned x), synchronous calls;
+    # under --gpus N every rank runs its own shard's calls (the same number
+    # of steps on every rank) and the slowest rank's time counts
     e2e = None
-    if not args.no_e2e and world == 1:
+    if not args.no_e2e:
         method = {"Q4_K": be.matmul_q4k, "Q6_K": be.matmul_q6k, "Q8_0": be.matmul_q8_0,
                   "Q5_K": be.matmul_q5k, "Q1_0": be.matmul_q1_0}
         pinned = []
@@ -873,17 +880,25 @@ def main() -> None:
             for i, (_, q, n, k, _) in enumerate(mats):
                 method[q](pinned[i], host_arrays[s % copies][i], n, k)
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         t0 = time.perf_counter()
         for s in range(e2e_steps):
             for i, (_, q, n, k, _) in enumerate(mats):
                 method[q](pinned[i], host_arrays[s % copies][i], n, k)
         t_e2e = (time.perf_counter() - t0) / e2e_steps
-        e2e = {"value": round(step_bytes / t_e2e / 1e9, 2), "unit": UNIT,
-               "h2d_bytes_per_step": sum(batch * k * 4 for _, _, _, k, _ in mats),
-               "d2h_bytes_per_step": sum(batch * n * 4 for _, _, n, _, _ in mats),
+        if world > 1:
+            t = torch.tensor([t_e2e], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            t_e2e = float(t.item())
+        e2e = {"value": round(step_bytes * world / t_e2e / 1e9, 2), "unit": UNIT,
+               "h2d_bytes_per_step": world * sum(batch * k * 4 for _, _, _, k, _ in mats),
+               "d2h_bytes_per_step": world * sum(batch * n * 4 for _, _, n, _, _ in mats),
                "ms_per_step": round(t_e2e * 1e3, 4), "steps": e2e_steps,
                "tokens_per_s": round(1.0 / t_e2e, 2) if args.workload.startswith("decode") else None,
-               "timer": "host wall clock over synchronous calls (each call copies x in, y out and synchronises)"}
+               "timer": ("host wall clock over synchronous calls (each call copies x in, y out and synchronises)"
+                         + ("; each rank its own row shard, the slowest rank's time; y shards stay on their ranks"
+                            if world > 1 else ""))}
 
     # CPU baselines (rank 0 at N = 1 only): the reference's native C++ path
     # and its NumPy path, each on a bounded sample of the same workload
