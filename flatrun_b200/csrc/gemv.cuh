@@ -92,6 +92,7 @@ struct GemvParams {
   // gemv_tc1: chunks per part of k (the activation fragments a CTA holds at
   // a time) and the most rows one CTA owns
   int tc_part_chunks, tc_rows_max;
+  int tc_rg;  // gemv_tc1: rows per row group (16 per MMA tile of a warp)
 };
 
 constexpr int kMaxMats = 4;

@@ -31,7 +31,7 @@
 // and a single-thread issue per tile.
 //
 // Operand layout (m16n8k16, thread (g = lane / 4, t = lane % 4)):
-//   * A: rows g and g + 8 of a 16-row group; thread t converts quant bytes
+//   * A: rows g and g + 8 of a 16-row MMA tile; thread t converts quant bytes
 //     [32t, 32t + 32) of each super-block's qs (its chunk t: low nibbles are
 //     sub-block 2t, high nibbles sub-block 2t + 1).  Word i of the chunk gives
 //     two MMAs: low nibbles (bytes 0, 2 -> k-slots 2t, 2t+1; bytes 1, 3 ->
@@ -50,16 +50,18 @@
 //     the end of the row group.
 //
 // Work split: each CTA owns rows [c0, c1) (balanced to one row), in row
-// groups of 16 (clipped at matrix ends).  A row group is streamed in chunks
+// groups of 16 MT rows (clipped at matrix ends; MT = 2 MMA tiles per warp by
+// default, which share each B fragment).  A row group is streamed in chunks
 // of NW super-blocks (one per warp): one 3-D tensor copy (TMA, no multicast)
-// of 16 rows x NW super-blocks per tile, or, for a short row group, one bulk
-// copy per row.  Warp w takes super-block w of every chunk; at the end of a
-// row group the warps' partial sums meet in shared memory and the first 16
-// threads write y.  A producer warp (its lane 0) fills the ring before the
-// grid dependency wait and refills each stage once every compute warp has
-// released it.  Rows longer than the activation fragments shared memory holds are done in
-// parts of k, the rows' partial sums carried in shared memory and added in
-// order.  All waits are bounded as in the other kernels.
+// of 16 MT rows x NW super-blocks per tile, or, for a short row group, one
+// bulk copy per row.  Warp w takes super-block w of every chunk for all the
+// group's rows; at the end of a row group the warps' partial sums meet in
+// shared memory and warp 0 writes y.  A producer warp (its lane 0) fills the
+// ring before the grid dependency wait and refills each stage once every
+// compute warp has released it.  Rows longer than the activation fragments
+// shared memory holds are done in parts of k, the rows' partial sums carried
+// in shared memory and added in order.  All waits are bounded as in the
+// other kernels.
 #pragma once
 
 #include <cuda.h>
@@ -69,7 +71,8 @@
 
 namespace frc {
 
-constexpr int kTc1Rows = 16;         // rows per row group: the MMA's M
+constexpr int kTc1Rows = 16;         // rows of one MMA tile (the MMA's M)
+constexpr int kTc1MaxRows = 32;      // rows per row group, at most (two MMA tiles per warp)
 constexpr int kTc1MaxWarps = 16;     // compute warps (one super-block each per chunk)
 constexpr int kTc1Lanes = 12;        // lanes of a B fragment that carry x terms
 constexpr int kTc1FragBytes = 16 * kTc1Lanes * 8;  // per super-block: 16 MMAs x 12 lanes x 8 bytes
@@ -87,8 +90,8 @@ __host__ __device__ constexpr int tc1_align(int v, int a) { return (v + a - 1) /
 __host__ __device__ inline Tc1Layout tc1_layout(int nst, int psb, int rows, int stage_bytes) {
   Tc1Layout L{};
   L.bars = 0;                                        // full[nst], empty[nst], abort and void flags
-  L.red = tc1_align(16 * nst + 8, 16);               // [2][kTc1MaxWarps][16] row partials
-  L.scr = L.red + 2 * kTc1MaxWarps * kTc1Rows * 4;   // [kTc1MaxWarps] reduction scratch
+  L.red = tc1_align(16 * nst + 8, 16);               // [2][kTc1MaxWarps][row group] row partials
+  L.scr = L.red + 2 * kTc1MaxWarps * kTc1MaxRows * 4;  // [kTc1MaxWarps] reduction scratch
   L.yacc = L.scr + kTc1MaxWarps * 4;                 // [rows] partial row sums over parts of k
   L.sums = tc1_align(L.yacc + rows * 4, 16);         // [psb][8] fp32 sub-block sums of x
   L.invs = L.sums + psb * 32;                        // [psb] 1 / s per super-block
@@ -201,93 +204,95 @@ FRC_DEVICE_INLINE void tc1_q4k_scales(const uint4& h, uint32_t sh, bool hi_t, ui
   mn = (x2 & m1) | ((b >> 2) & m2);
 }
 
-// One super-block of a 16-row group for this warp.  row: shared address of
-// row g's block; xf: shared address of this lane's B fragment words for the
-// super-block (lanes >= 12 point at a zero fragment), fragments 2i and 2i + 1
-// at xf + 192 i; sums: the super-block's 8 sub-block sums.
-FRC_DEVICE_INLINE void tc1_q4k_sb(uint32_t row, uint32_t stride, uint32_t xf, uint32_t sums, float inv_s,
-                                  int t, uint32_t sh, bool hi_t, uint32_t m1, uint32_t m2, uint32_t bias, float& acc0,
-                                  float& acc8, float& mn0, float& mn8) {
-  const uint32_t row8 = row + 8u * stride;
-  const uint4 h0 = lds128<0>(row), h8 = lds128<0>(row8);
-  const uint32_t q0 = row + 16u + 32u * static_cast<uint32_t>(t), q8 = row8 + 16u + 32u * static_cast<uint32_t>(t);
-  uint32_t sc0, mnw0, sc8, mnw8;
-  tc1_q4k_scales(h0, sh, hi_t, m1, m2, sc0, mnw0);
-  tc1_q4k_scales(h8, sh, hi_t, m1, m2, sc8, mnw8);
-  // (sc, sc) of the low sub-block, and (sc/16, sc/16) of the high one, with
-  // their bias terms -1024 sc and -64 sc
-  const uint32_t sl0 = hadd2_u(prmt(sc0, kH2Bias, 0x7050), kH2Neg1024);
-  const uint32_t nl0 = hmul2_u(sl0, kH2Neg1024);
-  const uint32_t sg0 = hfma2_u(prmt(sc0, kH2Bias, 0x7151), kH2Sixteenth, kH2Neg64);
-  const uint32_t ng0 = hmul2_u(sg0, kH2Neg1024);
-  const uint32_t sl8 = hadd2_u(prmt(sc8, kH2Bias, 0x7050), kH2Neg1024);
-  const uint32_t nl8 = hmul2_u(sl8, kH2Neg1024);
-  const uint32_t sg8 = hfma2_u(prmt(sc8, kH2Bias, 0x7151), kH2Sixteenth, kH2Neg64);
-  const uint32_t ng8 = hmul2_u(sg8, kH2Neg1024);
-
-  // one accumulator over the super-block's 16 MMAs (the first starts it at
-  // zero): low nibbles (sub-block 2t) and high nibbles (2t + 1) of each word
-  float c[4];
+// One super-block of MT 16-row MMA tiles for this warp (rows g + 16 m and
+// g + 8 + 16 m of the row group, m < MT; the tiles share the B fragments).
+// row: shared address of row g's block; xf: shared address of this lane's
+// B fragment words for the super-block (lanes >= 12 point at a zero
+// fragment), fragments 2i and 2i + 1 at xf + 192 i; sums: the super-block's
+// 8 sub-block sums.  acc[2m], acc[2m+1] (rows g + 16 m, g + 8 + 16 m) gain
+// d / s times the column sums; mn[...] gain dmin times the min terms.
+template <int MT>
+FRC_DEVICE_INLINE void tc1_q4k_sb(uint32_t row, uint32_t stride, uint32_t xf, uint32_t sums, float inv_s, int t,
+                                  uint32_t sh, bool hi_t, uint32_t m1, uint32_t m2, uint32_t bias, float (&acc)[2 * MT],
+                                  float (&mn)[2 * MT]) {
+  constexpr int R = 2 * MT;  // rows of this thread
+  uint4 hd[R];
+  uint32_t q[R], sl[R], nl[R], sg[R], ng[R], mw[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const uint32_t ra = row + static_cast<uint32_t>(8 * r) * stride;  // rows g, g + 8, g + 16, g + 24
+    hd[r] = lds128<0>(ra);
+    q[r] = ra + 16u + 32u * static_cast<uint32_t>(t);
+    uint32_t sc;
+    tc1_q4k_scales(hd[r], sh, hi_t, m1, m2, sc, mw[r]);
+    // (sc, sc) of the low sub-block, and (sc/16, sc/16) of the high one,
+    // with their bias terms -1024 sc and -64 sc
+    sl[r] = hadd2_u(prmt(sc, kH2Bias, 0x7050), kH2Neg1024);
+    nl[r] = hmul2_u(sl[r], kH2Neg1024);
+    sg[r] = hfma2_u(prmt(sc, kH2Bias, 0x7151), kH2Sixteenth, kH2Neg64);
+    ng[r] = hmul2_u(sg[r], kH2Neg1024);
+  }
+  // per tile one accumulator over the super-block's 16 MMAs (the first
+  // starts it at zero): low nibbles (sub-block 2t) and high nibbles (2t + 1)
+  float c[MT][4];
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
-    // words 4 half .. 4 half + 3 of chunk t in rows g and g + 8
-    const uint4 a0 = half ? lds128<16>(q0) : lds128<0>(q0);
-    const uint4 a8 = half ? lds128<16>(q8) : lds128<0>(q8);
-    const uint32_t w0[4] = {a0.x, a0.y, a0.z, a0.w};
-    const uint32_t w8[4] = {a8.x, a8.y, a8.z, a8.w};
+    // words 4 half .. 4 half + 3 of chunk t in each row
+    uint32_t w[R][4];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const uint4 a = half ? lds128<16>(q[r]) : lds128<0>(q[r]);
+      w[r][0] = a.x;
+      w[r][1] = a.y;
+      w[r][2] = a.z;
+      w[r][3] = a.w;
+    }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int i = 4 * half + j;
-      const uint32_t x0 = w0[j], x8 = w8[j];
-      const uint32_t s0 = x0 >> 8, s8 = x8 >> 8;
       // B fragments of MMAs 2i (low) and 2i + 1 (high), side by side
       const uint4 b = lds128u(xf + static_cast<uint32_t>(i * kTc1Lanes * 16));
-      const uint32_t l0 = hfma2_u((x0 & 0x000F000Fu) | bias, sl0, nl0), l1 = hfma2_u((x8 & 0x000F000Fu) | bias, sl8, nl8);
-      const uint32_t l2 = hfma2_u((s0 & 0x000F000Fu) | bias, sl0, nl0), l3 = hfma2_u((s8 & 0x000F000Fu) | bias, sl8, nl8);
-      if (i == 0) {
-        mma_f16_16816_z(c, l0, l1, l2, l3, b.x, b.y);
-      } else {
-        mma_f16_16816(c, l0, l1, l2, l3, b.x, b.y);
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        const uint32_t x0 = w[2 * m][j], x8 = w[2 * m + 1][j];
+        const uint32_t s0 = x0 >> 8, s8 = x8 >> 8;
+        const int r0 = 2 * m, r8 = 2 * m + 1;
+        const uint32_t l0 = hfma2_u((x0 & 0x000F000Fu) | bias, sl[r0], nl[r0]);
+        const uint32_t l1 = hfma2_u((x8 & 0x000F000Fu) | bias, sl[r8], nl[r8]);
+        const uint32_t l2 = hfma2_u((s0 & 0x000F000Fu) | bias, sl[r0], nl[r0]);
+        const uint32_t l3 = hfma2_u((s8 & 0x000F000Fu) | bias, sl[r8], nl[r8]);
+        if (i == 0) {
+          mma_f16_16816_z(c[m], l0, l1, l2, l3, b.x, b.y);
+        } else {
+          mma_f16_16816(c[m], l0, l1, l2, l3, b.x, b.y);
+        }
+        mma_f16_16816(c[m], hfma2_u((x0 & 0x00F000F0u) | bias, sg[r0], ng[r0]),
+                      hfma2_u((x8 & 0x00F000F0u) | bias, sg[r8], ng[r8]),
+                      hfma2_u((s0 & 0x00F000F0u) | bias, sg[r0], ng[r0]),
+                      hfma2_u((s8 & 0x00F000F0u) | bias, sg[r8], ng[r8]), b.z, b.w);
       }
-      mma_f16_16816(c, hfma2_u((x0 & 0x00F000F0u) | bias, sg0, ng0), hfma2_u((x8 & 0x00F000F0u) | bias, sg8, ng8),
-                    hfma2_u((s0 & 0x00F000F0u) | bias, sg0, ng0), hfma2_u((s8 & 0x00F000F0u) | bias, sg8, ng8), b.z,
-                    b.w);
     }
   }
-  // columns 2t, 2t+1 of rows g and g+8: (hi, mid) for t = 0, (lo, 0) for
-  // t = 1, zeros beyond
-  const float s_0 = c[0] + c[1];
-  const float s_8 = c[2] + c[3];
-  const float d0 = half_bits_to_float(h0.x), dm0 = half_bits_to_float(h0.x >> 16);
-  const float d8 = half_bits_to_float(h8.x), dm8 = half_bits_to_float(h8.x >> 16);
-  acc0 = fmaf(d0 * inv_s, s_0, acc0);
-  acc8 = fmaf(d8 * inv_s, s_8, acc8);
   // mins of sub-blocks 2t and 2t+1 against their x sums
   const uint2 xsw = lds64(sums + 8u * static_cast<uint32_t>(t));
   const float xs0 = __uint_as_float(xsw.x), xs1 = __uint_as_float(xsw.y);
-  mn0 = fmaf(dm0, fmaf(static_cast<float>(mnw0 & 0xFFu), xs0, static_cast<float>((mnw0 >> 8) & 0xFFu) * xs1), mn0);
-  mn8 = fmaf(dm8, fmaf(static_cast<float>(mnw8 & 0xFFu), xs0, static_cast<float>((mnw8 >> 8) & 0xFFu) * xs1), mn8);
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    // columns 2t, 2t+1 of rows g and g+8: (hi, mid) for t = 0, (lo, 0) for
+    // t = 1, zeros beyond
+    const float s_0 = c[m][0] + c[m][1];
+    const float s_8 = c[m][2] + c[m][3];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = 2 * m + h;
+      const float d = half_bits_to_float(hd[r].x), dm = half_bits_to_float(hd[r].x >> 16);
+      acc[r] = fmaf(d * inv_s, h ? s_8 : s_0, acc[r]);
+      mn[r] = fmaf(dm, fmaf(static_cast<float>(mw[r] & 0xFFu), xs0, static_cast<float>((mw[r] >> 8) & 0xFFu) * xs1),
+                   mn[r]);
+    }
+  }
 }
 
-// Non-blocking test of an mbarrier phase.
-FRC_DEVICE_INLINE bool mbar_test(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-template <int OFF>
-FRC_DEVICE_INLINE uint2 lds64i(uint32_t a) {
-  uint2 v;
-  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2+%3];" : "=r"(v.x), "=r"(v.y) : "r"(a), "n"(OFF));
-  return v;
-}
 FRC_DEVICE_INLINE float ldsf(uint32_t a) {
   float v;
   asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
@@ -337,14 +342,14 @@ FRC_DEVICE_INLINE void tc1_issue(const GemvParams& p, const Tc1Maps& maps, Tc1Cu
                                  uint8_t* dst, uint64_t* bar) {
   const int pc = p.tc_part_chunks;
   if (c.ch == c.part * pc) {
-    c.T = tile_at(p, c.t0, c1, kTc1Rows);
+    c.T = tile_at(p, c.t0, c1, p.tc_rg);
     c.rows = static_cast<int>(c.T.t1 - c.t0);
   }
   const int kc = p.tc_kc, sbs = p.k / 256;
-  if (c.rows == kTc1Rows) {
-    // a whole row group: one tensor copy of 16 rows x kc super-blocks (the
+  if (c.rows == p.tc_rg) {
+    // a whole row group: one tensor copy of its rows x kc super-blocks (the
     // super-blocks past the row's end read as zeros and are not used)
-    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(kTc1Rows * kc * 144));
+    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(p.tc_rg * kc * 144));
     asm volatile(
         "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
         ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(&maps.m[c.T.m])), "r"(0), "r"(c.ch * kc),
@@ -372,10 +377,15 @@ FRC_DEVICE_INLINE void tc1_issue(const GemvParams& p, const Tc1Maps& maps, Tc1Cu
   }
 }
 
-template <int Q>
-__global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(const __grid_constant__ Tc1Maps maps,
-                                                                       GemvParams p) {
+// MAXW: the most compute warps a launch of this instantiation has (16, or 15
+// so that the CTA's 16 warps get 128 registers each instead of 96).
+// MT: 16-row MMA tiles per warp and super-block (a row group is 16 MT rows).
+template <int Q, int MAXW, int MT>
+__global__ void __launch_bounds__((MAXW + 1) * 32, 1) gemv_tc1(const __grid_constant__ Tc1Maps maps, GemvParams p) {
   static_assert(Q == kQ4_K, "gemv_tc1 covers Q4_K");
+  static_assert(MT == 1 || MT == 2, "one or two MMA tiles per warp");
+  constexpr int RG = kTc1Rows * MT;
+  static_assert(MAXW <= kTc1MaxWarps, "reduction buffers hold kTc1MaxWarps warps");
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nw = static_cast<int>(blockDim.x >> 5) - 1;  // compute warps; the last warp produces
@@ -412,7 +422,7 @@ __global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(const __g
 
   int64_t c0, c1;
   cta_rows(p.n, c0, c1);
-  const int ntiles = count_tiles(p, c0, c1, kTc1Rows) * nch;
+  const int ntiles = count_tiles(p, c0, c1, RG) * nch;
 
   if (warp == nw) {
     // the producer warp: the weights are never written by another kernel, so
@@ -556,17 +566,18 @@ __global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(const __g
 
     // ---- row groups over this part's chunks ------------------------------
     for (int64_t t0 = c0; t0 < c1;) {
-      const Tile T = tile_at(p, t0, c1, kTc1Rows);
+      const Tile T = tile_at(p, t0, c1, RG);
       const int rows = static_cast<int>(T.t1 - t0);
-      float acc0 = 0.f, acc8 = 0.f, mn0 = 0.f, mn8 = 0.f;
+      float acc[2 * MT], mn[2 * MT];
+#pragma unroll
+      for (int r = 0; r < 2 * MT; ++r) acc[r] = mn[r] = 0.f;
       for (int ch = ch0; ch < ch1; ++ch) {
         const int sb = ch * kc + warp;  // this warp's super-block of the chunk
         if (wait_phase(&full[s], ph, abort)) {
           if (sb < sbs) {
             const uint32_t lsb = static_cast<uint32_t>(sb - sb0);
-            tc1_q4k_sb(row_lane + static_cast<uint32_t>(s * stage_bytes), stride, xf_lane + lsb * xf_step,
-                       sums_s + lsb * 32u, ldsf(invs_s + 4u * lsb), t, sh, hi_t, m1, m2, p.tc_bias, acc0, acc8, mn0,
-                       mn8);
+            tc1_q4k_sb<MT>(row_lane + static_cast<uint32_t>(s * stage_bytes), stride, xf_lane + lsb * xf_step,
+                           sums_s + lsb * 32u, ldsf(invs_s + 4u * lsb), t, sh, hi_t, m1, m2, p.tc_bias, acc, mn);
           }
         } else if (lane == 0) {
           atomicOr(p.status, kStatusFullWaitTimeout);
@@ -578,34 +589,38 @@ __global__ void __launch_bounds__((kTc1MaxWarps + 1) * 32, 1) gemv_tc1(const __g
           ph ^= 1u;
         }
       }
-      // rows g and g+8: the four lanes t of a row, then the warps
-      float v0 = acc0 - mn0, v8 = acc8 - mn8;
-      v0 += __shfl_xor_sync(0xFFFFFFFFu, v0, 1);
-      v8 += __shfl_xor_sync(0xFFFFFFFFu, v8, 1);
-      v0 += __shfl_xor_sync(0xFFFFFFFFu, v0, 2);
-      v8 += __shfl_xor_sync(0xFFFFFFFFu, v8, 2);
-      float* rb = red + par * kTc1MaxWarps * kTc1Rows;
-      if (t == 0) {
-        rb[warp * kTc1Rows + g] = v0;
-        rb[warp * kTc1Rows + g + 8] = v8;
+      // rows g + 8 r: the four lanes t of a row, then the warps
+      float* rb = red + par * kTc1MaxWarps * RG;
+#pragma unroll
+      for (int r = 0; r < 2 * MT; ++r) {
+        float v = acc[r] - mn[r];
+        v += __shfl_xor_sync(0xFFFFFFFFu, v, 1);
+        v += __shfl_xor_sync(0xFFFFFFFFu, v, 2);
+        if (t == 0) rb[warp * RG + g + 8 * r] = v;
       }
       named_barrier_sync(1, nct);
       if (warp == 0) {
-        // lane l adds the partials of row l & 15 from warps 8 (l >> 4) ..
-        // 8 (l >> 4) + 7 (independent loads), then the two halves meet:
-        // the same order for every row and every launch
-        const int r = lane & 15, w0 = 8 * (lane >> 4);
+        // RG = 16: lane l adds the partials of row l & 15 from warps
+        // 8 (l >> 4) .. 8 (l >> 4) + 7, then the two halves meet; RG = 32:
+        // lane l adds row l's partials from every warp.  Independent loads,
+        // the same order for every row and every launch.
         float h = 0.f;
+        if constexpr (RG == 16) {
+          const int r = lane & 15, w0 = 8 * (lane >> 4);
 #pragma unroll
-        for (int w = 0; w < 8; ++w) h += w0 + w < nw ? rb[(w0 + w) * kTc1Rows + r] : 0.f;
-        h += __shfl_xor_sync(0xFFFFFFFFu, h, 16);
+          for (int w = 0; w < 8; ++w) h += w0 + w < nw ? rb[(w0 + w) * RG + r] : 0.f;
+          h += __shfl_xor_sync(0xFFFFFFFFu, h, 16);
+        } else {
+#pragma unroll
+          for (int w = 0; w < MAXW; ++w) h += w < nw ? rb[w * RG + lane] : 0.f;
+        }
         if (lane < rows) {
           // parts of k are added in order: ((part 0 + part 1) + part 2) ...
           float y = h;
-          float* acc = yacc + (t0 - c0) + lane;
-          if (part > 0) y = *acc + y;
+          float* ya = yacc + (t0 - c0) + lane;
+          if (part > 0) y = *ya + y;
           if (part + 1 < nparts) {
-            *acc = y;
+            *ya = y;
           } else if (!*abort) {
             put_y(p, g_world, p.mat_y[T.m] + T.local + lane, y);
           }

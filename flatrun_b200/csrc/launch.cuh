@@ -90,7 +90,7 @@ inline int opt(const std::atomic<int>& v) { return v.load(std::memory_order_rela
 // every kernel runs its measured default configuration.  -1 = not set.
 struct Tuning {
   int upt = -1, rps = -1, tile_bytes = -1, nwarps = -1, nstage = -1, smem_bytes = -1, rt = -1, stage_bytes = -1,
-      ctas_per_sm = -1, mma_grid = -1, mma_mt = -1, pre_stages = -1, pdl = -1;
+      ctas_per_sm = -1, mma_grid = -1, mma_mt = -1, pre_stages = -1, pdl = -1, tc_mt = -1;
 };
 inline const Tuning& tuning() {
   static const Tuning t = [] {
@@ -114,6 +114,7 @@ inline const Tuning& tuning() {
     v.mma_mt = get("FRC_MMA_MT");
     v.pre_stages = get("FRC_PRE_STAGES");
     v.pdl = get("FRC_PDL");
+    v.tc_mt = get("FRC_TC_MT");
     return v;
   }();
   return t;
@@ -627,27 +628,53 @@ inline cudaError_t launch_gather_wait(const uint32_t* flags, int world, const ui
 // (else 3, else 2) are held at a time (a part of k); then as many stages as
 // fit, up to 8.
 struct Tc1Config {
-  int nw = 0, nch = 0, stride = 0, stage_bytes = 0, nst = 0, part_chunks = 0, rows_max = 0;
+  int nw = 0, mt = 1, nch = 0, stride = 0, stage_bytes = 0, nst = 0, part_chunks = 0, rows_max = 0;
   size_t smem = 0;
 };
 
-inline bool tc1_config(int k, int64_t n, int grid, bool long_rows, Tc1Config* c) {
-  if (k % 256 != 0 || k <= 0 || grid < 1) return false;
+// MMA tiles per warp of a batch-1 tensor-core launch (a row group is 16 rows
+// per tile).  Two, measured on B200 against one (twice the warps, 16-row
+// groups): Llama-3-70B gate+up 65.8 against 70.3 us, the Qwen2-7B layer step
+// 58.6 against 66.3 us; the per-tile and per-row-group work of a warp is
+// shared by twice the weights and the B fragments by both tiles.
+inline int tc1_mt_for(int k) {
+  (void)k;
+  const int forced = tuning().tc_mt;
+  if (forced == 1 || forced == 2) return forced;
+  return 2;
+}
+
+// CTAs of a batch-1 tensor-core launch of n rows (one per SM, at least one
+// row group each).
+inline int tc1_grid(int64_t n, int sms, int rg) {
+  int64_t g = (n + rg - 1) / rg;
+  if (g > sms) g = sms;
+  return g < 1 ? 1 : static_cast<int>(g);
+}
+
+inline bool tc1_config(int k, int64_t n, int sms, bool long_rows, Tc1Config* c) {
+  if (k % 256 != 0 || k <= 0 || sms < 1) return false;
   const int sbs = k / 256;
+  const int mt = tc1_mt_for(k);
+  // compute warps: one super-block each per chunk; two MMA tiles per warp
+  // use half as many warps for the same tile bytes
+  const int maxw = mt == 2 ? 8 : kTc1MaxWarps;
   int nw = 0;
-  if (sbs <= kTc1MaxWarps) {
+  if (sbs <= maxw) {
     nw = sbs;
   } else {
-    for (int d = kTc1MaxWarps; d >= 8 && !nw; --d)
+    for (int d = maxw; d >= maxw / 2 && !nw; --d)
       if (sbs % d == 0) nw = d;
-    if (!nw) nw = kTc1MaxWarps;
+    if (!nw) nw = maxw;
   }
   const int forced = tuning().nwarps;
-  if (forced >= 1 && forced <= kTc1MaxWarps) nw = forced;
+  if (forced >= 1 && forced <= maxw) nw = forced;
   c->nw = nw;
+  c->mt = mt;
   c->nch = (sbs + nw - 1) / nw;
   c->stride = tc1_row_stride(nw);
-  c->stage_bytes = round_up(kTc1Rows * c->stride, 128);
+  c->stage_bytes = round_up(kTc1Rows * mt * c->stride, 128);
+  const int grid = tc1_grid(n, sms, kTc1Rows * mt);
   const int64_t rows_max = (n + grid - 1) / grid;
   if (rows_max > (1 << 20)) return false;
   c->rows_max = static_cast<int>(rows_max);
@@ -679,14 +706,6 @@ inline bool tc1_config(int k, int64_t n, int grid, bool long_rows, Tc1Config* c)
   return true;
 }
 
-// CTAs of a batch-1 tensor-core launch of n rows (one per SM, at least one
-// row group each).
-inline int tc1_grid(int64_t n, int sms) {
-  int64_t g = (n + kTc1Rows - 1) / kTc1Rows;
-  if (g > sms) g = sms;
-  return g < 1 ? 1 : static_cast<int>(g);
-}
-
 template <int Q>
 inline cudaError_t launch_tc1(GemvParams p, const GemvRequest& r, const Tc1Config& c) {
   p.tc_kc = c.nw;
@@ -695,11 +714,16 @@ inline cudaError_t launch_tc1(GemvParams p, const GemvRequest& r, const Tc1Confi
   p.tc_bias = kH2Bias;
   p.tc_part_chunks = c.part_chunks;
   p.tc_rows_max = c.rows_max;
+  p.tc_rg = kTc1Rows * c.mt;
   p.stage_stride = c.stage_bytes;
   p.nstage = c.nst;
   const int threads = (c.nw + 1) * 32;
+  // two MMA tiles per warp: up to 8 compute warps; one: up to 15 compute
+  // warps run the 16-warp instantiation (128 registers), 16 the 17-warp one
+  auto kernel = c.mt == 2 ? gemv_tc1<Q, 8, 2>
+                          : (c.nw < kTc1MaxWarps ? gemv_tc1<Q, kTc1MaxWarps - 1, 1> : gemv_tc1<Q, kTc1MaxWarps, 1>);
   int per_sm = 0;
-  cudaError_t e = kernel_occupancy(reinterpret_cast<const void*>(gemv_tc1<Q>), r.device, threads, c.smem, &per_sm);
+  cudaError_t e = kernel_occupancy(reinterpret_cast<const void*>(kernel), r.device, threads, c.smem, &per_sm);
   if (e != cudaSuccess) return e;
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
   // one tensor map per matrix: [rows][super-blocks][18 x 8 bytes]
@@ -712,14 +736,14 @@ inline cudaError_t launch_tc1(GemvParams p, const GemvRequest& r, const Tc1Confi
     const int64_t rows = p.mat_end[m] - (m ? p.mat_end[m - 1] : 0);
     const cuuint64_t dims[3] = {18, static_cast<cuuint64_t>(sbs), static_cast<cuuint64_t>(rows > 0 ? rows : 1)};
     const cuuint64_t strides[2] = {144, static_cast<cuuint64_t>(p.row_bytes)};
-    const cuuint32_t box[3] = {18, static_cast<cuuint32_t>(c.nw), static_cast<cuuint32_t>(kTc1Rows)};
+    const cuuint32_t box[3] = {18, static_cast<cuuint32_t>(c.nw), static_cast<cuuint32_t>(kTc1Rows * c.mt)};
     const cuuint32_t estr[3] = {1, 1, 1};
     if (encode(&maps.m[m], CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<uint8_t*>(p.mat_w[m]), dims, strides, box,
                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
-  const int grid = tc1_grid(p.n, r.sms);
+  const int grid = tc1_grid(p.n, r.sms, kTc1Rows * c.mt);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(threads);
@@ -730,7 +754,7 @@ inline cudaError_t launch_tc1(GemvParams p, const GemvRequest& r, const Tc1Confi
   attr[0].val.programmaticStreamSerializationAllowed = tuned(tuning().pdl, 1) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemv_tc1<Q>, maps, p);
+  return cudaLaunchKernelEx(&cfg, kernel, maps, p);
 }
 
 // Largest tile footprint must fit in shared memory with two stages.
@@ -798,7 +822,7 @@ cudaError_t launch_gemv(const GemvRequest& r) {
     if constexpr (Q == kQ4_K) {
       Tc1Config c;
       if (!opt(options().batch1_int16) && opt(options().batch1_tc) &&
-          tc1_config(r.k, b1.n, tc1_grid(b1.n, r.sms), opt(options().batch1_tc) == 2, &c))
+          tc1_config(r.k, b1.n, r.sms, opt(options().batch1_tc) == 2, &c))
         return launch_tc1<Q>(b1, r, c);
     }
     const cudaError_t e =
