@@ -521,6 +521,8 @@ def main() -> None:
                     help="batch 1 on the 16-bit activation grid kernel (dp4a) instead of fp32 activations")
     ap.add_argument("--cuda-core", action="store_true",
                     help="batch-1 Q4_K on the CUDA-core fp32 kernel instead of the tensor-core one (same arithmetic)")
+    ap.add_argument("--tc-long-rows", action="store_true",
+                    help="batch-1 Q4_K rows longer than one part of k on the tensor-core kernel too (FRC_OPT_BATCH1_TC=2)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -592,6 +594,8 @@ def main() -> None:
         _lib.set_option("batch1_int16", 1)
     if args.cuda_core:
         _lib.set_option("batch1_tc", 0)
+    elif args.tc_long_rows:
+        _lib.set_option("batch1_tc", 2)
     be = CudaBackend(dev)
     if not be.available:
         raise RuntimeError(f"CUDA backend unavailable: {be._load_error}")

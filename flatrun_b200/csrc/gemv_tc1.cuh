@@ -148,14 +148,26 @@ FRC_DEVICE_INLINE void mma_f16_16816_z(float (&c)[4], uint32_t a0, uint32_t a1, 
       : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
 }
+// Shared-memory loads of data that TMA copies or other warps wrote before an
+// mbarrier wait or a barrier: not volatile, but ordered after those waits by
+// the memory clobber (the hardware schedule is the assembler's).
+template <int OFF>
+FRC_DEVICE_INLINE uint4 lds128f(uint32_t a) {
+  uint4 v;
+  asm("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4+%5];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "r"(a), "n"(OFF)
+      : "memory");
+  return v;
+}
 FRC_DEVICE_INLINE uint4 lds128u(uint32_t a) {
   uint4 v;
-  asm("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  asm("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a) : "memory");
   return v;
 }
 FRC_DEVICE_INLINE uint2 lds64(uint32_t a) {
   uint2 v;
-  asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a) : "memory");
   return v;
 }
 FRC_DEVICE_INLINE void sts64(uint32_t a, uint32_t x, uint32_t y) {
@@ -221,7 +233,7 @@ FRC_DEVICE_INLINE void tc1_q4k_sb(uint32_t row, uint32_t stride, uint32_t xf, ui
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const uint32_t ra = row + static_cast<uint32_t>(8 * r) * stride;  // rows g, g + 8, g + 16, g + 24
-    hd[r] = lds128<0>(ra);
+    hd[r] = lds128f<0>(ra);
     q[r] = ra + 16u + 32u * static_cast<uint32_t>(t);
     uint32_t sc;
     tc1_q4k_scales(hd[r], sh, hi_t, m1, m2, sc, mw[r]);
@@ -241,7 +253,7 @@ FRC_DEVICE_INLINE void tc1_q4k_sb(uint32_t row, uint32_t stride, uint32_t xf, ui
     uint32_t w[R][4];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      const uint4 a = half ? lds128<16>(q[r]) : lds128<0>(q[r]);
+      const uint4 a = half ? lds128f<16>(q[r]) : lds128f<0>(q[r]);
       w[r][0] = a.x;
       w[r][1] = a.y;
       w[r][2] = a.z;

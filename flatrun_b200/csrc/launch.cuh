@@ -689,12 +689,12 @@ inline bool tc1_config(int k, int64_t n, int sms, bool long_rows, Tc1Config* c) 
     }
   }
   if (!pc) return false;
-  // rows longer than one part of k (the down projections of the models
-  // measured, k = 18944 and 28672) rebuild the fragments per part while the
-  // ring drains: measured on B200 at or below the CUDA-core kernel there
-  // (Llama-3-70B down 48.6 against 47.0 us, Qwen2-7B down 21.0 against 20.5),
-  // so they stay on it unless long_rows (FRC_OPT_BATCH1_TC = 2)
-  if (pc < c->nch && !long_rows) return false;
+  // rows longer than one part of k rebuild the fragments per part while the
+  // ring drains: measured on B200 with two parts ahead of the CUDA-core
+  // kernel (Qwen2-7B down, k = 18944: 18.3 against 22.7 us), with three
+  // behind it (Llama-3-70B down, k = 28672: 50.8 against 47.1 us), so rows of
+  // more than two parts stay on it unless long_rows (FRC_OPT_BATCH1_TC = 2)
+  if ((c->nch + pc - 1) / pc > 2 && !long_rows) return false;
   const int forced_nst = tuning().nstage;
   int nst = forced_nst > 0 ? forced_nst : 8;
   for (; nst >= 2; --nst)
