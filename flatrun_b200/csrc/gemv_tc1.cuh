@@ -106,11 +106,14 @@ __host__ __device__ inline Tc1Layout tc1_layout(int nst, int psb, int rows, int 
 // copy of 16 rows x kc super-blocks lands in).
 __host__ __device__ constexpr int tc1_row_stride(int kc) { return kc * 144; }
 
-// One tensor map per matrix of the launch: the matrix as a 3-D tensor of
-// 8-byte words [rows][super-blocks][18] (strides row_bytes and 144 bytes);
-// a box of 16 rows x kc super-blocks x 18 words is one tile.
+// Tensor maps per matrix of the launch: the matrix as a 3-D tensor of 8-byte
+// words [rows][super-blocks][18] (strides row_bytes and 144 bytes), with
+// boxes of kc super-blocks x 18 words and 32, 16, 8, 4, 2 or 1 rows: a whole
+// row group is one copy, a short one (a matrix or CTA end) one copy per set
+// bit of its row count.
+constexpr int kTc1Boxes = 6;  // rows 32 >> b for b < kTc1Boxes
 struct Tc1Maps {
-  CUtensorMap m[4];
+  CUtensorMap m[4][kTc1Boxes];
 };
 
 FRC_DEVICE_INLINE uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -358,25 +361,40 @@ FRC_DEVICE_INLINE void tc1_issue(const GemvParams& p, const Tc1Maps& maps, Tc1Cu
     c.rows = static_cast<int>(c.T.t1 - c.t0);
   }
   const int kc = p.tc_kc, sbs = p.k / 256;
-  if (c.rows == p.tc_rg) {
-    // a whole row group: one tensor copy of its rows x kc super-blocks (the
-    // super-blocks past the row's end read as zeros and are not used)
-    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(p.tc_rg * kc * 144));
+  // the group's rows as tensor boxes of 32, 16, ..., 1 rows (the
+  // super-blocks past the row's end read as zeros and are not used), each
+  // landing on a 128-byte boundary of the stage as tensor copies require;
+  // rows left after the first box that would not are copied one bulk copy
+  // per row (16-byte aligned)
+  const uint32_t box_bytes = static_cast<uint32_t>(kc * 144);
+  const int nsb = (c.ch + 1) * kc <= sbs ? kc : sbs - c.ch * kc;
+  const uint32_t cb = static_cast<uint32_t>(nsb) * 144u;
+  int r0 = 0;
+  uint32_t tx = 0;
+  int nbox = 0, boxes[kTc1Boxes], starts[kTc1Boxes];
+  for (int b = 0; b < kTc1Boxes; ++b) {
+    const int box = kTc1MaxRows >> b;
+    if (c.rows - r0 >= box && (static_cast<uint32_t>(r0) * static_cast<uint32_t>(p.tc_stride)) % 128u == 0) {
+      boxes[nbox] = b;
+      starts[nbox++] = r0;
+      tx += static_cast<uint32_t>(box) * box_bytes;
+      r0 += box;
+    }
+  }
+  tx += static_cast<uint32_t>(c.rows - r0) * cb;
+  mbar_arrive_expect_tx(bar, tx);
+  for (int i = 0; i < nbox; ++i) {
     asm volatile(
         "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
-        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(&maps.m[c.T.m])), "r"(0), "r"(c.ch * kc),
-        "r"(static_cast<int>(c.T.local)), "r"(smem_u32(bar))
+        ::"r"(smem_u32(dst + starts[i] * p.tc_stride)), "l"(reinterpret_cast<uint64_t>(&maps.m[c.T.m][boxes[i]])),
+        "r"(0), "r"(c.ch * kc), "r"(static_cast<int>(c.T.local) + starts[i]), "r"(smem_u32(bar))
         : "memory");
-  } else {
-    // a short row group (the end of a matrix or of the CTA's rows): one bulk
-    // copy per row, so no byte past the CTA's rows is read
-    const int nsb = (c.ch + 1) * kc <= sbs ? kc : sbs - c.ch * kc;
-    const uint32_t cb = static_cast<uint32_t>(nsb) * 144u;
-    mbar_arrive_expect_tx(bar, cb * static_cast<uint32_t>(c.rows));
-    const uint8_t* src =
-        p.mat_w[c.T.m] + static_cast<uint64_t>(c.T.local) * p.row_bytes + static_cast<uint64_t>(c.ch) * kc * 144;
-    for (int r = 0; r < c.rows; ++r)
-      bulk_g2s(dst + r * p.tc_stride, src + static_cast<uint64_t>(r) * p.row_bytes, cb, bar);
+  }
+  if (r0 < c.rows) {
+    const uint8_t* src = p.mat_w[c.T.m] + static_cast<uint64_t>(c.T.local + r0) * p.row_bytes +
+                         static_cast<uint64_t>(c.ch) * kc * 144;
+    for (int r = r0; r < c.rows; ++r)
+      bulk_g2s(dst + r * p.tc_stride, src + static_cast<uint64_t>(r - r0) * p.row_bytes, cb, bar);
   }
   const int part_end = (c.part + 1) * pc < p.tc_nchunk ? (c.part + 1) * pc : p.tc_nchunk;
   if (++c.ch == part_end) {  // the row group's share of this part is issued

@@ -736,12 +736,14 @@ inline cudaError_t launch_tc1(GemvParams p, const GemvRequest& r, const Tc1Confi
     const int64_t rows = p.mat_end[m] - (m ? p.mat_end[m - 1] : 0);
     const cuuint64_t dims[3] = {18, static_cast<cuuint64_t>(sbs), static_cast<cuuint64_t>(rows > 0 ? rows : 1)};
     const cuuint64_t strides[2] = {144, static_cast<cuuint64_t>(p.row_bytes)};
-    const cuuint32_t box[3] = {18, static_cast<cuuint32_t>(c.nw), static_cast<cuuint32_t>(kTc1Rows * c.mt)};
     const cuuint32_t estr[3] = {1, 1, 1};
-    if (encode(&maps.m[m], CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<uint8_t*>(p.mat_w[m]), dims, strides, box,
-               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return cudaErrorInvalidValue;
+    for (int b = 0; b < kTc1Boxes; ++b) {
+      const cuuint32_t box[3] = {18, static_cast<cuuint32_t>(c.nw), static_cast<cuuint32_t>(kTc1MaxRows >> b)};
+      if (encode(&maps.m[m][b], CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<uint8_t*>(p.mat_w[m]), dims, strides,
+                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    }
   }
   const int grid = tc1_grid(p.n, r.sms, kTc1Rows * c.mt);
   cudaLaunchConfig_t cfg = {};
