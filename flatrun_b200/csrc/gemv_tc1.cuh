@@ -86,17 +86,19 @@ struct Tc1Layout {
 __host__ __device__ constexpr int tc1_align(int v, int a) { return (v + a - 1) / a * a; }
 
 // psb: super-blocks per part of k (the fragments held at a time); rows:
-// the most rows one CTA owns (partial sums carried across parts).
-__host__ __device__ inline Tc1Layout tc1_layout(int nst, int psb, int rows, int stage_bytes) {
+// the most rows one CTA owns (partial sums carried across parts); nbuf: 1,
+// or 2 when a builder warp fills one fragment buffer while the compute warps
+// read the other.
+__host__ __device__ inline Tc1Layout tc1_layout(int nst, int psb, int rows, int stage_bytes, int nbuf = 1) {
   Tc1Layout L{};
-  L.bars = 0;                                        // full[nst], empty[nst], abort and void flags
-  L.red = tc1_align(16 * nst + 8, 16);               // [2][kTc1MaxWarps][row group] row partials
+  L.bars = 0;  // full[nst], empty[nst], frag_full[2], frag_empty[2], norm, then abort and void flags, inv norm
+  L.red = tc1_align(16 * nst + 40 + 12, 16);         // [2][kTc1MaxWarps][row group] row partials
   L.scr = L.red + 2 * kTc1MaxWarps * kTc1MaxRows * 4;  // [kTc1MaxWarps] reduction scratch
   L.yacc = L.scr + kTc1MaxWarps * 4;                 // [rows] partial row sums over parts of k
-  L.sums = tc1_align(L.yacc + rows * 4, 16);         // [psb][8] fp32 sub-block sums of x
-  L.invs = L.sums + psb * 32;                        // [psb] 1 / s per super-block
-  L.frags = tc1_align(L.invs + psb * 4, 128);        // [psb][16][12] uint2
-  L.zeros = L.frags + psb * kTc1FragBytes;           // kTc1ZeroBytes of zeros
+  L.sums = tc1_align(L.yacc + rows * 4, 16);         // [nbuf][psb][8] fp32 sub-block sums of x
+  L.invs = L.sums + nbuf * psb * 32;                 // [nbuf][psb] 1 / s per super-block
+  L.frags = tc1_align(L.invs + nbuf * psb * 4, 128);  // [nbuf][psb][16][12] uint2
+  L.zeros = L.frags + nbuf * psb * kTc1FragBytes;    // kTc1ZeroBytes of zeros
   L.stages = tc1_align(L.zeros + kTc1ZeroBytes, 128);
   L.total = L.stages + nst * stage_bytes;
   return L;
@@ -407,18 +409,78 @@ FRC_DEVICE_INLINE void tc1_issue(const GemvParams& p, const Tc1Maps& maps, Tc1Cu
   }
 }
 
+// Activation fragments, sub-block sums and scales of super-blocks [sb0, sb1)
+// into one buffer: thread `tid` of `nthreads` (whole warps) owns sub-blocks
+// 8 sb0 + tid, + nthreads, ...; lanes 8a .. 8a+7 hold one super-block.
+FRC_DEVICE_INLINE void tc1_build(const GemvParams& p, int sb0, int sb1, int tid, int nthreads, float inv_norm,
+                                 uint32_t frag_base, float* sums, float* invs) {
+  const int rounds = (8 * (sb1 - sb0) + nthreads - 1) / nthreads;
+  for (int rr = 0; rr < rounds; ++rr) {
+    const int j = 8 * sb0 + tid + rr * nthreads;
+    float v[32];
+    if (j < 8 * sb1) {
+      tc1_load_sub(p, j, v);
+      if (p.x_norm_w) {
+        const float4* ws = reinterpret_cast<const float4*>(p.x_norm_w + static_cast<int64_t>(j) * 32);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 gw = __ldg(ws + q);
+          const float gg[4] = {gw.x, gw.y, gw.z, gw.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[4 * q + e] = (v[4 * q + e] * inv_norm) * gg[e];
+        }
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) v[e] = 0.f;
+    }
+    float m = 0.f, xsum = 0.f;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      m = fmaxf(m, fabsf(v[e]));
+      xsum += v[e];
+    }
+    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
+    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
+    if (j < 8 * sb1) {
+      float sc, inv;
+      tc1_scale(m, sc, inv);
+      const int lj = j - 8 * sb0, sb = lj >> 3, jj = lj & 7, tt = jj >> 1, h = jj & 1;
+      sums[lj] = xsum;
+      if (jj == 0) invs[sb] = inv;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        uint32_t p0, p1, p2, q0, q1, q2;
+        split3(v[4 * i] * sc, v[4 * i + 2] * sc, p0, p1, p2);
+        split3(v[4 * i + 1] * sc, v[4 * i + 3] * sc, q0, q1, q2);
+        const uint32_t a = frag_base + static_cast<uint32_t>(((sb * 8 + i) * kTc1Lanes + tt) * 16 + h * 8);
+        sts64(a, p0, q0);
+        sts64(a + 64u, p1, q1);
+        sts64(a + 128u, p2, q2);
+      }
+    }
+  }
+}
+
 // MAXW: the most compute warps a launch of this instantiation has (16, or 15
 // so that the CTA's 16 warps get 128 registers each instead of 96).
 // MT: 16-row MMA tiles per warp and super-block (a row group is 16 MT rows).
-template <int Q, int MAXW, int MT>
-__global__ void __launch_bounds__((MAXW + 1) * 32, 1) gemv_tc1(const __grid_constant__ Tc1Maps maps, GemvParams p) {
+// NB: rows in several parts of k with NB builder warps (the last ones) that
+// build part p + 1's fragments into the second buffer while the compute
+// warps read part p's; 0: the compute warps build every part.
+template <int Q, int MAXW, int MT, int NB>
+__global__ void __launch_bounds__((MAXW + 1 + NB) * 32, 1) gemv_tc1(const __grid_constant__ Tc1Maps maps,
+                                                                   GemvParams p) {
   static_assert(Q == kQ4_K, "gemv_tc1 covers Q4_K");
   static_assert(MT == 1 || MT == 2, "one or two MMA tiles per warp");
   constexpr int RG = kTc1Rows * MT;
   static_assert(MAXW <= kTc1MaxWarps, "reduction buffers hold kTc1MaxWarps warps");
+  static_assert(NB >= 0 && NB <= 2, "up to two builder warps");
+  constexpr bool BUILDER = NB > 0;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nw = static_cast<int>(blockDim.x >> 5) - 1;  // compute warps; the last warp produces
+  const int nw = static_cast<int>(blockDim.x >> 5) - 1 - NB;  // compute warps; then the producer, the builders
   const int nct = nw * 32;
   const int ct = threadIdx.x;
   const int nst = p.nstage;
@@ -426,11 +488,17 @@ __global__ void __launch_bounds__((MAXW + 1) * 32, 1) gemv_tc1(const __grid_cons
   const int stage_bytes = p.stage_stride;
   const int kc = p.tc_kc, nch = p.tc_nchunk, pc = p.tc_part_chunks;
   const int nparts = (nch + pc - 1) / pc;
-  const Tc1Layout L = tc1_layout(nst, pc * kc, p.tc_rows_max, stage_bytes);
+  constexpr int NBUF = BUILDER ? 2 : 1;
+  const int psb = pc * kc;
+  const Tc1Layout L = tc1_layout(nst, psb, p.tc_rows_max, stage_bytes, NBUF);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + nst;
-  int* abort_flag = reinterpret_cast<int*>(empty + nst);
+  uint64_t* frag_full = empty + nst;   // [2] a part's fragments are built (builder)
+  uint64_t* frag_empty = frag_full + 2;  // [2] a buffer's part is done (compute warps)
+  uint64_t* norm_ready = frag_empty + 2;  // the RMSNorm scale is in shared memory
+  int* abort_flag = reinterpret_cast<int*>(norm_ready + 1);
   int* void_flag = abort_flag + 1;  // an earlier gather's wait ran out
+  float* norm_scale = reinterpret_cast<float*>(void_flag + 1);
   float* red = reinterpret_cast<float*>(smem + L.red);
   float* scr = reinterpret_cast<float*>(smem + L.scr);
   float* yacc = reinterpret_cast<float*>(smem + L.yacc);
@@ -443,6 +511,11 @@ __global__ void __launch_bounds__((MAXW + 1) * 32, 1) gemv_tc1(const __grid_cons
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], static_cast<uint32_t>(nw));
     }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&frag_full[i], BUILDER ? 32u * NB : 1u);
+      mbar_init(&frag_empty[i], static_cast<uint32_t>(nw));
+    }
+    mbar_init(norm_ready, 1);
     *abort_flag = 0;
     *void_flag = 0;
     fence_barrier_init();
@@ -476,6 +549,26 @@ __global__ void __launch_bounds__((MAXW + 1) * 32, 1) gemv_tc1(const __grid_cons
         if (!wait_phase(&full[i % nst], static_cast<uint32_t>(i / nst) & 1u, &zero))
           atomicOr(p.status, kStatusDrainTimeout);
       }
+    }
+    return;
+  }
+  if (BUILDER && warp > nw) {
+    // the builder warps: parts 1, 2, ... into buffer part % 2, each once the
+    // compute warps have released that buffer's previous part
+    const int bt = (warp - nw - 1) * 32 + lane;
+    griddep_wait();
+    griddep_launch_dependents();
+    // x is final (an earlier fused gather complete) and its RMSNorm scale
+    // is known once the compute warps publish it
+    if (!wait_phase(norm_ready, 0u, abort)) return;
+    const float inv_norm = *reinterpret_cast<volatile float*>(norm_scale);
+    for (int part = 1; part < nparts; ++part) {
+      const int b = part & 1;
+      if (part >= 2 && !wait_phase(&frag_empty[b], static_cast<uint32_t>((part - 2) >> 1) & 1u, abort)) return;
+      const int sb0 = part * pc * kc, sb1 = (part + 1) * pc * kc < sbs ? (part + 1) * pc * kc : sbs;
+      tc1_build(p, sb0, sb1, bt, 32 * NB, inv_norm, smem_u32(smem + L.frags) + static_cast<uint32_t>(b * psb * kTc1FragBytes),
+                reinterpret_cast<float*>(smem + L.sums) + b * psb * 8, reinterpret_cast<float*>(smem + L.invs) + b * psb);
+      mbar_arrive(&frag_full[b]);  // every builder thread: its stores are released
     }
     return;
   }
@@ -521,6 +614,10 @@ __global__ void __launch_bounds__((MAXW + 1) * 32, 1) gemv_tc1(const __grid_cons
     for (int w = 0; w < nw; ++w) ss += scr[w];
     inv_norm = 1.0f / sqrtf(ss / static_cast<float>(p.k) + p.x_norm_eps);
   }
+  if (BUILDER && ct == 0) {  // the builder reads x and normalises the later parts with the same scale
+    *norm_scale = inv_norm;
+    mbar_arrive(norm_ready);
+  }
   // the zero fragment read by lanes >= 12 (columns 3..7 of B)
   const uint32_t zero_base = smem_u32(smem + L.zeros);
   for (int i = ct; i < kTc1ZeroBytes / 8; i += nct) sts64(zero_base + 8u * i, 0u, 0u);
@@ -542,57 +639,22 @@ __global__ void __launch_bounds__((MAXW + 1) * 32, 1) gemv_tc1(const __grid_cons
   int par = 0;
   for (int part = 0; part < nparts; ++part) {
     const int ch0 = part * pc, ch1 = (part + 1) * pc < nch ? (part + 1) * pc : nch;
-    const int sb0 = ch0 * kc, sb1 = ch1 * kc < sbs ? ch1 * kc : sbs;
-    // ---- x fragments of super-blocks [sb0, sb1): thread ct owns sub-blocks
-    // 8 sb0 + ct, + nct, ...; lanes 8a .. 8a+7 hold one super-block.  The
-    // previous part's fragments are free: every warp has passed the barrier
-    // that ended its last row group.
-    for (int j = 8 * sb0 + ct; j < 8 * sb0 + ((8 * (sb1 - sb0) + nct - 1) / nct) * nct; j += nct) {
-      float v[32];
-      if (j < 8 * sb1) {
-        tc1_load_sub(p, j, v);
-        if (p.x_norm_w) {
-          const float4* ws = reinterpret_cast<const float4*>(p.x_norm_w + static_cast<int64_t>(j) * 32);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float4 gw = __ldg(ws + q);
-            const float gg[4] = {gw.x, gw.y, gw.z, gw.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) v[4 * q + e] = (v[4 * q + e] * inv_norm) * gg[e];
-          }
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) v[e] = 0.f;
-      }
-      float m = 0.f, xsum = 0.f;
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        m = fmaxf(m, fabsf(v[e]));
-        xsum += v[e];
-      }
-      m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
-      m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
-      m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
-      if (j < 8 * sb1) {
-        float sc, inv;
-        tc1_scale(m, sc, inv);
-        const int lj = j - 8 * sb0, sb = lj >> 3, jj = lj & 7, tt = jj >> 1, h = jj & 1;
-        sums[lj] = xsum;
-        if (jj == 0) invs[sb] = inv;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          uint32_t p0, p1, p2, q0, q1, q2;
-          split3(v[4 * i] * sc, v[4 * i + 2] * sc, p0, p1, p2);
-          split3(v[4 * i + 1] * sc, v[4 * i + 3] * sc, q0, q1, q2);
-          const uint32_t a = frag_base + static_cast<uint32_t>(((sb * 8 + i) * kTc1Lanes + tt) * 16 + h * 8);
-          sts64(a, p0, q0);
-          sts64(a + 64u, p1, q1);
-          sts64(a + 128u, p2, q2);
-        }
-      }
+    const int sb0 = ch0 * kc;
+    const int b = BUILDER ? (part & 1) : 0;  // this part's fragment buffer
+    bool frags_ok = true;
+    if (!BUILDER || part == 0) {
+      // x fragments of super-blocks [sb0, sb1), built by the compute warps
+      // (without a builder the previous part's fragments are free: every
+      // warp has passed the barrier that ended its last row group)
+      const int sb1 = ch1 * kc < sbs ? ch1 * kc : sbs;
+      tc1_build(p, sb0, sb1, ct, nct, inv_norm, frag_base, sums, invs);
+      named_barrier_sync(1, nct);  // fragments, sums, scales (and zeros) complete
+    } else {
+      frags_ok = wait_phase(&frag_full[b], static_cast<uint32_t>((part - 1) >> 1) & 1u, abort);
     }
-    named_barrier_sync(1, nct);  // fragments, sums, scales (and zeros) complete
+    const uint32_t boff = static_cast<uint32_t>(b * psb);
+    const uint32_t xf_part = xf_lane + (lane < kTc1Lanes ? boff * static_cast<uint32_t>(kTc1FragBytes) : 0u);
+    const uint32_t sums_part = sums_s + boff * 32u, invs_part = invs_s + boff * 4u;
 
     // ---- row groups over this part's chunks ------------------------------
     for (int64_t t0 = c0; t0 < c1;) {
@@ -604,10 +666,11 @@ __global__ void __launch_bounds__((MAXW + 1) * 32, 1) gemv_tc1(const __grid_cons
       for (int ch = ch0; ch < ch1; ++ch) {
         const int sb = ch * kc + warp;  // this warp's super-block of the chunk
         if (wait_phase(&full[s], ph, abort)) {
-          if (sb < sbs) {
+          if (sb < sbs && frags_ok) {
             const uint32_t lsb = static_cast<uint32_t>(sb - sb0);
-            tc1_q4k_sb<MT>(row_lane + static_cast<uint32_t>(s * stage_bytes), stride, xf_lane + lsb * xf_step,
-                           sums_s + lsb * 32u, ldsf(invs_s + 4u * lsb), t, sh, hi_t, m1, m2, p.tc_bias, acc, mn);
+            tc1_q4k_sb<MT>(row_lane + static_cast<uint32_t>(s * stage_bytes), stride, xf_part + lsb * xf_step,
+                           sums_part + lsb * 32u, ldsf(invs_part + 4u * lsb), t, sh, hi_t, m1, m2, p.tc_bias, acc,
+                           mn);
           }
         } else if (lane == 0) {
           atomicOr(p.status, kStatusFullWaitTimeout);
@@ -659,6 +722,9 @@ __global__ void __launch_bounds__((MAXW + 1) * 32, 1) gemv_tc1(const __grid_cons
       par ^= 1;
       t0 = T.t1;
     }
+    // every compute warp has passed the last row group's barrier: this
+    // part's buffer is free for the builder's part + 2
+    if (BUILDER && part + 2 < nparts && lane == 0) mbar_arrive(&frag_empty[b]);
   }
   if (g_world > 1) {  // publish this CTA's gathered rows
     named_barrier_sync(1, nct);

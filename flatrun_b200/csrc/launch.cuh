@@ -90,7 +90,8 @@ inline int opt(const std::atomic<int>& v) { return v.load(std::memory_order_rela
 // every kernel runs its measured default configuration.  -1 = not set.
 struct Tuning {
   int upt = -1, rps = -1, tile_bytes = -1, nwarps = -1, nstage = -1, smem_bytes = -1, rt = -1, stage_bytes = -1,
-      ctas_per_sm = -1, mma_grid = -1, mma_mt = -1, pre_stages = -1, pdl = -1, tc_mt = -1;
+      ctas_per_sm = -1, mma_grid = -1, mma_mt = -1, pre_stages = -1, pdl = -1, tc_mt = -1, tc_builders = -1,
+      tc_stages = -1, tc_part_chunks = -1;
 };
 inline const Tuning& tuning() {
   static const Tuning t = [] {
@@ -115,6 +116,9 @@ inline const Tuning& tuning() {
     v.pre_stages = get("FRC_PRE_STAGES");
     v.pdl = get("FRC_PDL");
     v.tc_mt = get("FRC_TC_MT");
+    v.tc_builders = get("FRC_TC_BUILDERS");
+    v.tc_stages = get("FRC_TC_STAGES");
+    v.tc_part_chunks = get("FRC_TC_PC");
     return v;
   }();
   return t;
@@ -629,6 +633,7 @@ inline cudaError_t launch_gather_wait(const uint32_t* flags, int world, const ui
 // fit, up to 8.
 struct Tc1Config {
   int nw = 0, mt = 1, nch = 0, stride = 0, stage_bytes = 0, nst = 0, part_chunks = 0, rows_max = 0;
+  int builders = 0;  // rows in several parts of k: builder warps, two fragment buffers
   size_t smem = 0;
 };
 
@@ -679,30 +684,54 @@ inline bool tc1_config(int k, int64_t n, int sms, bool long_rows, Tc1Config* c) 
   if (rows_max > (1 << 20)) return false;
   c->rows_max = static_cast<int>(rows_max);
   const int budget = tuned(tuning().smem_bytes, kSmemBudget);
-  int pc = 0;
-  for (int want = 4; want >= 2 && !pc; --want) {
-    for (int q = c->nch; q >= 1; --q) {
-      if (tc1_layout(want, q * nw, c->rows_max, c->stage_bytes).total <= budget) {
-        pc = q;
-        break;
+  // the whole row's fragments if they leave room for `want` stages, else
+  // parts of k: with two tiles per warp two builder warps fill one fragment
+  // buffer while the compute warps read the other, and each buffer holds as
+  // many whole chunks as leave room for `want` stages (else fewer, down to
+  // 2).  Measured on B200 (down projections, us): Llama-3-70B k = 28672
+  // 41.6 at 3 stages x 4 parts, 41.7 at 4 x 5, 45.7 at 2 x 7 (one builder
+  // warp 44.2, none 47.2 on the CUDA-core kernel); Qwen2-7B k = 18944 17.1 at
+  // 3 x 3, 18.1 at 4 x 4, 18.9 at 2 x 2 without builders.
+  const int want = tuned(tuning().tc_stages, 3);
+  int pc = 0, builders = 0;
+  if (tc1_layout(want, c->nch * nw, c->rows_max, c->stage_bytes).total <= budget) {
+    pc = c->nch;
+  } else {
+    builders = mt == 2 ? tuned(tuning().tc_builders, 2) : 0;
+    if (builders > 2) builders = 2;
+    const int nbuf = builders ? 2 : 1;
+    const int forced_pc = tuning().tc_part_chunks;
+    if (forced_pc >= 1 && forced_pc < c->nch) {
+      pc = forced_pc;
+    } else {
+      for (int w = want; w >= 2 && !pc; --w) {
+        for (int q = c->nch - 1; q >= 1; --q) {
+          if (tc1_layout(w, q * nw, c->rows_max, c->stage_bytes, nbuf).total <= budget) {
+            pc = q;
+            break;
+          }
+        }
       }
     }
   }
   if (!pc) return false;
-  // rows longer than one part of k rebuild the fragments per part while the
-  // ring drains: measured on B200 with two parts ahead of the CUDA-core
-  // kernel (Qwen2-7B down, k = 18944: 18.3 against 22.7 us), with three
-  // behind it (Llama-3-70B down, k = 28672: 50.8 against 47.1 us), so rows of
-  // more than two parts stay on it unless long_rows (FRC_OPT_BATCH1_TC = 2)
-  if ((c->nch + pc - 1) / pc > 2 && !long_rows) return false;
+  // rows longer than one part of k: with builder warps the parts' fragments
+  // are built behind the compute; without them they are rebuilt while the
+  // ring drains, which measured on B200 behind the CUDA-core kernel at three
+  // parts (Llama-3-70B down, k = 28672: 50.8 against 47.1 us), so rows of
+  // more than two parts without builders stay on it unless long_rows
+  // (FRC_OPT_BATCH1_TC = 2)
+  if (!builders && (c->nch + pc - 1) / pc > 2 && !long_rows) return false;
+  const int nbuf = builders ? 2 : 1;
   const int forced_nst = tuning().nstage;
   int nst = forced_nst > 0 ? forced_nst : 8;
   for (; nst >= 2; --nst)
-    if (tc1_layout(nst, pc * nw, c->rows_max, c->stage_bytes).total <= budget) break;
+    if (tc1_layout(nst, pc * nw, c->rows_max, c->stage_bytes, nbuf).total <= budget) break;
   if (nst < 2) return false;
   c->part_chunks = pc;
+  c->builders = builders;
   c->nst = nst;
-  c->smem = static_cast<size_t>(tc1_layout(nst, pc * nw, c->rows_max, c->stage_bytes).total);
+  c->smem = static_cast<size_t>(tc1_layout(nst, pc * nw, c->rows_max, c->stage_bytes, nbuf).total);
   return true;
 }
 
@@ -717,11 +746,15 @@ inline cudaError_t launch_tc1(GemvParams p, const GemvRequest& r, const Tc1Confi
   p.tc_rg = kTc1Rows * c.mt;
   p.stage_stride = c.stage_bytes;
   p.nstage = c.nst;
-  const int threads = (c.nw + 1) * 32;
-  // two MMA tiles per warp: up to 8 compute warps; one: up to 15 compute
-  // warps run the 16-warp instantiation (128 registers), 16 the 17-warp one
-  auto kernel = c.mt == 2 ? gemv_tc1<Q, 8, 2>
-                          : (c.nw < kTc1MaxWarps ? gemv_tc1<Q, kTc1MaxWarps - 1, 1> : gemv_tc1<Q, kTc1MaxWarps, 1>);
+  const int threads = (c.nw + 1 + c.builders) * 32;
+  // two MMA tiles per warp: up to 8 compute warps (+ builder warps for rows
+  // in parts of k); one: up to 15 compute warps run the 16-warp
+  // instantiation (128 registers), 16 the 17-warp one
+  auto kernel = c.mt == 2 ? (c.builders == 2   ? gemv_tc1<Q, 8, 2, 2>
+                             : c.builders == 1 ? gemv_tc1<Q, 8, 2, 1>
+                                               : gemv_tc1<Q, 8, 2, 0>)
+                          : (c.nw < kTc1MaxWarps ? gemv_tc1<Q, kTc1MaxWarps - 1, 1, 0>
+                                                 : gemv_tc1<Q, kTc1MaxWarps, 1, 0>);
   int per_sm = 0;
   cudaError_t e = kernel_occupancy(reinterpret_cast<const void*>(kernel), r.device, threads, c.smem, &per_sm);
   if (e != cudaSuccess) return e;
