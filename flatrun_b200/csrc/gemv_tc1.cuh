@@ -74,6 +74,9 @@ namespace frc {
 constexpr int kTc1Rows = 16;         // rows of one MMA tile (the MMA's M)
 constexpr int kTc1MaxRows = 32;      // rows per row group, at most (two MMA tiles per warp)
 constexpr int kTc1MaxWarps = 16;     // compute warps (one super-block each per chunk)
+// compute warps of the widest two-tile instantiation: with the producer 12
+// warps, three per SM sub-partition, which leaves each up to 170 registers
+constexpr int kTc1MaxWarpsMt2 = 11;
 constexpr int kTc1Lanes = 12;        // lanes of a B fragment that carry x terms
 constexpr int kTc1FragBytes = 16 * kTc1Lanes * 8;  // per super-block: 16 MMAs x 12 lanes x 8 bytes
 constexpr int kTc1ZeroBytes = 16 * kTc1Lanes * 8;  // the zero B fragment of lanes >= 12

@@ -657,7 +657,11 @@ inline int tc1_grid(int64_t n, int sms, int rg) {
   return g < 1 ? 1 : static_cast<int>(g);
 }
 
-inline bool tc1_config(int k, int64_t n, int sms, bool long_rows, Tc1Config* c) {
+// swiglu: x is read as silu(x) * x_mul (the down projection's SwiGLU),
+// whose exponentials the 64 threads of the builder warps would form more
+// slowly than the compute warps (Qwen2-7B decode token: 2.85 ms with
+// builders against 2.79 without).
+inline bool tc1_config(int k, int64_t n, int sms, bool long_rows, bool swiglu, Tc1Config* c) {
   if (k % 256 != 0 || k <= 0 || sms < 1) return false;
   const int sbs = k / 256;
   const int mt = tc1_mt_for(k);
@@ -672,18 +676,30 @@ inline bool tc1_config(int k, int64_t n, int sms, bool long_rows, Tc1Config* c) 
       if (sbs % d == 0) nw = d;
     if (!nw) nw = maxw;
   }
-  const int forced = tuning().nwarps;
-  if (forced >= 1 && forced <= maxw) nw = forced;
-  c->nw = nw;
-  c->mt = mt;
-  c->nch = (sbs + nw - 1) / nw;
-  c->stride = tc1_row_stride(nw);
-  c->stage_bytes = round_up(kTc1Rows * mt * c->stride, 128);
   const int grid = tc1_grid(n, sms, kTc1Rows * mt);
   const int64_t rows_max = (n + grid - 1) / grid;
   if (rows_max > (1 << 20)) return false;
   c->rows_max = static_cast<int>(rows_max);
   const int budget = tuned(tuning().smem_bytes, kSmemBudget);
+  const int want = tuned(tuning().tc_stages, 3);
+  // two tiles per warp: 11 compute warps (three warps per SM sub-partition
+  // with the producer) where the chunks waste at most one super-block each
+  // and the whole row's fragments leave room for `want` stages.  Measured on
+  // B200 (Llama-3-70B, k = 8192, 3 chunks of 11, 11 and 10 super-blocks):
+  // gate+up 61.3 us against 64.2 with 8 warps (4 chunks of 8), q+k+v 18.5
+  // against 19.1; 9 or 10 warps (4 chunks) 69.6-72.9.
+  if (mt == 2 && sbs > kTc1MaxWarpsMt2) {
+    const int w = kTc1MaxWarpsMt2, ch = (sbs + w - 1) / w;
+    const int st = round_up(kTc1Rows * mt * tc1_row_stride(w), 128);
+    if (ch * w - sbs <= ch && tc1_layout(want, ch * w, c->rows_max, st).total <= budget) nw = w;
+  }
+  const int forced = tuning().nwarps;
+  if (forced >= 1 && forced <= (mt == 2 ? kTc1MaxWarpsMt2 : maxw)) nw = forced;
+  c->nw = nw;
+  c->mt = mt;
+  c->nch = (sbs + nw - 1) / nw;
+  c->stride = tc1_row_stride(nw);
+  c->stage_bytes = round_up(kTc1Rows * mt * c->stride, 128);
   // the whole row's fragments if they leave room for `want` stages, else
   // parts of k: with two tiles per warp two builder warps fill one fragment
   // buffer while the compute warps read the other, and each buffer holds as
@@ -692,12 +708,11 @@ inline bool tc1_config(int k, int64_t n, int sms, bool long_rows, Tc1Config* c) 
   // 41.6 at 3 stages x 4 parts, 41.7 at 4 x 5, 45.7 at 2 x 7 (one builder
   // warp 44.2, none 47.2 on the CUDA-core kernel); Qwen2-7B k = 18944 17.1 at
   // 3 x 3, 18.1 at 4 x 4, 18.9 at 2 x 2 without builders.
-  const int want = tuned(tuning().tc_stages, 3);
   int pc = 0, builders = 0;
   if (tc1_layout(want, c->nch * nw, c->rows_max, c->stage_bytes).total <= budget) {
     pc = c->nch;
   } else {
-    builders = mt == 2 ? tuned(tuning().tc_builders, 2) : 0;
+    builders = mt == 2 && nw <= 8 && !swiglu ? tuned(tuning().tc_builders, 2) : 0;
     if (builders > 2) builders = 2;
     const int nbuf = builders ? 2 : 1;
     const int forced_pc = tuning().tc_part_chunks;
@@ -752,6 +767,7 @@ inline cudaError_t launch_tc1(GemvParams p, const GemvRequest& r, const Tc1Confi
   // instantiation (128 registers), 16 the 17-warp one
   auto kernel = c.mt == 2 ? (c.builders == 2   ? gemv_tc1<Q, 8, 2, 2>
                              : c.builders == 1 ? gemv_tc1<Q, 8, 2, 1>
+                             : c.nw > 8        ? gemv_tc1<Q, kTc1MaxWarpsMt2, 2, 0>
                                                : gemv_tc1<Q, 8, 2, 0>)
                           : (c.nw < kTc1MaxWarps ? gemv_tc1<Q, kTc1MaxWarps - 1, 1, 0>
                                                  : gemv_tc1<Q, kTc1MaxWarps, 1, 0>);
@@ -857,7 +873,7 @@ cudaError_t launch_gemv(const GemvRequest& r) {
     if constexpr (Q == kQ4_K) {
       Tc1Config c;
       if (!opt(options().batch1_int16) && opt(options().batch1_tc) &&
-          tc1_config(r.k, b1.n, r.sms, opt(options().batch1_tc) == 2, &c))
+          tc1_config(r.k, b1.n, r.sms, opt(options().batch1_tc) == 2, r.x_mul != nullptr, &c))
         return launch_tc1<Q>(b1, r, c);
     }
     const cudaError_t e =
