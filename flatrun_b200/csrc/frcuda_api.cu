@@ -612,8 +612,8 @@ int frc_batch1_kernel(int quant, int64_t k, int* kind) {
   frc::Tc1Config c;
   if (frc::opt(o.batch1_int16)) {
     *kind = FRC_B1_INT16;
-  } else if (quant == FRC_Q4_K && frc::opt(o.batch1_tc) &&
-             frc::tc1_config(static_cast<int>(k), 148, 148, frc::opt(o.batch1_tc) == 2, false, &c)) {
+  } else if ((quant == FRC_Q4_K || quant == FRC_Q5_K) && frc::opt(o.batch1_tc) &&
+             frc::tc1_config(ts, static_cast<int>(k), 148, 148, frc::opt(o.batch1_tc) == 2, false, &c)) {
     *kind = FRC_B1_TENSOR_FP32;
   } else {
     *kind = FRC_B1_CUDA_CORE_FP32;

@@ -1,5 +1,5 @@
 // Batch-1 GEMV on the tensor cores with exact fp32 activations: gemv_tc1<Q>
-// (Q4_K).
+// (Q4_K, and Q5_K with its fifth bits joined to the nibbles, see tc1_sb).
 //
 // The reference multiplies dequantised fp32 weights by fp32 x and sums in
 // fp32 (src/flatrun_native/kernels/q4_k.h:153-184; the NumPy path is dequant
@@ -109,11 +109,12 @@ __host__ __device__ inline Tc1Layout tc1_layout(int nst, int psb, int rows, int 
 
 // Row stride of a stage: the chunk's bytes, dense (the layout a 3-D tensor
 // copy of 16 rows x kc super-blocks lands in).
-__host__ __device__ constexpr int tc1_row_stride(int kc) { return kc * 144; }
+__host__ __device__ constexpr int tc1_row_stride(int kc, int ts) { return kc * ts; }
 
 // Tensor maps per matrix of the launch: the matrix as a 3-D tensor of 8-byte
-// words [rows][super-blocks][18] (strides row_bytes and 144 bytes), with
-// boxes of kc super-blocks x 18 words and 32, 16, 8, 4, 2 or 1 rows: a whole
+// words [rows][super-blocks][TS / 8] (strides row_bytes and TS bytes: 144
+// for Q4_K, 176 for Q5_K), with boxes of kc super-blocks x TS / 8 words
+// and 32, 16, 8, 4, 2 or 1 rows: a whole
 // row group is one copy, a short one (a matrix or CTA end) one copy per set
 // bit of its row count.
 constexpr int kTc1Boxes = 6;  // rows 32 >> b for b < kTc1Boxes
@@ -231,18 +232,27 @@ FRC_DEVICE_INLINE void tc1_q4k_scales(const uint4& h, uint32_t sh, bool hi_t, ui
 // fragment), fragments 2i and 2i + 1 at xf + 192 i; sums: the super-block's
 // 8 sub-block sums.  acc[2m], acc[2m+1] (rows g + 16 m, g + 8 + 16 m) gain
 // d / s times the column sums; mn[...] gain dmin times the min terms.
-template <int MT>
-FRC_DEVICE_INLINE void tc1_q4k_sb(uint32_t row, uint32_t stride, uint32_t xf, uint32_t sums, float inv_s, int t,
+//
+// Q5_K (gguf.py:223-263) has the Q4_K header and nibbles (at byte 48) plus
+// qh[32] at byte 16, whose bit 2t (2t + 1) of byte i is the fifth bit of
+// element i of sub-block 2t (2t + 1).  The bit joins the fp16 lane below the
+// bias: at bit 4 beside a low nibble (1024 + q), at bit 8 beside a high
+// nibble (1024 + 16 q), so the same HFMA2 gives q sc exactly (q sc <= 31 x
+// 63 = 1953; the fused product-add rounds once, at the exact result).
+template <int Q, int MT>
+FRC_DEVICE_INLINE void tc1_sb(uint32_t row, uint32_t stride, uint32_t xf, uint32_t sums, float inv_s, int t,
                                   uint32_t sh, bool hi_t, uint32_t m1, uint32_t m2, uint32_t bias, float (&acc)[2 * MT],
                                   float (&mn)[2 * MT]) {
   constexpr int R = 2 * MT;  // rows of this thread
+  constexpr bool Q5 = Q == kQ5_K;
+  constexpr uint32_t kQsOff = Q5 ? 48u : 16u;
   uint4 hd[R];
   uint32_t q[R], sl[R], nl[R], sg[R], ng[R], mw[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const uint32_t ra = row + static_cast<uint32_t>(8 * r) * stride;  // rows g, g + 8, g + 16, g + 24
     hd[r] = lds128f<0>(ra);
-    q[r] = ra + 16u + 32u * static_cast<uint32_t>(t);
+    q[r] = ra + kQsOff + 32u * static_cast<uint32_t>(t);
     uint32_t sc;
     tc1_q4k_scales(hd[r], sh, hi_t, m1, m2, sc, mw[r]);
     // (sc, sc) of the low sub-block, and (sc/16, sc/16) of the high one,
@@ -258,7 +268,7 @@ FRC_DEVICE_INLINE void tc1_q4k_sb(uint32_t row, uint32_t stride, uint32_t xf, ui
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     // words 4 half .. 4 half + 3 of chunk t in each row
-    uint32_t w[R][4];
+    uint32_t w[R][4], hq[R][4];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const uint4 a = half ? lds128f<16>(q[r]) : lds128f<0>(q[r]);
@@ -266,6 +276,16 @@ FRC_DEVICE_INLINE void tc1_q4k_sb(uint32_t row, uint32_t stride, uint32_t xf, ui
       w[r][1] = a.y;
       w[r][2] = a.z;
       w[r][3] = a.w;
+      if constexpr (Q5) {
+        // qh bytes 16 half .. 16 half + 15 (row start + 16), bits of
+        // sub-blocks 2t, 2t + 1 moved to bits 0 and 1 of each byte
+        const uint32_t qa = q[r] - kQsOff - 32u * static_cast<uint32_t>(t) + 16u;
+        const uint4 b = half ? lds128f<16>(qa) : lds128f<0>(qa);
+        hq[r][0] = b.x >> (2 * t);
+        hq[r][1] = b.y >> (2 * t);
+        hq[r][2] = b.z >> (2 * t);
+        hq[r][3] = b.w >> (2 * t);
+      }
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -277,19 +297,32 @@ FRC_DEVICE_INLINE void tc1_q4k_sb(uint32_t row, uint32_t stride, uint32_t xf, ui
         const uint32_t x0 = w[2 * m][j], x8 = w[2 * m + 1][j];
         const uint32_t s0 = x0 >> 8, s8 = x8 >> 8;
         const int r0 = 2 * m, r8 = 2 * m + 1;
-        const uint32_t l0 = hfma2_u((x0 & 0x000F000Fu) | bias, sl[r0], nl[r0]);
-        const uint32_t l1 = hfma2_u((x8 & 0x000F000Fu) | bias, sl[r8], nl[r8]);
-        const uint32_t l2 = hfma2_u((s0 & 0x000F000Fu) | bias, sl[r0], nl[r0]);
-        const uint32_t l3 = hfma2_u((s8 & 0x000F000Fu) | bias, sl[r8], nl[r8]);
+        // the bias of each lane pair, with Q5_K's fifth bits below it
+        uint32_t bl0 = bias, bl8 = bias, bs0 = bias, bs8 = bias, hl0 = bias, hl8 = bias, hs0 = bias, hs8 = bias;
+        if constexpr (Q5) {
+          const uint32_t h0 = hq[r0][j], h8 = hq[r8][j];
+          bl0 = ((h0 << 4) & 0x00100010u) | bias;  // bytes 0, 2: bit 0 -> bit 4
+          bl8 = ((h8 << 4) & 0x00100010u) | bias;
+          bs0 = ((h0 >> 4) & 0x00100010u) | bias;  // bytes 1, 3: bit 8 -> bit 4
+          bs8 = ((h8 >> 4) & 0x00100010u) | bias;
+          hl0 = ((h0 << 7) & 0x01000100u) | bias;  // bytes 0, 2: bit 1 -> bit 8
+          hl8 = ((h8 << 7) & 0x01000100u) | bias;
+          hs0 = ((h0 >> 1) & 0x01000100u) | bias;  // bytes 1, 3: bit 9 -> bit 8
+          hs8 = ((h8 >> 1) & 0x01000100u) | bias;
+        }
+        const uint32_t l0 = hfma2_u((x0 & 0x000F000Fu) | bl0, sl[r0], nl[r0]);
+        const uint32_t l1 = hfma2_u((x8 & 0x000F000Fu) | bl8, sl[r8], nl[r8]);
+        const uint32_t l2 = hfma2_u((s0 & 0x000F000Fu) | bs0, sl[r0], nl[r0]);
+        const uint32_t l3 = hfma2_u((s8 & 0x000F000Fu) | bs8, sl[r8], nl[r8]);
         if (i == 0) {
           mma_f16_16816_z(c[m], l0, l1, l2, l3, b.x, b.y);
         } else {
           mma_f16_16816(c[m], l0, l1, l2, l3, b.x, b.y);
         }
-        mma_f16_16816(c[m], hfma2_u((x0 & 0x00F000F0u) | bias, sg[r0], ng[r0]),
-                      hfma2_u((x8 & 0x00F000F0u) | bias, sg[r8], ng[r8]),
-                      hfma2_u((s0 & 0x00F000F0u) | bias, sg[r0], ng[r0]),
-                      hfma2_u((s8 & 0x00F000F0u) | bias, sg[r8], ng[r8]), b.z, b.w);
+        mma_f16_16816(c[m], hfma2_u((x0 & 0x00F000F0u) | hl0, sg[r0], ng[r0]),
+                      hfma2_u((x8 & 0x00F000F0u) | hl8, sg[r8], ng[r8]),
+                      hfma2_u((s0 & 0x00F000F0u) | hs0, sg[r0], ng[r0]),
+                      hfma2_u((s8 & 0x00F000F0u) | hs8, sg[r8], ng[r8]), b.z, b.w);
       }
     }
   }
@@ -358,6 +391,7 @@ struct Tc1Cursor {
   int part;    // current part of k
 };
 
+template <int TS>
 FRC_DEVICE_INLINE void tc1_issue(const GemvParams& p, const Tc1Maps& maps, Tc1Cursor& c, int64_t c0, int64_t c1,
                                  uint8_t* dst, uint64_t* bar) {
   const int pc = p.tc_part_chunks;
@@ -371,9 +405,9 @@ FRC_DEVICE_INLINE void tc1_issue(const GemvParams& p, const Tc1Maps& maps, Tc1Cu
   // landing on a 128-byte boundary of the stage as tensor copies require;
   // rows left after the first box that would not are copied one bulk copy
   // per row (16-byte aligned)
-  const uint32_t box_bytes = static_cast<uint32_t>(kc * 144);
+  const uint32_t box_bytes = static_cast<uint32_t>(kc * TS);
   const int nsb = (c.ch + 1) * kc <= sbs ? kc : sbs - c.ch * kc;
-  const uint32_t cb = static_cast<uint32_t>(nsb) * 144u;
+  const uint32_t cb = static_cast<uint32_t>(nsb) * TS;
   int r0 = 0;
   uint32_t tx = 0;
   int nbox = 0, boxes[kTc1Boxes], starts[kTc1Boxes];
@@ -397,7 +431,7 @@ FRC_DEVICE_INLINE void tc1_issue(const GemvParams& p, const Tc1Maps& maps, Tc1Cu
   }
   if (r0 < c.rows) {
     const uint8_t* src = p.mat_w[c.T.m] + static_cast<uint64_t>(c.T.local + r0) * p.row_bytes +
-                         static_cast<uint64_t>(c.ch) * kc * 144;
+                         static_cast<uint64_t>(c.ch) * kc * TS;
     for (int r = r0; r < c.rows; ++r)
       bulk_g2s(dst + r * p.tc_stride, src + static_cast<uint64_t>(r - r0) * p.row_bytes, cb, bar);
   }
@@ -475,7 +509,8 @@ FRC_DEVICE_INLINE void tc1_build(const GemvParams& p, int sb0, int sb1, int tid,
 template <int Q, int MAXW, int MT, int NB>
 __global__ void __launch_bounds__((MAXW + 1 + NB) * 32, 1) gemv_tc1(const __grid_constant__ Tc1Maps maps,
                                                                    GemvParams p) {
-  static_assert(Q == kQ4_K, "gemv_tc1 covers Q4_K");
+  static_assert(Q == kQ4_K || Q == kQ5_K, "gemv_tc1 covers Q4_K and Q5_K");
+  constexpr int TS = Fmt<Q>::TS;
   static_assert(MT == 1 || MT == 2, "one or two MMA tiles per warp");
   constexpr int RG = kTc1Rows * MT;
   static_assert(MAXW <= kTc1MaxWarps, "reduction buffers hold kTc1MaxWarps warps");
@@ -544,7 +579,7 @@ __global__ void __launch_bounds__((MAXW + 1 + NB) * 32, 1) gemv_tc1(const __grid
           atomicOr(p.status, kStatusEmptyWaitTimeout);
           break;
         }
-        tc1_issue(p, maps, cur, c0, c1, stages + si * stage_bytes, &full[si]);
+        tc1_issue<TS>(p, maps, cur, c0, c1, stages + si * stage_bytes, &full[si]);
       }
       // the last stage-full of copies must land before the CTA may exit
       int zero = 0;
@@ -635,7 +670,7 @@ __global__ void __launch_bounds__((MAXW + 1 + NB) * 32, 1) gemv_tc1(const __grid
   const uint32_t xf_lane = lane < kTc1Lanes ? frag_base + static_cast<uint32_t>(lane) * 16u : zero_base;
   const uint32_t xf_step = lane < kTc1Lanes ? static_cast<uint32_t>(kTc1FragBytes) : 0u;
   const uint32_t stride = static_cast<uint32_t>(p.tc_stride);
-  const uint32_t row_lane = smem_u32(stages) + static_cast<uint32_t>(g) * stride + static_cast<uint32_t>(warp) * 144u;
+  const uint32_t row_lane = smem_u32(stages) + static_cast<uint32_t>(g) * stride + static_cast<uint32_t>(warp) * TS;
   const uint32_t sums_s = smem_u32(sums), invs_s = smem_u32(invs);
   int s = 0;
   uint32_t ph = 0u;
@@ -671,7 +706,7 @@ __global__ void __launch_bounds__((MAXW + 1 + NB) * 32, 1) gemv_tc1(const __grid
         if (wait_phase(&full[s], ph, abort)) {
           if (sb < sbs && frags_ok) {
             const uint32_t lsb = static_cast<uint32_t>(sb - sb0);
-            tc1_q4k_sb<MT>(row_lane + static_cast<uint32_t>(s * stage_bytes), stride, xf_part + lsb * xf_step,
+            tc1_sb<Q, MT>(row_lane + static_cast<uint32_t>(s * stage_bytes), stride, xf_part + lsb * xf_step,
                            sums_part + lsb * 32u, ldsf(invs_part + 4u * lsb), t, sh, hi_t, m1, m2, p.tc_bias, acc,
                            mn);
           }

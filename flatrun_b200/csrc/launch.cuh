@@ -661,7 +661,7 @@ inline int tc1_grid(int64_t n, int sms, int rg) {
 // whose exponentials the 64 threads of the builder warps would form more
 // slowly than the compute warps (Qwen2-7B decode token: 2.85 ms with
 // builders against 2.79 without).
-inline bool tc1_config(int k, int64_t n, int sms, bool long_rows, bool swiglu, Tc1Config* c) {
+inline bool tc1_config(int ts, int k, int64_t n, int sms, bool long_rows, bool swiglu, Tc1Config* c) {
   if (k % 256 != 0 || k <= 0 || sms < 1) return false;
   const int sbs = k / 256;
   const int mt = tc1_mt_for(k);
@@ -690,7 +690,7 @@ inline bool tc1_config(int k, int64_t n, int sms, bool long_rows, bool swiglu, T
   // against 19.1; 9 or 10 warps (4 chunks) 69.6-72.9.
   if (mt == 2 && sbs > kTc1MaxWarpsMt2) {
     const int w = kTc1MaxWarpsMt2, ch = (sbs + w - 1) / w;
-    const int st = round_up(kTc1Rows * mt * tc1_row_stride(w), 128);
+    const int st = round_up(kTc1Rows * mt * tc1_row_stride(w, ts), 128);
     if (ch * w - sbs <= ch && tc1_layout(want, ch * w, c->rows_max, st).total <= budget) nw = w;
   }
   const int forced = tuning().nwarps;
@@ -698,7 +698,7 @@ inline bool tc1_config(int k, int64_t n, int sms, bool long_rows, bool swiglu, T
   c->nw = nw;
   c->mt = mt;
   c->nch = (sbs + nw - 1) / nw;
-  c->stride = tc1_row_stride(nw);
+  c->stride = tc1_row_stride(nw, ts);
   c->stage_bytes = round_up(kTc1Rows * mt * c->stride, 128);
   // the whole row's fragments if they leave room for `want` stages, else
   // parts of k: with two tiles per warp two builder warps fill one fragment
@@ -775,7 +775,8 @@ inline cudaError_t launch_tc1(GemvParams p, const GemvRequest& r, const Tc1Confi
   cudaError_t e = kernel_occupancy(reinterpret_cast<const void*>(kernel), r.device, threads, c.smem, &per_sm);
   if (e != cudaSuccess) return e;
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
-  // one tensor map per matrix: [rows][super-blocks][18 x 8 bytes]
+  // one tensor map per matrix: [rows][super-blocks][TS / 8 words of 8 bytes]
+  constexpr int TS = Fmt<Q>::TS;
   Tc1Maps maps;
   std::memset(&maps, 0, sizeof(maps));
   auto encode = tensor_map_encoder();
@@ -783,11 +784,11 @@ inline cudaError_t launch_tc1(GemvParams p, const GemvRequest& r, const Tc1Confi
   const int sbs = p.k / 256;
   for (int m = 0; m < p.nmat; ++m) {
     const int64_t rows = p.mat_end[m] - (m ? p.mat_end[m - 1] : 0);
-    const cuuint64_t dims[3] = {18, static_cast<cuuint64_t>(sbs), static_cast<cuuint64_t>(rows > 0 ? rows : 1)};
-    const cuuint64_t strides[2] = {144, static_cast<cuuint64_t>(p.row_bytes)};
+    const cuuint64_t dims[3] = {TS / 8, static_cast<cuuint64_t>(sbs), static_cast<cuuint64_t>(rows > 0 ? rows : 1)};
+    const cuuint64_t strides[2] = {TS, static_cast<cuuint64_t>(p.row_bytes)};
     const cuuint32_t estr[3] = {1, 1, 1};
     for (int b = 0; b < kTc1Boxes; ++b) {
-      const cuuint32_t box[3] = {18, static_cast<cuuint32_t>(c.nw), static_cast<cuuint32_t>(kTc1MaxRows >> b)};
+      const cuuint32_t box[3] = {TS / 8, static_cast<cuuint32_t>(c.nw), static_cast<cuuint32_t>(kTc1MaxRows >> b)};
       if (encode(&maps.m[m][b], CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<uint8_t*>(p.mat_w[m]), dims, strides,
                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
@@ -870,10 +871,10 @@ cudaError_t launch_gemv(const GemvRequest& r) {
   if (r.batch == 1) {
     GemvParams b1 = p;
     b1.units = (r.k / F::QK) * I8<Q>::UPB;
-    if constexpr (Q == kQ4_K) {
+    if constexpr (Q == kQ4_K || Q == kQ5_K) {
       Tc1Config c;
       if (!opt(options().batch1_int16) && opt(options().batch1_tc) &&
-          tc1_config(r.k, b1.n, r.sms, opt(options().batch1_tc) == 2, r.x_mul != nullptr, &c))
+          tc1_config(Fmt<Q>::TS, r.k, b1.n, r.sms, opt(options().batch1_tc) == 2, r.x_mul != nullptr, &c))
         return launch_tc1<Q>(b1, r, c);
     }
     const cudaError_t e =

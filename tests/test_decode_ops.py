@@ -53,15 +53,17 @@ def _rope_ref(x, pos, cos, sin):
     return np.concatenate([a * c - b * s, b * c + a * s], axis=-1)
 
 
-def test_rope_append_and_attention_match_numpy(cuda_backend):
+@pytest.mark.parametrize("hd,past,splits", [(128, 777, 37), (128, 777, 1), (64, 300, 5), (128, 40, 64)])
+def test_rope_append_and_attention_match_numpy(cuda_backend, hd, past, splits):
     """Bias + rotate-half RoPE at the device position, the cache append, and
-    GQA decode attention (28 query / 4 KV heads of 128, 777 cached
-    positions, split over 37 ranges) against the reference's NumPy steps
-    (qwen2.py:1527-1614)."""
+    GQA decode attention (28 query / 4 KV heads) against the reference's
+    NumPy steps (qwen2.py:1527-1614): 778 positions over 37 ranges, over
+    one range (four passes of positions), head dim 64, and more ranges than
+    positions (empty ranges)."""
     from flatrun_b200.decode import rope_tables
     lib = _lib.load()
-    nh, nkv, hd, past = 28, 4, 128, 777
-    rng = np.random.default_rng(2)
+    nh, nkv = 28, 4
+    rng = np.random.default_rng(2 + hd + past + splits)
     cos, sin = rope_tables(hd, 1e6, 1024)
     kc = np.zeros((1024, nkv, hd), np.float32)
     vc = np.zeros((1024, nkv, hd), np.float32)
@@ -81,7 +83,6 @@ def test_rope_append_and_attention_match_numpy(cuda_backend):
     np.testing.assert_allclose(_np(qkv_d)[:nh * hd].reshape(nh, hd), q, rtol=1e-6, atol=1e-6)
     np.testing.assert_allclose(_np(kc_d)[past], k, rtol=1e-6, atol=1e-6)
     np.testing.assert_array_equal(_np(vc_d)[past], v)
-    splits = 37
     ws = ctypes.c_size_t()
     _lib.check(lib.frc_attention_workspace(nh, hd, splits, ctypes.byref(ws)), lib)
     import torch

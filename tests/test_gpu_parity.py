@@ -336,37 +336,41 @@ TC1_SHAPES = [(1, 256), (15, 512), (16, 2304), (17, 3584), (33, 4096), (300, 512
               (64, 36864)]
 
 
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q5_K"])
 @pytest.mark.parametrize("n,k", TC1_SHAPES)
-def test_batch1_tensor_core_q4k(cuda_backend, n, k):
-    """Q4_K batch 1 on the tensor-core kernel (weights as exact fp16 integers,
-    x as an exact sum of three fp16 terms, fp32 accumulation; batch1_tc = 1
-    and 2) and on the CUDA-core fp32 kernel (batch1_tc = 0): each within the
-    fp32 tolerance of fp64, normalised by the term magnitude (few rows can
-    cancel)."""
-    raw = synth.make_weight("Q4_K", n, k, seed=k + n)
+def test_batch1_tensor_core(cuda_backend, fmt, n, k):
+    """Q4_K and Q5_K batch 1 on the tensor-core kernel (weights as exact fp16
+    integers q sc, x as an exact sum of three fp16 terms, fp32 accumulation;
+    batch1_tc = 1 and 2) and on the CUDA-core fp32 kernel (batch1_tc = 0):
+    each within the fp32 tolerance of fp64, normalised by the term magnitude
+    (few rows can cancel).  The random blocks carry the largest q sc (Q5_K:
+    31 x 63) and every fifth-bit pattern."""
+    raw = synth.make_weight(fmt, n, k, seed=k + n)
     x = synth.make_x(k, seed=k - n)
-    ref = O.matvec_fp64("Q4_K", raw, x, n, k)
-    scale = O.term_scale("Q4_K", raw, x, n, k)
+    ref = O.matvec_fp64(fmt, raw, x, n, k)
+    scale = O.term_scale(fmt, raw, x, n, k)
     for tc in (1, 2, 0):
         with _lib.option("batch1_tc", tc):
-            y = cuda_backend.weight(raw, n, k, "Q4_K").matmul(x)
-        assert O.norm_err(y, ref, scale) < 5e-6, (n, k, tc)
-        assert O.rel_err(y, ref) < TOL, (n, k, tc)
+            assert _lib.batch1_kernel(fmt, k) == ("tensor_fp32" if tc else "cuda_core_fp32")
+            y = cuda_backend.weight(raw, n, k, fmt).matmul(x)
+        assert O.norm_err(y, ref, scale) < 5e-6, (fmt, n, k, tc)
+        assert O.rel_err(y, ref) < TOL, (fmt, n, k, tc)
     cuda_backend.close()
 
 
-def test_batch1_tensor_core_q4k_wide_range(cuda_backend):
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q5_K"])
+def test_batch1_tensor_core_wide_range(cuda_backend, fmt):
     """Activations spanning 60 decades, runs of exact zeros and sign changes:
     each super-block takes its own power-of-two scale, so the three fp16 terms
     stay exact where the magnitude matters."""
     n, k = 256, 4096
-    raw = synth.make_weight("Q4_K", n, k, seed=7)
+    raw = synth.make_weight(fmt, n, k, seed=7)
     rng = np.random.default_rng(8)
     x = (rng.standard_normal(k) * 10.0 ** rng.uniform(-30, 30, k)).astype(np.float32)
     x[100:300] = 0.0
-    y = cuda_backend.weight(raw, n, k, "Q4_K").matmul(x)
-    ref = O.matvec_fp64("Q4_K", raw, x, n, k)
-    assert O.norm_err(y, ref, O.term_scale("Q4_K", raw, x, n, k)) < 1e-6
+    y = cuda_backend.weight(raw, n, k, fmt).matmul(x)
+    ref = O.matvec_fp64(fmt, raw, x, n, k)
+    assert O.norm_err(y, ref, O.term_scale(fmt, raw, x, n, k)) < 1e-6
     cuda_backend.close()
 
 
