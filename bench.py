@@ -523,6 +523,8 @@ def main() -> None:
                     help="batch-1 Q4_K on the CUDA-core fp32 kernel instead of the tensor-core one (same arithmetic)")
     ap.add_argument("--tc-long-rows", action="store_true",
                     help="batch-1 Q4_K rows longer than one part of k on the tensor-core kernel too (FRC_OPT_BATCH1_TC=2)")
+    ap.add_argument("--batched-fp32", action="store_true",
+                    help="batch 2..16 on the fp32-activation CUDA-core kernel (gemv_xb) instead of the int8 tensor-core one")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -592,6 +594,8 @@ def main() -> None:
     lib = _lib.load()
     if args.batch1_int16:
         _lib.set_option("batch1_int16", 1)
+    if args.batched_fp32:
+        _lib.set_option("batched_fp32", 1)
     if args.cuda_core:
         _lib.set_option("batch1_tc", 0)
     elif args.tc_long_rows:
@@ -923,6 +927,8 @@ def main() -> None:
             else:
                 kname = "gemv_b1 (fp32 activations, fp32 FMAs)"
             dtype, calls_per_group = "f32", lambda g: 1
+        elif batch <= 16 and args.batched_fp32:
+            kname, dtype, calls_per_group = "gemv_xb (fp32 activations, fp32 FMAs)", "f32", lambda g: len(g)
         elif batch <= 16:
             kname, dtype, calls_per_group = "gemv_mma", "s8 x s8 -> s32 (mma.sync), fp32 scales", lambda g: 2 * len(g)
         else:

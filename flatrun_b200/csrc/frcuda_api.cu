@@ -356,6 +356,21 @@ int finish_host_call(DeviceState* ds) {
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
+// True if [p, p + bytes) is page-locked host memory (cudaHostAlloc,
+// cudaHostRegister, torch's pin_memory): both ends are looked up, since a
+// contiguous buffer lies inside one allocation.
+bool host_pinned(const void* p, size_t bytes) {
+  for (const void* q : {p, static_cast<const void*>(static_cast<const uint8_t*>(p) + bytes - 1)}) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, q) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return false;
+    }
+    if (a.type != cudaMemoryTypeHost) return false;
+  }
+  return true;
+}
+
 // Host-buffer matmul on device `dev` with weight bytes already at `w_dev`
 // (or, if w_host is non-null, uploaded into scratch first).
 int host_matmul(DeviceState* ds, int quant, const uint8_t* w_dev, const uint8_t* w_host, size_t w_bytes, int64_t n,
@@ -375,16 +390,22 @@ int host_matmul(DeviceState* ds, int quant, const uint8_t* w_dev, const uint8_t*
   rc = ensure(&ds->scratch_y, &ds->cap_y, sizeof(float) * seq * (n ? n : 1), "cudaMalloc(y scratch)");
   if (rc) return rc;
   const size_t xb = sizeof(float) * seq * k, yb = sizeof(float) * seq * n;
-  const bool staged = xb <= kPinnedStageMax && yb <= kPinnedStageMax;
+  // page-locked x and y are the DMA source and target themselves; the rest
+  // go through the library's pinned staging (one host copy each)
+  const bool x_direct = xb == 0 || host_pinned(x, xb);
+  const bool y_direct = yb == 0 || host_pinned(y, yb);
+  const size_t x_stage_bytes = x_direct ? 0 : (xb + 255) / 256 * 256, y_stage_bytes = y_direct ? 0 : yb;
+  const bool staged = x_stage_bytes + y_stage_bytes > 0 && x_stage_bytes + y_stage_bytes <= kPinnedStageMax;
   uint8_t* stage = nullptr;
   if (staged) {
-    rc = pinned_stage(ds, (xb + 255) / 256 * 256 + yb, &stage);
+    rc = pinned_stage(ds, x_stage_bytes + y_stage_bytes, &stage);
     if (rc) return rc;
   }
-  float* y_stage = staged ? reinterpret_cast<float*>(stage + (xb + 255) / 256 * 256) : y;
+  const bool y_staged = staged && !y_direct;
+  float* y_dst = y_staged ? reinterpret_cast<float*>(stage + x_stage_bytes) : y;
   if (xb) {
     const void* src = x;
-    if (staged) {
+    if (staged && !x_direct) {
       std::memcpy(stage, x, xb);
       src = stage;
     }
@@ -392,9 +413,9 @@ int host_matmul(DeviceState* ds, int quant, const uint8_t* w_dev, const uint8_t*
   }
   rc = gemv_device(ds, quant, w_dev, n, k, ds->scratch_x, seq, ds->scratch_y, ds->stream);
   if (rc) return rc;
-  if (yb) FRC_CUDA(cudaMemcpyAsync(y_stage, ds->scratch_y, yb, cudaMemcpyDeviceToHost, ds->stream), "y download");
+  if (yb) FRC_CUDA(cudaMemcpyAsync(y_dst, ds->scratch_y, yb, cudaMemcpyDeviceToHost, ds->stream), "y download");
   rc = finish_host_call(ds);
-  if (rc == FRC_OK && staged && yb) std::memcpy(y, y_stage, yb);
+  if (rc == FRC_OK && y_staged) std::memcpy(y, y_dst, yb);
   return rc;
 }
 

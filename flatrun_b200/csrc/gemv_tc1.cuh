@@ -67,6 +67,8 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 #include "gemv.cuh"
 
 namespace frc {
@@ -701,24 +703,44 @@ __global__ void __launch_bounds__((MAXW + 1 + NB) * 32, 1) gemv_tc1(const __grid
       float acc[2 * MT], mn[2 * MT];
 #pragma unroll
       for (int r = 0; r < 2 * MT; ++r) acc[r] = mn[r] = 0.f;
-      for (int ch = ch0; ch < ch1; ++ch) {
-        const int sb = ch * kc + warp;  // this warp's super-block of the chunk
-        if (wait_phase(&full[s], ph, abort)) {
-          if (sb < sbs && frags_ok) {
-            const uint32_t lsb = static_cast<uint32_t>(sb - sb0);
-            tc1_sb<Q, MT>(row_lane + static_cast<uint32_t>(s * stage_bytes), stride, xf_part + lsb * xf_step,
-                           sums_part + lsb * 32u, ldsf(invs_part + 4u * lsb), t, sh, hi_t, m1, m2, p.tc_bias, acc,
-                           mn);
+      // the row group's chunks with M MMA tiles per warp (a: 2 M row sums,
+      // b: 2 M min terms)
+      auto run_chunks = [&](auto& a, auto& b) {
+        constexpr int M = std::extent<std::remove_reference_t<decltype(a)>>::value / 2;
+        for (int ch = ch0; ch < ch1; ++ch) {
+          const int sb = ch * kc + warp;  // this warp's super-block of the chunk
+          if (wait_phase(&full[s], ph, abort)) {
+            if (sb < sbs && frags_ok) {
+              const uint32_t lsb = static_cast<uint32_t>(sb - sb0);
+              tc1_sb<Q, M>(row_lane + static_cast<uint32_t>(s * stage_bytes), stride, xf_part + lsb * xf_step,
+                           sums_part + lsb * 32u, ldsf(invs_part + 4u * lsb), t, sh, hi_t, m1, m2, p.tc_bias, a, b);
+            }
+          } else if (lane == 0) {
+            atomicOr(p.status, kStatusFullWaitTimeout);
           }
-        } else if (lane == 0) {
-          atomicOr(p.status, kStatusFullWaitTimeout);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
+          if (++s == nst) {
+            s = 0;
+            ph ^= 1u;
+          }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        if (++s == nst) {
-          s = 0;
-          ph ^= 1u;
-        }
+      };
+      // a row group of at most 16 rows (the short last group of a CTA or a
+      // matrix) converts and multiplies its first MMA tile only: half the
+      // work of a full group (Llama-3-70B gate+up: each CTA's 388 rows are
+      // 12 groups of 32 and one of 4)
+      bool one_tile = false;
+      if constexpr (MT == 2) one_tile = rows <= kTc1Rows;
+      if (one_tile) {
+        float a1[2] = {0.f, 0.f}, b1[2] = {0.f, 0.f};
+        run_chunks(a1, b1);
+        acc[0] = a1[0];
+        acc[1] = a1[1];
+        mn[0] = b1[0];
+        mn[1] = b1[1];
+      } else {
+        run_chunks(acc, mn);
       }
       // rows g + 8 r: the four lanes t of a row, then the warps
       float* rb = red + par * kTc1MaxWarps * RG;

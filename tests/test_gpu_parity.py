@@ -332,8 +332,11 @@ def test_batch1_activation_outliers(cuda_backend, fmt, int16):
 # part of k (18944: 74 super-blocks, chunks of 16 with a ragged last one, in
 # two parts; 36864: three parts), which batch1_tc = 2 runs on the tensor
 # cores and the default leaves on the CUDA-core kernel
+# (15, 512), (33, 4096), (33, 18944) (rows in parts of k) and (5328, 4096)
+# (148 CTAs of 36 rows: 32 + 4) end a CTA with a row group of at most 16
+# rows, which converts one MMA tile only
 TC1_SHAPES = [(1, 256), (15, 512), (16, 2304), (17, 3584), (33, 4096), (300, 5120), (100, 8192), (37, 18944),
-              (64, 36864)]
+              (33, 18944), (64, 36864), (5328, 4096)]
 
 
 @pytest.mark.parametrize("fmt", ["Q4_K", "Q5_K"])
@@ -346,7 +349,7 @@ def test_batch1_tensor_core(cuda_backend, fmt, n, k):
     (few rows can cancel).  The random blocks carry the largest q sc (Q5_K:
     31 x 63) and every fifth-bit pattern."""
     raw = synth.make_weight(fmt, n, k, seed=k + n)
-    x = synth.make_x(k, seed=k - n)
+    x = synth.make_x(k, seed=abs(k - n))
     ref = O.matvec_fp64(fmt, raw, x, n, k)
     scale = O.term_scale(fmt, raw, x, n, k)
     for tc in (1, 2, 0):
