@@ -135,6 +135,11 @@ struct DeviceState {
   // by the driver through its own buffer, one synchronous copy per call)
   uint8_t* pinned = nullptr;
   size_t cap_pinned = 0;
+  // device result of a host-buffer matmul: a kHostOutHead-byte head whose
+  // first word is the call's own status word (zero between calls), then y;
+  // one device-to-host copy returns both
+  uint8_t* host_out = nullptr;
+  size_t cap_host_out = 0;
   // activation records of the batched tensor-core kernel: grown on demand and
   // never freed while the process runs, so work already queued (or captured
   // in a graph) keeps a valid pointer after a larger call replaces it
@@ -261,7 +266,8 @@ int launch_gemv_quant(int quant, const frc::GemvRequest& r) {
 
 // y (seq, n) = x (seq, k) . W^T on `stream`, all pointers on device `ds`.
 int gemv_device(DeviceState* ds, int quant, const uint8_t* w, int64_t n, int64_t k, const float* x, int64_t seq,
-                float* y, cudaStream_t stream) {
+                float* y, cudaStream_t stream, uint32_t* status = nullptr) {
+  if (!status) status = ds->status;
   if (n == 0) return FRC_OK;
   if (k == 0) {
     FRC_CUDA(cudaMemsetAsync(y, 0, sizeof(float) * n * seq, stream), "cudaMemsetAsync");
@@ -277,7 +283,7 @@ int gemv_device(DeviceState* ds, int quant, const uint8_t* w, int64_t n, int64_t
     r.n = n;
     r.k = static_cast<int>(k);
     r.batch = static_cast<int>(seq);
-    r.status = ds->status;
+    r.status = status;
     r.stream = stream;
     r.device = ds->device;
     r.sms = ds->sms;
@@ -310,7 +316,7 @@ int gemv_device(DeviceState* ds, int quant, const uint8_t* w, int64_t n, int64_t
     r.n = n;
     r.k = static_cast<int>(k);
     r.batch = static_cast<int>(cb);
-    r.status = ds->status;
+    r.status = status;
     r.stream = stream;
     r.device = ds->device;
     r.sms = ds->sms;
@@ -371,8 +377,25 @@ bool host_pinned(const void* p, size_t bytes) {
   return true;
 }
 
+constexpr size_t kHostOutHead = 256;
+
+// The device result buffer of host-buffer matmuls, at least kHostOutHead +
+// y_bytes; a new buffer's status word starts at zero (the memset is queued
+// before any kernel that may set it).  The old buffer is free: host-buffer
+// calls are serialised by ds->mu and synchronise before they return.
+int host_out(DeviceState* ds, size_t y_bytes) {
+  const size_t want = kHostOutHead + y_bytes;
+  if (want <= ds->cap_host_out) return FRC_OK;
+  int rc = ensure(&ds->host_out, &ds->cap_host_out, want, "cudaMalloc(result buffer)");
+  if (rc) return rc;
+  FRC_CUDA(cudaMemsetAsync(ds->host_out, 0, kHostOutHead, ds->stream), "cudaMemsetAsync(result status)");
+  return FRC_OK;
+}
+
 // Host-buffer matmul on device `dev` with weight bytes already at `w_dev`
-// (or, if w_host is non-null, uploaded into scratch first).
+// (or, if w_host is non-null, uploaded into scratch first).  The kernels
+// report bounded-wait timeouts into the result buffer's own status word,
+// which comes back in the same copy as y (FRC_ERR_DEVICE if raised).
 int host_matmul(DeviceState* ds, int quant, const uint8_t* w_dev, const uint8_t* w_host, size_t w_bytes, int64_t n,
                 int64_t k, const float* x, int64_t seq, float* y) {
   std::lock_guard<std::mutex> lock(ds->mu);
@@ -387,22 +410,22 @@ int host_matmul(DeviceState* ds, int quant, const uint8_t* w_dev, const uint8_t*
   }
   int rc = ensure(&ds->scratch_x, &ds->cap_x, sizeof(float) * seq * (k ? k : 1), "cudaMalloc(x scratch)");
   if (rc) return rc;
-  rc = ensure(&ds->scratch_y, &ds->cap_y, sizeof(float) * seq * (n ? n : 1), "cudaMalloc(y scratch)");
-  if (rc) return rc;
   const size_t xb = sizeof(float) * seq * k, yb = sizeof(float) * seq * n;
-  // page-locked x and y are the DMA source and target themselves; the rest
-  // go through the library's pinned staging (one host copy each)
+  rc = host_out(ds, yb);
+  if (rc) return rc;
+  uint32_t* status_dev = reinterpret_cast<uint32_t*>(ds->host_out);
+  float* y_dev = reinterpret_cast<float*>(ds->host_out + kHostOutHead);
+  // page-locked x is the DMA source itself; pageable x goes through the
+  // library's pinned staging (one host copy), and so do y and its status
+  // word on the way back (one DMA, one host copy)
   const bool x_direct = xb == 0 || host_pinned(x, xb);
-  const bool y_direct = yb == 0 || host_pinned(y, yb);
-  const size_t x_stage_bytes = x_direct ? 0 : (xb + 255) / 256 * 256, y_stage_bytes = y_direct ? 0 : yb;
-  const bool staged = x_stage_bytes + y_stage_bytes > 0 && x_stage_bytes + y_stage_bytes <= kPinnedStageMax;
+  const size_t x_stage_bytes = x_direct ? 0 : (xb + 255) / 256 * 256;
+  const bool staged = x_stage_bytes + kHostOutHead + yb <= kPinnedStageMax;
   uint8_t* stage = nullptr;
   if (staged) {
-    rc = pinned_stage(ds, x_stage_bytes + y_stage_bytes, &stage);
+    rc = pinned_stage(ds, x_stage_bytes + kHostOutHead + yb, &stage);
     if (rc) return rc;
   }
-  const bool y_staged = staged && !y_direct;
-  float* y_dst = y_staged ? reinterpret_cast<float*>(stage + x_stage_bytes) : y;
   if (xb) {
     const void* src = x;
     if (staged && !x_direct) {
@@ -411,12 +434,26 @@ int host_matmul(DeviceState* ds, int quant, const uint8_t* w_dev, const uint8_t*
     }
     FRC_CUDA(cudaMemcpyAsync(ds->scratch_x, src, xb, cudaMemcpyHostToDevice, ds->stream), "x upload");
   }
-  rc = gemv_device(ds, quant, w_dev, n, k, ds->scratch_x, seq, ds->scratch_y, ds->stream);
+  rc = gemv_device(ds, quant, w_dev, n, k, ds->scratch_x, seq, y_dev, ds->stream, status_dev);
   if (rc) return rc;
-  if (yb) FRC_CUDA(cudaMemcpyAsync(y_dst, ds->scratch_y, yb, cudaMemcpyDeviceToHost, ds->stream), "y download");
-  rc = finish_host_call(ds);
-  if (rc == FRC_OK && y_staged) std::memcpy(y, y_dst, yb);
-  return rc;
+  uint8_t* out_stage = staged ? stage + x_stage_bytes : nullptr;
+  if (staged) {
+    FRC_CUDA(cudaMemcpyAsync(out_stage, ds->host_out, kHostOutHead + yb, cudaMemcpyDeviceToHost, ds->stream),
+             "y download");
+  } else {
+    if (yb) FRC_CUDA(cudaMemcpyAsync(y, y_dev, yb, cudaMemcpyDeviceToHost, ds->stream), "y download");
+    FRC_CUDA(cudaMemcpyAsync(ds->status_host, status_dev, sizeof(uint32_t), cudaMemcpyDeviceToHost, ds->stream),
+             "status readback");
+  }
+  FRC_CUDA(cudaStreamSynchronize(ds->stream), "cudaStreamSynchronize");
+  const uint32_t f = staged ? *reinterpret_cast<const uint32_t*>(out_stage) : *ds->status_host;
+  if (f != 0) {
+    cudaMemsetAsync(status_dev, 0, sizeof(uint32_t), ds->stream);
+    cudaStreamSynchronize(ds->stream);
+    return fail(FRC_ERR_DEVICE, "kernel reported status 0x%x (a bounded wait ran out)", f);
+  }
+  if (staged && yb) std::memcpy(y, out_stage + kHostOutHead, yb);
+  return FRC_OK;
 }
 
 int host_dequant(DeviceState* ds, int quant, const uint8_t* w_dev, const uint8_t* w_host, size_t w_bytes,
