@@ -649,10 +649,20 @@ inline int tc1_mt_for(int k) {
   return 2;
 }
 
-// CTAs of a batch-1 tensor-core launch of n rows (one per SM, at least one
-// row group each).
-inline int tc1_grid(int64_t n, int sms, int rg) {
-  int64_t g = (n + rg - 1) / rg;
+// CTAs of a batch-1 tensor-core launch of n rows: one per SM and one
+// two-tile row group (32 rows) each at least; but where that leaves more
+// than half the SMs idle, one 16-row MMA tile each (a row group of at most
+// 16 rows converts one tile, half the work): Llama-3-70B o and down
+// row-sharded over 8 GPUs, 1024 rows, run on 64 CTAs instead of 32.  A
+// row's arithmetic does not depend on its CTA or on its group's tiles.
+// Measured on B200 (Q4_K, us, 32-row / 16-row CTAs, bit-identical y):
+// 1024 x 8192 8.73 / 6.99, 2048 x 8192 9.08 / 7.46, 1024 x 28672 23.95 /
+// 18.63, 2048 x 28672 24.35 / 19.54, 512 x 3584 5.22 / 4.88; where 32-row
+// CTAs already cover more than half the SMs the extra CTAs cost a little
+// (3584 x 3584 7.45 / 7.64, 4096 x 28672 25.05 / 25.75).
+inline int tc1_grid(int64_t n, int sms) {
+  int64_t g = (n + 2 * kTc1Rows - 1) / (2 * kTc1Rows);
+  if (2 * g <= sms) g = (n + kTc1Rows - 1) / kTc1Rows;
   if (g > sms) g = sms;
   return g < 1 ? 1 : static_cast<int>(g);
 }
@@ -676,7 +686,7 @@ inline bool tc1_config(int ts, int k, int64_t n, int sms, bool long_rows, bool s
       if (sbs % d == 0) nw = d;
     if (!nw) nw = maxw;
   }
-  const int grid = tc1_grid(n, sms, kTc1Rows * mt);
+  const int grid = tc1_grid(n, sms);
   const int64_t rows_max = (n + grid - 1) / grid;
   if (rows_max > (1 << 20)) return false;
   c->rows_max = static_cast<int>(rows_max);
@@ -795,7 +805,7 @@ inline cudaError_t launch_tc1(GemvParams p, const GemvRequest& r, const Tc1Confi
         return cudaErrorInvalidValue;
     }
   }
-  const int grid = tc1_grid(p.n, r.sms, kTc1Rows * c.mt);
+  const int grid = tc1_grid(p.n, r.sms);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(threads);
