@@ -93,6 +93,10 @@ struct GemvParams {
   // a time) and the most rows one CTA owns
   int tc_part_chunks, tc_rows_max;
   int tc_rg;  // gemv_tc1: rows per row group (16 per MMA tile of a warp)
+  // gemv_tc1: CTAs per cluster.  1: each CTA owns a row range and every part
+  // of k; s > 1: the s CTAs of a cluster share a row range, CTA r computing
+  // part r of k, and cluster rank 0 adds the parts' row sums in order
+  int tc_split;
 };
 
 constexpr int kMaxMats = 4;

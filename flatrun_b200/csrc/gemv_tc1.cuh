@@ -185,6 +185,33 @@ FRC_DEVICE_INLINE void sts64(uint32_t a, uint32_t x, uint32_t y) {
   asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(a), "r"(x), "r"(y) : "memory");
 }
 
+// Thread-block clusters (split launches): every thread of the cluster
+// arrives (release) and waits (acquire); shared memory of cluster rank
+// `rank` at the address of a local shared variable.
+FRC_DEVICE_INLINE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+FRC_DEVICE_INLINE uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+FRC_DEVICE_INLINE uint32_t cluster_addr(uint32_t local, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(local), "r"(rank));
+  return a;
+}
+FRC_DEVICE_INLINE float ld_cluster_f32(uint32_t a) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+  return v;
+}
+FRC_DEVICE_INLINE uint32_t ld_cluster_u32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
+
 // fp16 constants, two per word
 constexpr uint32_t kH2Bias = 0x64006400u;      // 1024, 1024 (with a nibble or byte in the mantissa)
 constexpr uint32_t kH2Neg1024 = 0xE400E400u;   // -1024
@@ -563,9 +590,22 @@ __global__ void __launch_bounds__((MAXW + 1 + NB) * 32, 1) gemv_tc1(const __grid
   __syncthreads();
   volatile int* abort = abort_flag;
 
+  // split launches: the cluster's CTAs share one row range, CTA r taking
+  // part r of k (no builder warps); otherwise every part, in order
+  const int split = p.tc_split;
   int64_t c0, c1;
-  cta_rows(p.n, c0, c1);
-  const int ntiles = count_tiles(p, c0, c1, RG) * nch;
+  int pb = 0, pe = nparts;
+  if (split > 1) {
+    const int64_t ranges = gridDim.x / split, j = blockIdx.x / split;
+    c0 = j * p.n / ranges;
+    c1 = (j + 1) * p.n / ranges;
+    pb = static_cast<int>(cluster_rank());
+    pe = pb + 1;
+  } else {
+    cta_rows(p.n, c0, c1);
+  }
+  const int ch_lo = pb * pc, ch_hi = pe * pc < nch ? pe * pc : nch;
+  const int ntiles = count_tiles(p, c0, c1, RG) * (ch_hi - ch_lo);
 
   if (warp == nw) {
     // the producer warp: the weights are never written by another kernel, so
@@ -573,7 +613,7 @@ __global__ void __launch_bounds__((MAXW + 1 + NB) * 32, 1) gemv_tc1(const __grid
     // (programmatic dependent launch)
     griddep_launch_dependents();
     if (lane == 0) {
-      Tc1Cursor cur{c0, Tile{}, 0, 0, 0};
+      Tc1Cursor cur{c0, Tile{}, 0, ch_lo, pb};
       int issued = 0;
       for (; issued < ntiles; ++issued) {
         const int si = issued % nst;
@@ -589,6 +629,10 @@ __global__ void __launch_bounds__((MAXW + 1 + NB) * 32, 1) gemv_tc1(const __grid
         if (!wait_phase(&full[i % nst], static_cast<uint32_t>(i / nst) & 1u, &zero))
           atomicOr(p.status, kStatusDrainTimeout);
       }
+    }
+    if (split > 1) {  // every thread of the cluster takes part in both cluster barriers
+      cluster_sync();
+      cluster_sync();
     }
     return;
   }
@@ -677,12 +721,12 @@ __global__ void __launch_bounds__((MAXW + 1 + NB) * 32, 1) gemv_tc1(const __grid
   int s = 0;
   uint32_t ph = 0u;
   int par = 0;
-  for (int part = 0; part < nparts; ++part) {
+  for (int part = pb; part < pe; ++part) {
     const int ch0 = part * pc, ch1 = (part + 1) * pc < nch ? (part + 1) * pc : nch;
     const int sb0 = ch0 * kc;
     const int b = BUILDER ? (part & 1) : 0;  // this part's fragment buffer
     bool frags_ok = true;
-    if (!BUILDER || part == 0) {
+    if (!BUILDER || part == pb) {
       // x fragments of super-blocks [sb0, sb1), built by the compute warps
       // (without a builder the previous part's fragments are free: every
       // warp has passed the barrier that ended its last row group)
@@ -769,10 +813,11 @@ __global__ void __launch_bounds__((MAXW + 1 + NB) * 32, 1) gemv_tc1(const __grid
         }
         if (lane < rows) {
           // parts of k are added in order: ((part 0 + part 1) + part 2) ...
+          // (a split launch keeps its part's sums for cluster rank 0)
           float y = h;
           float* ya = yacc + (t0 - c0) + lane;
-          if (part > 0) y = *ya + y;
-          if (part + 1 < nparts) {
+          if (part > pb) y = *ya + y;
+          if (part + 1 < pe || split > 1) {
             *ya = y;
           } else if (!*abort) {
             put_y(p, g_world, p.mat_y[T.m] + T.local + lane, y);
@@ -785,6 +830,30 @@ __global__ void __launch_bounds__((MAXW + 1 + NB) * 32, 1) gemv_tc1(const __grid
     // every compute warp has passed the last row group's barrier: this
     // part's buffer is free for the builder's part + 2
     if (BUILDER && part + 2 < nparts && lane == 0) mbar_arrive(&frag_empty[b]);
+  }
+  if (split > 1) {
+    // every CTA's part sums are in its shared memory: rank 0 adds them in
+    // part order, as the one-CTA launch does, and writes y (none if a wait
+    // ran out in any CTA of the cluster); the second barrier keeps the
+    // others' shared memory until rank 0 has read it
+    cluster_sync();
+    if (pb == 0) {
+      bool bad = *abort != 0;
+      for (int r = 1; r < split; ++r)
+        bad = bad || ld_cluster_u32(cluster_addr(smem_u32(abort_flag), static_cast<uint32_t>(r))) != 0u;
+      if (!bad) {
+        for (int i = ct; i < static_cast<int>(c1 - c0); i += nct) {
+          float y = yacc[i];
+          const uint32_t la = smem_u32(yacc + i);
+          for (int r = 1; r < split; ++r) y = y + ld_cluster_f32(cluster_addr(la, static_cast<uint32_t>(r)));
+          const int64_t row = c0 + i;
+          int m = 0;
+          while (m + 1 < p.nmat && row >= p.mat_end[m]) ++m;
+          put_y(p, g_world, p.mat_y[m] + (row - (m ? p.mat_end[m - 1] : 0)), y);
+        }
+      }
+    }
+    cluster_sync();
   }
   if (g_world > 1) {  // publish this CTA's gathered rows
     named_barrier_sync(1, nct);

@@ -91,7 +91,7 @@ inline int opt(const std::atomic<int>& v) { return v.load(std::memory_order_rela
 struct Tuning {
   int upt = -1, rps = -1, tile_bytes = -1, nwarps = -1, nstage = -1, smem_bytes = -1, rt = -1, stage_bytes = -1,
       ctas_per_sm = -1, mma_grid = -1, mma_mt = -1, pre_stages = -1, pdl = -1, tc_mt = -1, tc_builders = -1,
-      tc_stages = -1, tc_part_chunks = -1;
+      tc_stages = -1, tc_part_chunks = -1, tc_split = -1;
 };
 inline const Tuning& tuning() {
   static const Tuning t = [] {
@@ -119,6 +119,7 @@ inline const Tuning& tuning() {
     v.tc_builders = get("FRC_TC_BUILDERS");
     v.tc_stages = get("FRC_TC_STAGES");
     v.tc_part_chunks = get("FRC_TC_PC");
+    v.tc_split = get("FRC_TC_SPLIT");
     return v;
   }();
   return t;
@@ -154,6 +155,29 @@ inline cudaError_t kernel_occupancy(const void* kernel, int device, int threads,
   if (nb < 1) return cudaErrorInvalidConfiguration;
   cache[key] = nb;
   *blocks = nb;
+  return cudaSuccess;
+}
+
+// Clusters of `cfg`'s shape (cluster size, block size, shared memory) the
+// device holds at once, looked up once per kernel, device and shape.
+inline cudaError_t max_active_clusters(const void* kernel, int device, const cudaLaunchConfig_t& cfg, int* clusters) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, unsigned, unsigned, size_t>, int> cache;
+  unsigned csize = 1;
+  for (unsigned i = 0; i < cfg.numAttrs; ++i)
+    if (cfg.attrs[i].id == cudaLaunchAttributeClusterDimension) csize = cfg.attrs[i].val.clusterDim.x;
+  const auto key = std::make_tuple(kernel, device, csize, cfg.blockDim.x, cfg.dynamicSmemBytes);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *clusters = it->second;
+    return cudaSuccess;
+  }
+  int n = 0;
+  const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+  if (e != cudaSuccess) return e;
+  cache[key] = n;
+  *clusters = n;
   return cudaSuccess;
 }
 
@@ -634,8 +658,11 @@ inline cudaError_t launch_gather_wait(const uint32_t* flags, int world, const ui
 struct Tc1Config {
   int nw = 0, mt = 1, nch = 0, stride = 0, stage_bytes = 0, nst = 0, part_chunks = 0, rows_max = 0;
   int builders = 0;  // rows in several parts of k: builder warps, two fragment buffers
+  int split = 1;     // rows in several parts of k: CTAs per cluster, one part each
+  int ranges = 0;    // split: row ranges (clusters) wanted
   size_t smem = 0;
 };
+constexpr int kTc1MaxSplit = 8;  // portable cluster size
 
 // MMA tiles per warp of a batch-1 tensor-core launch (a row group is 16 rows
 // per tile).  Two, measured on B200 against one (twice the warps, 16-row
@@ -665,6 +692,17 @@ inline int tc1_grid(int64_t n, int sms) {
   if (2 * g <= sms) g = (n + kTc1Rows - 1) / kTc1Rows;
   if (g > sms) g = sms;
   return g < 1 ? 1 : static_cast<int>(g);
+}
+
+// Row ranges (clusters of s CTAs, one per s SMs) of a split launch of n
+// rows, sized as tc1_grid sizes CTAs; and the most rows one range may hold,
+// allowing for as few as half of those clusters resident at once (the launch
+// runs no more ranges than the device holds clusters).
+inline int tc1_split_ranges(int64_t n, int sms, int s) { return tc1_grid(n, sms / s > 0 ? sms / s : 1); }
+inline int tc1_split_rows(int64_t n, int sms, int s) {
+  const int t = tc1_split_ranges(n, sms, s);
+  const int lo = t / 2 > 0 ? t / 2 : 1;
+  return static_cast<int>((n + lo - 1) / lo);
 }
 
 // swiglu: x is read as silu(x) * x_mul (the down projection's SwiGLU),
@@ -718,10 +756,32 @@ inline bool tc1_config(int ts, int k, int64_t n, int sms, bool long_rows, bool s
   // 41.6 at 3 stages x 4 parts, 41.7 at 4 x 5, 45.7 at 2 x 7 (one builder
   // warp 44.2, none 47.2 on the CUDA-core kernel); Qwen2-7B k = 18944 17.1 at
   // 3 x 3, 18.1 at 4 x 4, 18.9 at 2 x 2 without builders.
-  int pc = 0, builders = 0;
+  int pc = 0, builders = 0, split = 1;
   if (tc1_layout(want, c->nch * nw, c->rows_max, c->stage_bytes).total <= budget) {
     pc = c->nch;
-  } else {
+  } else if (tuned(tuning().tc_split, 1) && sms >= 2) {
+    // a cluster of s CTAs per row range, CTA r building and streaming part r
+    // of k only: the fewest parts whose fragments leave room for `want`
+    // stages (else fewer), balanced in chunks.  Each part's row sums are
+    // formed as in a one-CTA launch and cluster rank 0 adds them in part
+    // order, so y does not depend on n or on the grid.  Measured on B200
+    // (Q4_K, us, one CTA per range with builder warps / clusters of two):
+    // 8192 x 28672 42.9 / 39.5, 2048 x 28672 24.5 / 15.7, 1024 x 28672
+    // 24.0 / 12.7; where the row ranges are as many either way a little
+    // slower (4096 x 28672 25.1 / 25.6, 3584 x 18944 18.1 / 18.3).
+    for (int w = want; w >= 2 && split == 1; --w) {
+      for (int s = 2; s <= kTc1MaxSplit && s <= sms; ++s) {
+        const int q = (c->nch + s - 1) / s;
+        if ((c->nch + q - 1) / q != s) continue;  // s parts of q chunks would leave one empty
+        if (tc1_layout(w, q * nw, tc1_split_rows(n, sms, s), c->stage_bytes).total <= budget) {
+          pc = q;
+          split = s;
+          break;
+        }
+      }
+    }
+  }
+  if (!pc) {
     builders = mt == 2 && nw <= 8 && !swiglu ? tuned(tuning().tc_builders, 2) : 0;
     if (builders > 2) builders = 2;
     const int nbuf = builders ? 2 : 1;
@@ -740,13 +800,17 @@ inline bool tc1_config(int ts, int k, int64_t n, int sms, bool long_rows, bool s
     }
   }
   if (!pc) return false;
-  // rows longer than one part of k: with builder warps the parts' fragments
-  // are built behind the compute; without them they are rebuilt while the
-  // ring drains, which measured on B200 behind the CUDA-core kernel at three
-  // parts (Llama-3-70B down, k = 28672: 50.8 against 47.1 us), so rows of
-  // more than two parts without builders stay on it unless long_rows
-  // (FRC_OPT_BATCH1_TC = 2)
-  if (!builders && (c->nch + pc - 1) / pc > 2 && !long_rows) return false;
+  if (split > 1) {
+    c->rows_max = tc1_split_rows(n, sms, split);
+    c->ranges = tc1_split_ranges(n, sms, split);
+  }
+  // rows longer than one part of k in one CTA: with builder warps the parts'
+  // fragments are built behind the compute; without them they are rebuilt
+  // while the ring drains, which measured on B200 behind the CUDA-core
+  // kernel at three parts (Llama-3-70B down, k = 28672: 50.8 against 47.1
+  // us), so rows of more than two parts without builders stay on it unless
+  // long_rows (FRC_OPT_BATCH1_TC = 2)
+  if (split == 1 && !builders && (c->nch + pc - 1) / pc > 2 && !long_rows) return false;
   const int nbuf = builders ? 2 : 1;
   const int forced_nst = tuning().nstage;
   int nst = forced_nst > 0 ? forced_nst : 8;
@@ -755,6 +819,7 @@ inline bool tc1_config(int ts, int k, int64_t n, int sms, bool long_rows, bool s
   if (nst < 2) return false;
   c->part_chunks = pc;
   c->builders = builders;
+  c->split = split;
   c->nst = nst;
   c->smem = static_cast<size_t>(tc1_layout(nst, pc * nw, c->rows_max, c->stage_bytes, nbuf).total);
   return true;
@@ -771,6 +836,8 @@ inline cudaError_t launch_tc1(GemvParams p, const GemvRequest& r, const Tc1Confi
   p.tc_rg = kTc1Rows * c.mt;
   p.stage_stride = c.stage_bytes;
   p.nstage = c.nst;
+  p.tc_split = c.split;
+  if (c.split > 1 && (c.builders || c.mt != 2 || c.nw > 8)) return cudaErrorInvalidValue;  // not a split form
   const int threads = (c.nw + 1 + c.builders) * 32;
   // two MMA tiles per warp: up to 8 compute warps (+ builder warps for rows
   // in parts of k); one: up to 15 compute warps run the 16-warp
@@ -805,17 +872,32 @@ inline cudaError_t launch_tc1(GemvParams p, const GemvRequest& r, const Tc1Confi
         return cudaErrorInvalidValue;
     }
   }
-  const int grid = tc1_grid(p.n, r.sms);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.gridDim = dim3(static_cast<unsigned>(tc1_grid(p.n, r.sms)));
   cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = c.smem;
   cfg.stream = r.stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = tuned(tuning().pdl, 1) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (c.split > 1) {
+    // clusters of c.split CTAs along x, as many row ranges as the device
+    // holds clusters at once (at least the half tc1_config sized rows for)
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = static_cast<unsigned>(c.split);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+    cfg.gridDim = dim3(static_cast<unsigned>(c.split * c.ranges));
+    int clusters = 0;
+    e = max_active_clusters(reinterpret_cast<const void*>(kernel), r.device, cfg, &clusters);
+    if (e != cudaSuccess) return e;
+    const int ranges = c.ranges < clusters ? c.ranges : clusters;
+    if (ranges < 1 || (p.n + ranges - 1) / ranges > c.rows_max) return cudaErrorInvalidConfiguration;
+    cfg.gridDim = dim3(static_cast<unsigned>(c.split * ranges));
+  }
   return cudaLaunchKernelEx(&cfg, kernel, maps, p);
 }
 

@@ -361,6 +361,25 @@ def test_batch1_tensor_core(cuda_backend, fmt, n, k):
     cuda_backend.close()
 
 
+@pytest.mark.parametrize("fmt,k", [("Q4_K", 28672), ("Q5_K", 18944)])
+def test_batch1_tensor_core_rows_independent_of_n(cuda_backend, fmt, k):
+    """Rows in parts of k run on clusters of CTAs, one part each, the parts'
+    row sums added in order by cluster rank 0: a row's bits do not depend on
+    the matrix's row count, its grid or its row ranges (the first m rows as a
+    matrix of their own give the same y), and the fp64 bound holds."""
+    n = 600
+    raw = synth.make_weight(fmt, n, k, seed=11 + k)
+    x = synth.make_x(k, seed=12)
+    y_full = cuda_backend.weight(raw, n, k, fmt).matmul(x)
+    rb = synth.row_bytes(fmt, k)
+    for m in (1, 17, 100, 333):
+        sub = np.ascontiguousarray(raw[: m * rb])
+        assert np.array_equal(cuda_backend.weight(sub, m, k, fmt).matmul(x), y_full[:m]), (fmt, k, m)
+    ref = O.matvec_fp64(fmt, raw, x, n, k)
+    assert O.norm_err(y_full, ref, O.term_scale(fmt, raw, x, n, k)) < 5e-6
+    cuda_backend.close()
+
+
 @pytest.mark.parametrize("fmt", ["Q4_K", "Q5_K"])
 def test_batch1_tensor_core_wide_range(cuda_backend, fmt):
     """Activations spanning 60 decades, runs of exact zeros and sign changes:
