@@ -79,7 +79,9 @@ int frc_block_geometry(int quant, int* elems_per_block, int* bytes_per_block);
 /* Bytes of an (n, k) weight: n * (k / QK) * TS.  FRC_ERR_INVALID if k % QK != 0. */
 int frc_weight_nbytes(int quant, int64_t n, int64_t k, size_t* nbytes);
 /* Reads and clears the device status word of `device` (set by kernels whose
- * bounded waits ran out); *flags == 0 means no fault was recorded. */
+ * bounded waits ran out, launched through the device-pointer entry points;
+ * the host-buffer calls return FRC_ERR_DEVICE from their own status word
+ * instead); *flags == 0 means no fault was recorded. */
 int frc_device_status(int device, uint32_t* flags);
 
 /* Library options (no reference counterpart).  Process-wide, read by every
@@ -280,7 +282,9 @@ int frc_weight_info(const frc_weight* w, const void** dev_ptr, size_t* nbytes,
                     int* quant, int64_t* n, int64_t* k, int* device);
 /* y_host (seq, n) = x_host (seq, k) . W^T with host buffers: copies x in,
  * runs frc_gemv (seq <= 16) or the batched prefill path (seq > 16), copies y
- * out and synchronises.  seq >= 1.  (Reference: matmul_*[_batched].) */
+ * out and synchronises.  seq >= 1.  Page-locked x is copied from directly;
+ * the call's status word comes back with y, and a bounded wait that ran out
+ * makes the call return FRC_ERR_DEVICE.  (Reference: matmul_*[_batched].) */
 int frc_weight_matmul(frc_weight* w, const float* x_host, int64_t seq, float* y_host);
 /* Device-pointer variant on a caller stream; no synchronisation. */
 int frc_weight_matmul_dev(frc_weight* w, const float* x_dev, int64_t seq, float* y_dev,
