@@ -48,6 +48,7 @@ SIGNATURES: dict[str, list] = {
     "frc_set_option": [_i, _i],
     "frc_get_option": [_i, ctypes.POINTER(_i)],
     "frc_batch1_kernel": [_i, ctypes.c_int64, ctypes.POINTER(_i)],
+    "frc_batch1_plan": [_i, _i64, _i64, _i, ctypes.POINTER(_i64)],
     "frc_noalloc_status": [_i, ctypes.POINTER(ctypes.c_uint32)],
     "frc_gemv_ex": [_i, _i, ctypes.POINTER(_p), ctypes.POINTER(_sz), ctypes.POINTER(_i64), _i64, _p, _p, _p,
                     ctypes.c_float, _i, ctypes.POINTER(_p), _p],
@@ -178,6 +179,21 @@ def batch1_kernel(quant: str, k: int) -> str:
     v = ctypes.c_int(-1)
     check(lib.frc_batch1_kernel(QUANT_IDS[quant], int(k), ctypes.byref(v)), lib)
     return BATCH1_KERNELS[int(v.value)]
+
+
+PLAN_FIELDS = ("kernel", "warps", "chunks", "part_chunks", "split", "ranges", "ctas", "builders", "stages",
+               "rows_max", "smem", "tiles_per_warp")
+
+
+def batch1_plan(quant: str, n: int, k: int, sms: int = 148) -> dict:
+    """The batch-1 launch plan of an (n, k) matrix on a device of `sms` SMs
+    (frc_batch1_plan; host-side, no GPU needed)."""
+    lib = load()
+    arr = (ctypes.c_int64 * len(PLAN_FIELDS))()
+    check(lib.frc_batch1_plan(QUANT_IDS[quant], int(n), int(k), int(sms), arr), lib)
+    plan = dict(zip(PLAN_FIELDS, (int(v) for v in arr)))
+    plan["kernel"] = BATCH1_KERNELS[plan["kernel"]]
+    return plan
 
 
 class option:

@@ -679,6 +679,37 @@ int frc_batch1_kernel(int quant, int64_t k, int* kind) {
   return FRC_OK;
 }
 
+int frc_batch1_plan(int quant, int64_t n, int64_t k, int sms, int64_t* plan) {
+  if (!plan) return fail(FRC_ERR_INVALID, "null pointer");
+  for (int i = 0; i < FRC_B1_PLAN_LEN; ++i) plan[i] = 0;
+  int kind = 0;
+  int rc = frc_batch1_kernel(quant, k, &kind);
+  if (rc) return rc;
+  plan[0] = kind;
+  if (n < 1 || n > (int64_t(1) << 40) || sms < 1 || sms > 4096)
+    return fail(FRC_ERR_INVALID, "frc_batch1_plan: n must be >= 1 and sms 1..4096");
+  if (plan[0] != FRC_B1_TENSOR_FP32) return FRC_OK;
+  int qk, ts;
+  geometry(quant, &qk, &ts);
+  frc::Tc1Config c;
+  if (!frc::tc1_config(ts, static_cast<int>(k), n, sms, frc::opt(frc::options().batch1_tc) == 2, false, &c)) {
+    plan[0] = FRC_B1_CUDA_CORE_FP32;  // this n does not fit the tensor-core kernel
+    return FRC_OK;
+  }
+  plan[1] = c.nw;
+  plan[2] = c.nch;
+  plan[3] = c.part_chunks;
+  plan[4] = c.split;
+  plan[5] = c.split > 1 ? c.ranges : 0;
+  plan[6] = c.split > 1 ? static_cast<int64_t>(c.split) * c.ranges : frc::tc1_grid(n, sms);
+  plan[7] = c.builders;
+  plan[8] = c.nst;
+  plan[9] = c.rows_max;
+  plan[10] = static_cast<int64_t>(c.smem);
+  plan[11] = c.mt;
+  return FRC_OK;
+}
+
 int frc_gemv(int quant, const void* w_dev, size_t w_bytes, int64_t n, int64_t k, const float* x_dev, int64_t batch,
              float* y_dev, void* stream) {
   int rc = check_matmul(quant, w_bytes, n, k, batch);

@@ -122,6 +122,18 @@ int frc_get_option(int option, int* value);
 #define FRC_B1_TENSOR_FP32    1
 #define FRC_B1_INT16          2
 int frc_batch1_kernel(int quant, int64_t k, int* kind);
+/* The batch-1 launch plan of an (n, k) matrix on a device of `sms` SMs under
+ * the current options, computed on the host without launching anything (no
+ * reference counterpart; for diagnostics and for tests that need no GPU).
+ * plan[FRC_B1_PLAN_LEN]: [0] the kernel (FRC_B1_*); for FRC_B1_TENSOR_FP32
+ * also [1] compute warps (super-blocks per chunk), [2] chunks per row,
+ * [3] chunks per part of k, [4] CTAs per cluster (1: one CTA per row range,
+ * every part; s > 1: one part per CTA), [5] row ranges (clusters) wanted
+ * when split, [6] CTAs, [7] builder warps, [8] shared-memory stages,
+ * [9] most rows one CTA or cluster holds, [10] dynamic shared memory bytes,
+ * [11] 16-row MMA tiles per warp. */
+#define FRC_B1_PLAN_LEN 12
+int frc_batch1_plan(int quant, int64_t n, int64_t k, int sms, int64_t* plan);
 
 /* ---- stream-ordered device-pointer kernels ------------------------------ *
  * No synchronisation: the work is enqueued on `stream` (a cudaStream_t;
