@@ -24,11 +24,12 @@ e2e    = the same metric through the public call a user makes,
          CudaBackend.matmul_q4k(x, weight, n, k) with x in pinned host memory:
          x host->device, kernel, y device->host and a synchronise per call
          (N > 1: each rank its own shard, the slowest rank's time).
-kernels: batch-1 Q4_K on gemv_tc1 (x in fp32 as three exact fp16 terms,
-         weights as exact fp16 q*sc, products on the tensor cores, fp32
-         accumulation) where the row's activation fragments fit in shared
-         memory, else (and for the other formats) the fp32 CUDA-core gemv_b1;
-         --cuda-core forces the latter for Q4_K too.
+kernels: batch-1 Q4_K and Q5_K on gemv_tc1 (x in fp32 as three exact fp16
+         terms, weights as exact fp16 q*sc, products on the tensor cores,
+         fp32 accumulation); rows whose activation fragments do not fit in
+         shared memory (the k = 28672 down) run in parts of k on clusters of
+         CTAs, one part each; the other formats on the fp32 CUDA-core
+         gemv_b1; --cuda-core forces the latter for Q4_K too.
 roofline: achieved GB/s of the dominant launch (the one carrying the most
          bytes: gate+up for the layer workloads) from K back-to-back launches
          timed with CUDA events, against the measured copy bandwidth in

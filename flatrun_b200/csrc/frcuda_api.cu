@@ -142,7 +142,9 @@ struct DeviceState {
   size_t cap_host_out = 0;
   // activation records of the batched tensor-core kernel: grown on demand and
   // never freed while the process runs, so work already queued (or captured
-  // in a graph) keeps a valid pointer after a larger call replaces it
+  // in a graph) keeps a valid pointer after a larger call replaces it; the
+  // capacity at least doubles at each growth, so the retired buffers
+  // together are smaller than the current one
   std::mutex rec_mu;
   uint8_t* scratch_rec = nullptr;
   size_t cap_rec = 0;

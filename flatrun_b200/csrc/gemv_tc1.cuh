@@ -232,11 +232,15 @@ FRC_DEVICE_INLINE void split3(float a, float b, uint32_t& t0, uint32_t& t1, uint
 }
 
 // Power-of-two scale s with |m s| < 2^15 for the largest magnitude m of a
-// super-block (exponent clamped so s and 1 / s stay normal), and 1 / s.
+// super-block, and 1 / s.  The exponent is at least -113, its value for the
+// largest finite fp32 m (so |m s| < 2^15 holds for every finite m and the
+// fp16 terms never overflow), and at most 100: for m below 2^-86 the scale
+// stays 2^100, so that d / s of a normal fp16 d stays a normal fp32 number
+// (the terms then start below 2^14).
 FRC_DEVICE_INLINE void tc1_scale(float m, float& s, float& inv) {
   int e = static_cast<int>((__float_as_uint(m) >> 23) & 0xFFu) - 127;  // floor(log2 m) for normal m
   int se = 14 - e;
-  se = se < -100 ? -100 : (se > 100 ? 100 : se);
+  se = se < -113 ? -113 : (se > 100 ? 100 : se);
   s = __uint_as_float(static_cast<uint32_t>(127 + se) << 23);
   inv = __uint_as_float(static_cast<uint32_t>(127 - se) << 23);
 }

@@ -396,6 +396,22 @@ def test_batch1_tensor_core_wide_range(cuda_backend, fmt):
     cuda_backend.close()
 
 
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q5_K"])
+def test_batch1_tensor_core_huge_activations(cuda_backend, fmt):
+    """A super-block whose largest |x| lies in [2^116, 2^117) (1.2e35): its
+    power-of-two scale still brings it below 2^15, so no fp16 term overflows
+    and y stays within the fp32 bound of fp64."""
+    n, k = 64, 1024
+    raw = synth.make_weight(fmt, n, k, seed=9)
+    x = synth.make_x(k, seed=10)
+    x[256:512] *= np.float32(1.2e35 / np.abs(x[256:512]).max())
+    y = cuda_backend.weight(raw, n, k, fmt).matmul(x)
+    assert np.isfinite(y).all()
+    ref = O.matvec_fp64(fmt, raw, x, n, k)
+    assert O.norm_err(y, ref, O.term_scale(fmt, raw, x, n, k)) < 5e-6
+    cuda_backend.close()
+
+
 def test_batch1_tensor_core_q4k_repeatable(cuda_backend):
     """The kernel's sums run in a fixed order: repeated launches agree bit
     for bit."""
