@@ -99,13 +99,16 @@ int frc_device_status(int device, uint32_t* flags);
  *                         the shape; n > 0: n splits (clamped to 1..16).
  *  FRC_OPT_INJECT_OOM     1: frc_weight_create fails with FRC_ERR_NOMEM before
  *                         any CUDA call (a test of the error path); default 0.
- *  FRC_OPT_BATCH1_TC      1 (default): batch-1 Q4_K with x in fp32 runs on the
- *                         tensor cores (weights as exact fp16 integers q * sc,
- *                         x as an exact sum of three fp16 terms, fp32
- *                         accumulation) where the whole row's activation
- *                         fragments fit in shared memory (k <= 16384 at 16
- *                         warps); 2: longer rows too, in parts of k; 0: on
- *                         the CUDA-core fp32 kernel. */
+ *  FRC_OPT_BATCH1_TC      1 (default): batch-1 Q4_K and Q5_K with x in fp32
+ *                         run on the tensor cores (weights as exact fp16
+ *                         integers q * sc, x as an exact sum of three fp16
+ *                         terms, fp32 accumulation); rows whose activation
+ *                         fragments do not fit one CTA's shared memory run
+ *                         in parts of k on thread-block clusters, one part
+ *                         per CTA (up to 8 parts); 2: also rows of more
+ *                         than two parts on one CTA without builder warps
+ *                         (reached only without clusters); 0: on the
+ *                         CUDA-core fp32 kernel. */
 #define FRC_OPT_BATCH1_INT16   1
 #define FRC_OPT_BATCHED_FP32   2
 #define FRC_OPT_PREFILL_TC     3
