@@ -329,9 +329,9 @@ def test_batch1_activation_outliers(cuda_backend, fmt, int16):
 # Q4_K batch-1 shapes for the tensor-core kernel: one super-block, odd (9)
 # and even super-block counts per chunk, two chunks (5120: 10 warps; 8192:
 # 16), ragged row groups (1, 15, 17, 33, 37 rows), and rows longer than one
-# part of k (18944: 74 super-blocks, chunks of 16 with a ragged last one, in
-# two parts; 36864: three parts), which batch1_tc = 2 runs on the tensor
-# cores and the default leaves on the CUDA-core kernel
+# part of k (18944: 74 super-blocks, 10 chunks of 8 with a ragged last one,
+# in two parts; 36864: two or three parts), which run on clusters of CTAs,
+# one part each, under both batch1_tc = 1 and 2
 # (15, 512), (33, 4096), (33, 18944) (rows in parts of k) and (5328, 4096)
 # (148 CTAs of 36 rows: 32 + 4) end a CTA with a row group of at most 16
 # rows, which converts one MMA tile only
